@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""bench.py — the decoder MoE hot path on B200, one JSON line on stdout.
+
+Default workload: the 24-layer decode-shape MoE stack in
+bf16 — hidden 2048, 64 routed experts (top-6, renormalised) + shared width
+2048, expert ffn 1024 — at a token batch of 1. One step = one pass of the
+stack (h <- h + MoE_l(h), l = 0..23) over the batch; metric = tokens/s.
+Synthetic seeded inputs (the counter-based generator, seed 1), random-init
+weights of that architecture; weights (20 GB) exceed L2, so no flush is
+needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch T] [--format bf16|int8]
+  python bench.py --impl reference ...   # the reference's own fp32 CPU MoE, same metric
+
+N > 1 (torchrun, one rank per GPU): decode does not shard — every rank runs
+an independent replica ("replicas only"), value = all ranks' tokens / max
+rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "grpc-unlimited-ocr_b200"))
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def decode_bytes(cfg, active_counts, fmt_int8: bool):
+    """Algorithmic bytes of one stack pass and of the gate/up launches, from the
+    distinct experts each layer's produced ids touched (U_l)."""
+    H, F, S, E = cfg.hidden, cfg.ffn, cfg.shared_ffn, cfg.experts
+    eb = 1 if fmt_int8 else 2
+    sc = 4 if fmt_int8 else 0  # per-row fp32 scales
+    expert_gu = 2 * (F * H * eb + F * sc)
+    expert_dn = H * F * eb + H * sc
+    shared_gu = 2 * (S * H * eb + S * sc)
+    shared_dn = H * S * eb + H * sc
+    router = E * H * 4
+    total = sum(u * (expert_gu + expert_dn) + shared_gu + shared_dn + router for u in active_counts)
+    gate_up = [u * expert_gu + shared_gu for u in active_counts]
+    return total, gate_up
+
+
+def traffic_from_profile(name):
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for ln in open(path):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_reference_layer_time(cfg, host_layer, T, budget_s, threads):
+    """The reference's own MixtureOfExperts::forward (oracle/_ref) when built,
+    else the C restatement; returns (seconds per layer call, kind, cores, reps)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    x = O.synth(cfg.seed, 0, O.KIND_X, 0, T * cfg.hidden, 1.0)
+    x = (O.round_bf16(x) if cfg.bf16_values else x).reshape(T, cfg.hidden)
+    if O.ref_available():
+        O.set_ref_threads(threads)
+        ref = O.RefMoe(host_layer, cfg.top_k)
+        run, kind = (lambda: ref(x)), "reference"
+    else:
+        run, kind = (lambda: O.moe_forward(host_layer, x, cfg.top_k, True, threads=threads)), "port"
+    run()  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), kind, threads, len(times)
+
+
+def host_layer_weights(cfg, layer=0):
+    """Layer weights generated on the host (no GPU), as the CPU arms need them."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    H, E, F, S = cfg.hidden, cfg.experts, cfg.ffn, cfg.shared_ffn
+
+    def g(kind, idx, n):
+        v = O.synth(cfg.seed, layer, kind, idx, n, 0.02)
+        return O.round_bf16(v) if cfg.bf16_values else v
+    w = O.MoeWeights(
+        router=g(O.KIND_ROUTER, 0, E * H).reshape(E, H),
+        gate=np.concatenate([g(O.KIND_GATE, e, F * H) for e in range(E)]).reshape(E * F, H),
+        up=np.concatenate([g(O.KIND_UP, e, F * H) for e in range(E)]).reshape(E * F, H),
+        down=np.concatenate([g(O.KIND_DOWN, e, H * F) for e in range(E)]).reshape(E * H, F),
+        shared_gate=g(O.KIND_SGATE, 0, S * H).reshape(S, H), shared_up=g(O.KIND_SUP, 0, S * H).reshape(S, H),
+        shared_down=g(O.KIND_SDOWN, 0, H * S).reshape(H, S))
+    if cfg.weight_format == 1:  # int8: the CPU runs the dequantised per-channel weights
+        deq = lambda a: O.dequantize_q8(*O.quantize_q8(a))  # noqa: E731
+        w = O.MoeWeights(w.router, deq(w.gate), deq(w.up), deq(w.down), deq(w.shared_gate), deq(w.shared_up),
+                         deq(w.shared_down))
+    return w
+
+
+def run_reference_arm(args, cfg, world, rank):
+    """--impl reference: the reference's CPU MoE on the host cores, same metric."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    w = host_layer_weights(cfg)
+    per_step = []
+    kind = None
+    for i in range(args.warmup + args.steps):
+        t, kind, cores, reps = cpu_reference_layer_time(cfg, w, args.batch, budget_s=2.0, threads=threads)
+        if i >= args.warmup:
+            per_step.append(t)
+    layer_s = statistics.median(per_step)
+    step_s = layer_s * cfg.layers
+    value = args.batch / step_s
+    line = {
+        "impl": "reference", "metric": "MoE layer tokens/s (decode)", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.layers}-layer MoE stack, batch {args.batch}",
+                   "global_batch": args.batch * world, "layers": cfg.layers, "hidden": cfg.hidden,
+                   "experts": cfg.experts, "top_k": cfg.top_k, "ffn": cfg.ffn, "shared_ffn": cfg.shared_ffn,
+                   "parallelism": "replicas" if world > 1 else "single"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"layer 0 of {cfg.layers}, batch {args.batch}, median of ~2 s of calls per step, "
+                                   f"scaled to the {cfg.layers}-layer stack"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    if kind == "reference":
+        line["note"] = ("reference MixtureOfExperts::forward has no renormalisation; its arithmetic is the same "
+                        "as the renormalised config's")
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--format", default="bf16", choices=["bf16", "int8"])
+    ap.add_argument("--layers", type=int, default=None, help="override the stack depth (default 24)")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import moe_configs as C
+    cfg = C.CONFIGS[2 if args.format == "int8" else 1]
+    if args.layers:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, layers=args.layers)
+    world, rank, local = dist_setup()
+
+    if args.impl == "reference":
+        if world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("gloo")
+        run_reference_arm(args, cfg, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    import torch
+    import uocr_moe as M
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    T = args.batch
+    fmt_int8 = args.format == "int8"
+    plan = M.Plan(cfg.dims(), max_rows=max(T, 1), weight_format=M.WEIGHT_INT8 if fmt_int8 else M.WEIGHT_BF16,
+                  renormalize=True, device=local)
+    host_layer0 = None
+    for layer in range(cfg.layers):
+        t = C.device_layer(cfg, layer, device=dev)
+        C.load_layer(plan, cfg, layer, t)
+        del t
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    x = C.device_input(cfg, T, device=dev)
+    h = torch.empty_like(x)
+
+    def step():
+        h.copy_(x)
+        plan.forward_stack(h, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        plan.check(stream=stream)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clk = clocks.stop()
+        ms = start.elapsed_time(end) / args.steps
+        plan.check(stream=stream)
+
+        # End to end through the public call with host buffers: pinned x in,
+        # h out, both copies inside the timed region.
+        x_host = x.cpu().pin_memory()
+        h_host = torch.empty_like(x_host).pin_memory()
+        for _ in range(3):
+            h.copy_(x_host, non_blocking=True)
+            plan.forward_stack(h, stream=stream)
+            h_host.copy_(h, non_blocking=True)
+        torch.cuda.synchronize()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(args.steps):
+            h.copy_(x_host, non_blocking=True)
+            plan.forward_stack(h, stream=stream)
+            h_host.copy_(h, non_blocking=True)
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e_start.elapsed_time(e_end) / args.steps
+
+        # Per-kernel device times (same workload, events between the kernels).
+        h.copy_(x)
+        prof = plan.profile_stack(h, iters=5, stream=stream)
+        # Distinct experts per layer, from the ids the stack produces.
+        hh = x.clone()
+        y = torch.empty_like(hh)
+        ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
+        active = []
+        for layer in range(cfg.layers):
+            plan.forward(layer, hh, y, ids, None, stream=stream)
+            torch.cuda.synchronize()
+            active.append(len(set(ids.cpu().numpy().ravel().tolist())))
+            hh = hh + y
+        plan.check(stream=stream)
+
+    times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max = float(times[0]), float(times[1])
+
+    step_bytes, gu_bytes = decode_bytes(cfg, active, fmt_int8)
+    hbm_peak, peak_kind = measured_peaks()
+    gu_achieved = (sum(gu_bytes) / len(gu_bytes)) / (prof["gate_up"] * 1e-3) / 1e9
+    step_gbs = step_bytes / (ms_max * 1e-3) / 1e9
+    traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_layer0 = host_layer_weights(cfg)
+        t_layer, kind, cores, reps = cpu_reference_layer_time(cfg, host_layer0, T, args.cpu_budget,
+                                                              os.cpu_count() or 1)
+        cpu = {"value": T / (t_layer * cfg.layers), "unit": "tokens/s", "cores": cores, "kind": kind,
+               "sample": f"layer 0 of {cfg.layers} at batch {T}: median of {reps} calls over ~{args.cpu_budget:.0f} s, "
+                         f"scaled to the {cfg.layers}-layer stack"}
+
+    if rank == 0:
+        launches_per_step = 3 * cfg.layers
+        line = {
+            "metric": "MoE layer tokens/s (decode)",
+            "value": world * T / (ms_max * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8" if fmt_int8 else "bf16", "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: {cfg.layers}-layer MoE stack, batch {T}",
+                       "global_batch": T * world, "layers": cfg.layers, "hidden": cfg.hidden,
+                       "experts": cfg.experts, "top_k": cfg.top_k, "ffn": cfg.ffn, "shared_ffn": cfg.shared_ffn,
+                       "weights": args.format, "renormalize": True,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "no flush: 20 GB of weights per step pass exceed the 126 MB L2"},
+            "roofline": {"bound": "hbm", "kernel": "gate_up_decode", "achieved": gu_achieved, "peak": hbm_peak,
+                         "peak_source": peak_kind, "unit": "GB/s", "frac": gu_achieved / hbm_peak,
+                         "traffic": traffic,
+                         "step_achieved": step_gbs, "step_frac": step_gbs / hbm_peak,
+                         "algorithmic_bytes_per_step": step_bytes,
+                         "kernel_ms": {k: round(v, 5) for k, v in prof.items()},
+                         "distinct_experts_per_layer": active},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * T / (e2e_max * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * cfg.hidden * 4, "d2h_bytes_per_step": T * cfg.hidden * 4,
+                    "ms_per_step": e2e_max},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

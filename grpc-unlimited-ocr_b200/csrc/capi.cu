@@ -1,0 +1,615 @@
+// The C ABI (include/uocr_moe.h): plan lifetime, weight upload, the MoE
+// forward dispatch, and the op-level mirrors of the reference's uocr::cuda
+// MoE ops. Host code only; kernels live in router.cu, decode.cu, weights.cu.
+//
+// The dispatch replaces CudaDecoder::moe (src/model/cuda/cuda_decoder.cpp:
+// 137-192): it routes on the device for every row count (the reference
+// downloads the logits and routes on the host when rows > 1, :159-175) and
+// keeps all scratch in one arena allocated with the plan (the reference
+// cudaMallocAsync's per op, gemv_ops.cu:176, ops.cu:275).
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/uocr_moe.h"
+#include "moe_kernels.h"
+
+using namespace uocr_b200;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& what) {
+  g_error = what;
+  return code;
+}
+
+int cuda_fail(cudaError_t st, const char* what) {
+  return fail(st == cudaErrorMemoryAllocation ? UOCR_ERR_OUT_OF_MEMORY : UOCR_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(st));
+}
+
+#define UOCR_TRY(expr, what)                     \
+  do {                                           \
+    cudaError_t st_ = (expr);                    \
+    if (st_ != cudaSuccess) return cuda_fail(st_, what); \
+  } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device-side view of one layer's weights.
+struct LayerDev {
+  void* block = nullptr;
+  size_t bytes = 0;
+  bool loaded = false;
+  float* router = nullptr;
+  float* bias = nullptr;
+  void* gate = nullptr;
+  void* up = nullptr;
+  void* down = nullptr;
+  void* sgate = nullptr;
+  void* sup = nullptr;
+  void* sdown = nullptr;
+  float* gate_s = nullptr;
+  float* up_s = nullptr;
+  float* down_s = nullptr;
+  float* sgate_s = nullptr;
+  float* sup_s = nullptr;
+  float* sdown_s = nullptr;
+};
+
+// Bump allocator over one device block.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  template <typename T>
+  T* take(size_t count) {
+    off = align_up(off, 256);
+    T* p = base == nullptr ? nullptr : reinterpret_cast<T*>(base + off);
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    cudaGetDevice(&prev_);
+    if (prev_ != device) cudaSetDevice(device);
+  }
+  ~DeviceGuard() { cudaSetDevice(prev_); }
+
+ private:
+  int prev_ = 0;
+};
+
+}  // namespace
+
+struct uocr_moe_plan {
+  uocr_moe_desc d{};
+  int sm_count = 0;
+  int decode_rows = 0;  // largest row count the decode kernels take
+  std::vector<LayerDev> layers;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  size_t weight_bytes = 0;
+  float* logits = nullptr;
+  int* ids = nullptr;
+  float* weights = nullptr;
+  DecodeRoute* route = nullptr;
+  __nv_bfloat16* act = nullptr;
+  __nv_bfloat16* act_s = nullptr;
+  unsigned* counter = nullptr;
+  ErrorWord* err = nullptr;
+
+  // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
+  struct GraphEntry {
+    const float* h;
+    int64_t rows;
+    cudaStream_t stream;
+    cudaGraphExec_t exec;
+    uint64_t last_use;
+  };
+  std::vector<GraphEntry> graphs;
+  uint64_t tick = 0;
+  static constexpr size_t kMaxGraphs = 8;
+
+  size_t elem_bytes() const { return d.weight_format == UOCR_WEIGHT_INT8 ? 1 : 2; }
+
+  void carve_layer(Carver& c, LayerDev& L) const {
+    const size_t H = d.hidden, E = d.routed_experts, F = d.expert_ffn, S = d.shared_ffn, eb = elem_bytes();
+    L.router = c.take<float>(E * H);
+    L.bias = d.router_bias ? c.take<float>(E) : nullptr;
+    L.gate = c.take<char>(E * F * H * eb);
+    L.up = c.take<char>(E * F * H * eb);
+    L.down = c.take<char>(E * H * F * eb);
+    L.sgate = c.take<char>(S * H * eb);
+    L.sup = c.take<char>(S * H * eb);
+    L.sdown = c.take<char>(H * S * eb);
+    if (d.weight_format == UOCR_WEIGHT_INT8) {
+      L.gate_s = c.take<float>(E * F);
+      L.up_s = c.take<float>(E * F);
+      L.down_s = c.take<float>(E * H);
+      L.sgate_s = c.take<float>(S);
+      L.sup_s = c.take<float>(S);
+      L.sdown_s = c.take<float>(H);
+    }
+  }
+
+  void carve_arena(Carver& c) {
+    const size_t rows = d.max_rows, E = d.routed_experts, K = d.experts_per_token, F = d.expert_ffn,
+                 S = d.shared_ffn, dr = decode_rows;
+    logits = c.take<float>(rows * E);
+    ids = c.take<int>(rows * K);
+    weights = c.take<float>(rows * K);
+    route = c.take<DecodeRoute>(1);
+    act = c.take<__nv_bfloat16>(dr * K * F);
+    act_s = c.take<__nv_bfloat16>(dr * (S > 0 ? S : 1));
+    counter = c.take<unsigned>(1);
+    err = c.take<ErrorWord>(1);
+  }
+};
+
+namespace {
+
+// Shared body of the expert_ffn_one mirrors: scratch from cudaMallocAsync on
+// the stream, as the reference's expert_ffn does (gemv_ops.cu:176,182).
+template <typename Launch>
+int ffn_one(const float* x, int64_t hidden, int64_t ffn, const int64_t* ids, const float* weights, int64_t k,
+            float* out, int64_t experts_hint, cudaStream_t stream, Launch&& launch) {
+  if (hidden <= 0 || hidden % 16 != 0 || ffn <= 0 || ffn % 16 != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one: hidden and ffn must be positive multiples of 16");
+  if (k <= 0 || k > kMaxTopK) return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one: k must be in [1, 8]");
+  if (x == nullptr || ids == nullptr || weights == nullptr || out == nullptr)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one: null pointer");
+  const size_t route_off = 0, act_off = align_up(sizeof(DecodeRoute), 256),
+               err_off = align_up(act_off + static_cast<size_t>(k * ffn) * 2, 256),
+               total = err_off + sizeof(ErrorWord);
+  char* scratch = nullptr;
+  UOCR_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), total, stream), "expert_ffn_one: scratch");
+  auto* route = reinterpret_cast<DecodeRoute*>(scratch + route_off);
+  auto* act = reinterpret_cast<__nv_bfloat16*>(scratch + act_off);
+  auto* err = reinterpret_cast<ErrorWord*>(scratch + err_off);
+  cudaError_t st = cudaMemsetAsync(err, 0, sizeof(ErrorWord), stream);
+  if (st == cudaSuccess)
+    st = launch_route_from_ids(ids, weights, static_cast<int>(k), static_cast<int>(experts_hint), route, err, stream);
+  if (st == cudaSuccess) st = launch(route, act, err);
+  cudaFreeAsync(scratch, stream);
+  if (st != cudaSuccess) return cuda_fail(st, "expert_ffn_one");
+  return UOCR_OK;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* uocr_last_error(void) { return g_error.c_str(); }
+int uocr_abi_version(void) { return UOCR_MOE_ABI_VERSION; }
+
+int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
+  if (desc == nullptr || out == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: null argument");
+  *out = nullptr;
+  const uocr_moe_desc& d = *desc;
+  if (d.hidden <= 0 || d.hidden % 16 != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: hidden must be a positive multiple of 16");
+  if (d.routed_experts <= 0 || d.routed_experts > kMaxExperts)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: routed_experts must be in [1, 128]");
+  if (d.experts_per_token <= 0 || d.experts_per_token > kMaxTopK || d.experts_per_token > d.routed_experts)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: experts_per_token must be in [1, min(8, experts)]");
+  if (d.expert_ffn <= 0 || d.expert_ffn % 16 != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: expert_ffn must be a positive multiple of 16");
+  if (d.shared_ffn < 0 || d.shared_ffn % 16 != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: shared_ffn must be a non-negative multiple of 16");
+  if (d.layers <= 0 || d.max_rows <= 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: layers and max_rows must be positive");
+  if (d.weight_format != UOCR_WEIGHT_BF16 && d.weight_format != UOCR_WEIGHT_INT8)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: weight_format must be bf16 (0) or int8 (1)");
+  int ndev = 0;
+  UOCR_TRY(cudaGetDeviceCount(&ndev), "plan_create: cudaGetDeviceCount");
+  if (d.device < 0 || d.device >= ndev) return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: no such device");
+  DeviceGuard guard(d.device);
+
+  auto* p = new uocr_moe_plan;
+  p->d = d;
+  UOCR_TRY(cudaDeviceGetAttribute(&p->sm_count, cudaDevAttrMultiProcessorCount, d.device), "plan_create: SM count");
+  int smem_optin = 0;
+  UOCR_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device),
+           "plan_create: shared memory limit");
+  // The decode kernels stage the batch's rows in shared memory.
+  int dr = static_cast<int>(d.max_rows < kDecodeMaxRows ? d.max_rows : kDecodeMaxRows);
+  while (dr > 0 && (static_cast<size_t>(d.hidden) + static_cast<size_t>(dr) * (d.hidden + 8)) * 4 >
+                       static_cast<size_t>(smem_optin))
+    --dr;
+  p->decode_rows = dr;
+
+  Carver probe{nullptr};
+  LayerDev tmp;
+  p->carve_layer(probe, tmp);
+  const size_t layer_bytes = align_up(probe.off, 256);
+  p->layers.resize(static_cast<size_t>(d.layers));
+  for (auto& L : p->layers) {
+    cudaError_t st = cudaMalloc(&L.block, layer_bytes);
+    if (st != cudaSuccess) {
+      uocr_moe_plan_destroy(p);
+      return cuda_fail(st, "plan_create: weight allocation");
+    }
+    L.bytes = layer_bytes;
+    Carver c{static_cast<char*>(L.block)};
+    p->carve_layer(c, L);
+    p->weight_bytes += layer_bytes;
+  }
+  Carver ap{nullptr};
+  p->carve_arena(ap);
+  p->arena_bytes = align_up(ap.off, 256);
+  cudaError_t st = cudaMalloc(&p->arena, p->arena_bytes);
+  if (st != cudaSuccess) {
+    uocr_moe_plan_destroy(p);
+    return cuda_fail(st, "plan_create: arena allocation");
+  }
+  Carver ac{p->arena};
+  p->carve_arena(ac);
+  st = cudaMemset(p->arena, 0, p->arena_bytes);
+  if (st != cudaSuccess) {
+    uocr_moe_plan_destroy(p);
+    return cuda_fail(st, "plan_create: arena clear");
+  }
+  *out = p;
+  return UOCR_OK;
+}
+
+int uocr_moe_plan_destroy(uocr_moe_plan* p) {
+  if (p == nullptr) return UOCR_OK;
+  DeviceGuard guard(p->d.device);
+  for (auto& g : p->graphs) cudaGraphExecDestroy(g.exec);
+  for (auto& L : p->layers)
+    if (L.block != nullptr) cudaFree(L.block);
+  if (p->arena != nullptr) cudaFree(p->arena);
+  delete p;
+  return UOCR_OK;
+}
+
+int uocr_moe_plan_bytes(const uocr_moe_plan* p, int64_t* weight_bytes, int64_t* arena_bytes) {
+  if (p == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_bytes: null plan");
+  if (weight_bytes) *weight_bytes = static_cast<int64_t>(p->weight_bytes);
+  if (arena_bytes) *arena_bytes = static_cast<int64_t>(p->arena_bytes);
+  return UOCR_OK;
+}
+
+namespace {
+
+// Brings one matrix [rows, cols] into the plan's format at `dst` (+ scales).
+int upload_matrix(const uocr_moe_plan* p, const uocr_moe_layer_src& src, const void* from, int64_t rows,
+                  int64_t cols, void* dst, float* scales, cudaStream_t stream, const char* name) {
+  if (rows * cols == 0) return UOCR_OK;
+  if (from == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, std::string("set_layer: missing ") + name);
+  const size_t sb = src.dtype == UOCR_DTYPE_BF16 ? 2 : 4;
+  const size_t n = static_cast<size_t>(rows * cols);
+  const void* dev_src = from;
+  void* staging = nullptr;
+  if (src.memory == UOCR_MEMORY_HOST) {
+    UOCR_TRY(cudaMallocAsync(&staging, n * sb, stream), "set_layer: staging allocation");
+    UOCR_TRY(cudaMemcpyAsync(staging, from, n * sb, cudaMemcpyHostToDevice, stream), "set_layer: upload");
+    dev_src = staging;
+  }
+  cudaError_t st = cudaSuccess;
+  if (p->d.weight_format == UOCR_WEIGHT_INT8) {
+    st = launch_quantize_rows(dev_src, src.dtype == UOCR_DTYPE_BF16, rows, cols, cols, static_cast<int8_t*>(dst),
+                              scales, stream);
+  } else if (src.dtype == UOCR_DTYPE_BF16) {
+    st = cudaMemcpyAsync(dst, dev_src, n * 2, cudaMemcpyDeviceToDevice, stream);
+  } else {
+    st = launch_f32_to_bf16(static_cast<const float*>(dev_src), static_cast<__nv_bfloat16*>(dst),
+                            static_cast<int64_t>(n), stream);
+  }
+  if (staging != nullptr) cudaFreeAsync(staging, stream);
+  if (st != cudaSuccess) return cuda_fail(st, "set_layer: conversion");
+  if (src.memory == UOCR_MEMORY_HOST) UOCR_TRY(cudaStreamSynchronize(stream), "set_layer: upload wait");
+  return UOCR_OK;
+}
+
+int copy_f32(const uocr_moe_layer_src& src, const float* from, float* dst, size_t n, cudaStream_t stream,
+             const char* name) {
+  if (from == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, std::string("set_layer: missing ") + name);
+  UOCR_TRY(cudaMemcpyAsync(dst, from, n * 4,
+                           src.memory == UOCR_MEMORY_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                           stream),
+           "set_layer: fp32 copy");
+  return UOCR_OK;
+}
+
+}  // namespace
+
+int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src* src, void* stream_v) {
+  if (p == nullptr || src == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer: null argument");
+  if (layer < 0 || layer >= p->d.layers) return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer: layer out of range");
+  if (src->memory != UOCR_MEMORY_HOST && src->memory != UOCR_MEMORY_DEVICE)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer: memory must be host (0) or device (1)");
+  if (src->dtype != UOCR_DTYPE_F32 && src->dtype != UOCR_DTYPE_BF16)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer: dtype must be f32 (0) or bf16 (1)");
+  if (p->d.router_bias && src->router_bias == nullptr)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer: the plan expects a router bias");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  LayerDev& L = p->layers[static_cast<size_t>(layer)];
+  const int64_t H = p->d.hidden, E = p->d.routed_experts, F = p->d.expert_ffn, S = p->d.shared_ffn;
+  int rc = copy_f32(*src, src->router, L.router, static_cast<size_t>(E * H), stream, "router");
+  if (rc == UOCR_OK && p->d.router_bias) rc = copy_f32(*src, src->router_bias, L.bias, E, stream, "router_bias");
+  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->gate, E * F, H, L.gate, L.gate_s, stream, "gate");
+  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->up, E * F, H, L.up, L.up_s, stream, "up");
+  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->down, E * H, F, L.down, L.down_s, stream, "down");
+  if (rc == UOCR_OK && S > 0) {
+    rc = upload_matrix(p, *src, src->shared_gate, S, H, L.sgate, L.sgate_s, stream, "shared_gate");
+    if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->shared_up, S, H, L.sup, L.sup_s, stream, "shared_up");
+    if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->shared_down, H, S, L.sdown, L.sdown_s, stream, "shared_down");
+  }
+  if (rc == UOCR_OK && src->memory == UOCR_MEMORY_HOST)
+    UOCR_TRY(cudaStreamSynchronize(stream), "set_layer: host copies");
+  if (rc == UOCR_OK) L.loaded = true;
+  return rc;
+}
+
+namespace {
+
+// One layer on `rows` rows: route, then experts. resid != null adds the
+// layer input back (the stack's residual); y may then alias resid.
+int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows, const float* resid, float* y,
+              cudaStream_t stream, const cudaEvent_t* ev = nullptr) {
+  const uocr_moe_desc& d = p->d;
+  const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts),
+            K = static_cast<int>(d.experts_per_token), F = static_cast<int>(d.expert_ffn),
+            S = static_cast<int>(d.shared_ffn);
+  if (rows > p->decode_rows)
+    return fail(UOCR_ERR_UNSUPPORTED, "forward: rows above the decode limit need the prefill path, not built yet");
+  UOCR_TRY(launch_router_decode(x, T, H, L.router, L.bias, E, K, d.renormalize, p->logits, p->ids, p->weights,
+                                p->route, p->counter, p->err, stream),
+           "forward: router");
+  if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
+  cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
+  if (d.weight_format == UOCR_WEIGHT_BF16) {
+    auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
+    UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
+                                        b(L.sdown), p->route, p->act, p->act_s, resid, y, p->err, p->sm_count,
+                                        stream, between),
+             "forward: experts");
+  } else {
+    auto q = [](void* v, float* s, int64_t cols) { return Q8Rows{static_cast<const int8_t*>(v), s, cols}; };
+    UOCR_TRY(launch_decode_experts_q8(x, T, H, F, S, q(L.gate, L.gate_s, H), q(L.up, L.up_s, H),
+                                      q(L.down, L.down_s, F), q(L.sgate, L.sgate_s, H), q(L.sup, L.sup_s, H),
+                                      q(L.sdown, L.sdown_s, S), p->route, p->act, p->act_s, resid, y, p->err,
+                                      p->sm_count, stream, between),
+             "forward: experts");
+  }
+  return UOCR_OK;
+}
+
+}  // namespace
+
+int uocr_moe_forward(uocr_moe_plan* p, int64_t layer, const float* x, int64_t rows, float* y, int32_t* ids,
+                     float* weights, void* stream_v) {
+  if (p == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null plan");
+  if (layer < 0 || layer >= p->d.layers) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: layer out of range");
+  if (rows < 0 || rows > p->d.max_rows) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: rows outside [0, max_rows]");
+  if (rows == 0) return UOCR_OK;
+  if (x == nullptr || y == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null x or y");
+  if (x == y) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: x and y must not overlap");
+  const LayerDev& L = p->layers[static_cast<size_t>(layer)];
+  if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: layer weights not set");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  int rc = run_layer(p, L, x, rows, nullptr, y, stream);
+  if (rc != UOCR_OK) return rc;
+  const size_t nk = static_cast<size_t>(rows * p->d.experts_per_token);
+  if (ids != nullptr)
+    UOCR_TRY(cudaMemcpyAsync(ids, p->ids, nk * 4, cudaMemcpyDeviceToDevice, stream), "forward: ids copy");
+  if (weights != nullptr)
+    UOCR_TRY(cudaMemcpyAsync(weights, p->weights, nk * 4, cudaMemcpyDeviceToDevice, stream), "forward: weights copy");
+  return UOCR_OK;
+}
+
+int uocr_moe_forward_stack(uocr_moe_plan* p, float* h, int64_t rows, void* stream_v) {
+  if (p == nullptr || h == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: null argument");
+  if (rows < 0 || rows > p->d.max_rows)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: rows outside [0, max_rows]");
+  if (rows == 0) return UOCR_OK;
+  for (const auto& L : p->layers)
+    if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: a layer's weights are not set");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  auto run_all = [&]() {
+    for (const auto& L : p->layers) {
+      int rc = run_layer(p, L, h, rows, h, h, stream);
+      if (rc != UOCR_OK) return rc;
+    }
+    return static_cast<int>(UOCR_OK);
+  };
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  UOCR_TRY(cudaStreamIsCapturing(stream, &cap), "forward_stack: capture status");
+  if ((p->d.flags & UOCR_PLAN_NO_GRAPHS) != 0 || cap != cudaStreamCaptureStatusNone || stream == nullptr ||
+      stream == cudaStreamLegacy)
+    return run_all();
+  for (auto& g : p->graphs)
+    if (g.h == h && g.rows == rows && g.stream == stream) {
+      g.last_use = ++p->tick;
+      UOCR_TRY(cudaGraphLaunch(g.exec, stream), "forward_stack: graph launch");
+      return UOCR_OK;
+    }
+  // First call for this (h, rows, stream): capture the stack once.
+  UOCR_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "forward_stack: begin capture");
+  const int rc = run_all();
+  cudaGraph_t graph = nullptr;
+  const cudaError_t end = cudaStreamEndCapture(stream, &graph);
+  if (rc != UOCR_OK) {
+    if (graph != nullptr) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (end != cudaSuccess) return cuda_fail(end, "forward_stack: end capture");
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (inst != cudaSuccess) return cuda_fail(inst, "forward_stack: instantiate");
+  if (p->graphs.size() >= uocr_moe_plan::kMaxGraphs) {
+    size_t oldest = 0;
+    for (size_t i = 1; i < p->graphs.size(); ++i)
+      if (p->graphs[i].last_use < p->graphs[oldest].last_use) oldest = i;
+    cudaGraphExecDestroy(p->graphs[oldest].exec);
+    p->graphs.erase(p->graphs.begin() + static_cast<std::ptrdiff_t>(oldest));
+  }
+  p->graphs.push_back({h, rows, stream, exec, ++p->tick});
+  UOCR_TRY(cudaGraphLaunch(exec, stream), "forward_stack: graph launch");
+  return UOCR_OK;
+}
+
+int uocr_moe_profile_stack(uocr_moe_plan* p, float* h, int64_t rows, int32_t iters, float* ms, void* stream_v) {
+  if (p == nullptr || h == nullptr || ms == nullptr || iters <= 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "profile_stack: bad argument");
+  if (rows <= 0 || rows > p->d.max_rows)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "profile_stack: rows outside [1, max_rows]");
+  for (const auto& L : p->layers)
+    if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "profile_stack: a layer's weights are not set");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const size_t nl = p->layers.size();
+  // Per layer and pass: start, after router, after gate/up, after down.
+  std::vector<cudaEvent_t> ev(static_cast<size_t>(iters) * nl * 3 + 1);
+  for (auto& e : ev) UOCR_TRY(cudaEventCreate(&e), "profile_stack: event");
+  int rc = UOCR_OK;
+  size_t k = 0;
+  UOCR_TRY(cudaEventRecord(ev[k++], stream), "profile_stack: event");
+  for (int it = 0; it < iters && rc == UOCR_OK; ++it)
+    for (size_t l = 0; l < nl && rc == UOCR_OK; ++l) {
+      rc = run_layer(p, p->layers[l], h, rows, h, h, stream, &ev[k]);
+      if (rc == UOCR_OK) rc = cudaEventRecord(ev[k + 2], stream) == cudaSuccess ? UOCR_OK : UOCR_ERR_CUDA;
+      k += 3;
+    }
+  double sum[3] = {0, 0, 0};
+  float total = 0;
+  if (rc == UOCR_OK && cudaEventSynchronize(ev[k - 1]) == cudaSuccess) {
+    // Layer pass j spans ev[3j] (its start) .. ev[3j+3] (end of its down kernel).
+    for (size_t j = 0; j < static_cast<size_t>(iters) * nl; ++j) {
+      float a = 0, b = 0, c = 0;
+      cudaEventElapsedTime(&a, ev[3 * j], ev[3 * j + 1]);
+      cudaEventElapsedTime(&b, ev[3 * j + 1], ev[3 * j + 2]);
+      cudaEventElapsedTime(&c, ev[3 * j + 2], ev[3 * j + 3]);
+      sum[0] += a;
+      sum[1] += b;
+      sum[2] += c;
+    }
+    cudaEventElapsedTime(&total, ev[0], ev[k - 1]);
+  } else if (rc == UOCR_OK) {
+    rc = fail(UOCR_ERR_CUDA, "profile_stack: synchronise");
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  if (rc != UOCR_OK) return rc;
+  const double n = static_cast<double>(iters) * static_cast<double>(nl);
+  for (int i = 0; i < 3; ++i) ms[i] = static_cast<float>(sum[i] / n);
+  ms[3] = total / static_cast<float>(iters);
+  return UOCR_OK;
+}
+
+int uocr_moe_check(uocr_moe_plan* p, void* stream_v) {
+  if (p == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "check: null plan");
+  DeviceGuard guard(p->d.device);
+  UOCR_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream_v)), "check: stream");
+  ErrorWord e{};
+  UOCR_TRY(cudaMemcpy(&e, p->err, sizeof(e), cudaMemcpyDeviceToHost), "check: error word");
+  if (e.code == kDevOk) return UOCR_OK;
+  UOCR_TRY(cudaMemset(p->err, 0, sizeof(ErrorWord)), "check: clear");
+  char buf[160];
+  std::snprintf(buf, sizeof(buf), "device error %d at site %d (%d, %d)", e.code, e.where, e.a, e.b);
+  return fail(e.code == kDevWaitTimeout ? UOCR_ERR_TIMEOUT : UOCR_ERR_DEVICE, buf);
+}
+
+// ---- op-level mirrors ----------------------------------------------------
+
+int uocr_expert_topk(const float* logits, int64_t rows, int64_t experts, int64_t k, int32_t renormalize,
+                     int64_t* ids, float* weights, void* stream) {
+  if (experts > kMaxExperts) return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_topk: more than 128 experts");
+  if (experts <= 0 || k <= 0 || k > experts || k > kMaxTopK || rows < 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_topk: bad shape");
+  if (rows > 0 && (logits == nullptr || ids == nullptr || weights == nullptr))
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_topk: null pointer");
+  UOCR_TRY(launch_topk_rows(logits, rows, static_cast<int>(experts), static_cast<int>(k), renormalize, ids, weights,
+                            static_cast<cudaStream_t>(stream)),
+           "expert_topk");
+  return UOCR_OK;
+}
+
+
+int uocr_expert_ffn_one(const float* x, int64_t hidden, int64_t ffn, const uint16_t* gate, const uint16_t* up,
+                        const uint16_t* down, const int64_t* ids, const float* weights, int64_t k, float* out,
+                        void* stream_v) {
+  if (gate == nullptr || up == nullptr || down == nullptr)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one: null weights");
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const int sms = device_sms();
+  auto b = [](const uint16_t* v) { return reinterpret_cast<const __nv_bfloat16*>(v); };
+  // Expert ids are not bounded by a plan here; the stacks' extent is the
+  // caller's contract, as in the reference (ops.h:82-89).
+  return ffn_one(x, hidden, ffn, ids, weights, k, out, kMaxExperts, stream,
+                 [&](DecodeRoute* route, __nv_bfloat16* act, ErrorWord* err) {
+                   return launch_decode_experts_bf16(x, 1, static_cast<int>(hidden), static_cast<int>(ffn), 0,
+                                                     b(gate), b(up), b(down), nullptr, nullptr, nullptr, route, act,
+                                                     nullptr, nullptr, out, err, sms, stream);
+                 });
+}
+
+int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const int8_t* gate_q, const float* gate_s,
+                           const int8_t* up_q, const float* up_s, const int8_t* down_q, const float* down_s,
+                           const int64_t* ids, const float* weights, int64_t k, float* out, void* stream_v) {
+  if (gate_q == nullptr || up_q == nullptr || down_q == nullptr || gate_s == nullptr || up_s == nullptr ||
+      down_s == nullptr)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one_q8: null weights");
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const int sms = device_sms();
+  const int H = static_cast<int>(hidden), F = static_cast<int>(ffn);
+  return ffn_one(x, hidden, ffn, ids, weights, k, out, kMaxExperts, stream,
+                 [&](DecodeRoute* route, __nv_bfloat16* act, ErrorWord* err) {
+                   const Q8Rows none{nullptr, nullptr, 0};
+                   return launch_decode_experts_q8(x, 1, H, F, 0, Q8Rows{gate_q, gate_s, H}, Q8Rows{up_q, up_s, H},
+                                                   Q8Rows{down_q, down_s, F}, none, none, none, route, act, nullptr,
+                                                   nullptr, out, err, sms, stream);
+                 });
+}
+
+int uocr_quantize_q8(const void* w, int32_t dtype, int64_t rows, int64_t cols, int64_t group, int8_t* q,
+                     float* scales, void* stream) {
+  if (rows < 0 || cols <= 0 || group <= 0 || cols % group != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "quantize_q8: the group must divide the row width");
+  if (dtype != UOCR_DTYPE_F32 && dtype != UOCR_DTYPE_BF16)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "quantize_q8: dtype must be f32 or bf16");
+  if (rows > 0 && (w == nullptr || q == nullptr || scales == nullptr))
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "quantize_q8: null pointer");
+  UOCR_TRY(launch_quantize_rows(w, dtype == UOCR_DTYPE_BF16, rows, cols, group, q, scales,
+                                static_cast<cudaStream_t>(stream)),
+           "quantize_q8");
+  return UOCR_OK;
+}
+
+uint64_t uocr_synth_stream(uint64_t layer, uint64_t kind, uint64_t index) {
+  return (layer << 40) | (kind << 32) | index;
+}
+
+int uocr_synth_fill(uint64_t seed, uint64_t stream_id, float sigma, int64_t offset, int64_t n, int32_t dtype,
+                    void* out, void* stream) {
+  if (n < 0 || offset < 0) return fail(UOCR_ERR_INVALID_ARGUMENT, "synth_fill: negative size");
+  if (dtype != UOCR_DTYPE_F32 && dtype != UOCR_DTYPE_BF16)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "synth_fill: dtype must be f32 or bf16");
+  if (n > 0 && out == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "synth_fill: null output");
+  UOCR_TRY(launch_synth(seed, stream_id, sigma, offset, n, dtype == UOCR_DTYPE_BF16, out,
+                        static_cast<cudaStream_t>(stream)),
+           "synth_fill");
+  return UOCR_OK;
+}
+
+}  // extern "C"

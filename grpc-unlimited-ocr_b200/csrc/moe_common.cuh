@@ -1,0 +1,122 @@
+// Shared device-side pieces of the MoE path: limits, the error word, the
+// decode routing table, weight row views and small numeric helpers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace uocr_b200 {
+
+constexpr int kWarp = 32;
+constexpr int kMaxExperts = 128;     // the reference's expert_topk limit (ops.cu:653)
+constexpr int kMaxTopK = 8;
+constexpr int kDecodeMaxRows = 16;   // rows at or below this take the weight-streaming decode path
+constexpr int kMaxActive = kDecodeMaxRows * kMaxTopK;  // distinct experts one decode batch can touch
+constexpr int kMaxDevices = 64;
+constexpr int kMaxDynamicSmem = 227 * 1024;  // sm_100 opt-in limit per block
+
+// A kernel that meets a bad index, a capacity overflow or a wait that ran out
+// records it here instead of touching memory it should not; the host reads
+// it through uocr_moe_check. The first error wins.
+enum DeviceErrorCode : int {
+  kDevOk = 0,
+  kDevBadIndex = 1,
+  kDevCapacity = 2,
+  kDevWaitTimeout = 3,
+};
+struct ErrorWord {
+  int code;
+  int where;
+  int a;
+  int b;
+};
+__device__ inline void raise_error(ErrorWord* e, int code, int where, int a, int b) {
+  if (atomicCAS(&e->code, 0, code) == 0) {
+    e->where = where;
+    e->a = a;
+    e->b = b;
+  }
+}
+
+// Routing of one decode batch (rows <= kDecodeMaxRows), written by the
+// router's last block. Experts appear once each, in ascending id order (for
+// the op-level mirror of expert_ffn_one: in rank order), with the batch rows
+// routed to them in row order. Slot = slot_base[u] + s indexes the [slots, F]
+// activation scratch.
+struct DecodeRoute {
+  int active_count;
+  int slot_total;
+  int active_expert[kMaxActive];
+  int tok_count[kMaxActive];
+  int slot_base[kMaxActive];
+  int tok_index[kMaxActive][kDecodeMaxRows];
+  float tok_weight[kMaxActive][kDecodeMaxRows];
+};
+
+// A stack of weight rows: bf16, or int8 with one fp32 scale per row.
+struct Bf16Rows {
+  const __nv_bfloat16* w;
+  int64_t cols;
+};
+struct Q8Rows {
+  const int8_t* q;
+  const float* scale;
+  int64_t cols;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// silu(g) * u as the reference backend writes it: v * (1 / (1 + exp(-v)))
+// (src/backend/reference/ops.cpp:40,163-167), then times the up projection.
+__device__ __forceinline__ float swiglu(float g, float u) {
+  const float s = 1.0f / (1.0f + expf(-g));
+  return (g * s) * u;
+}
+
+// Eight bf16 weights (one 128-bit load) dotted with eight fp32 inputs.
+__device__ __forceinline__ float dot8_bf16(const uint4& w, const float4& x0, const float4& x1) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&w);
+  const float2 a = __bfloat1622float2(p[0]), b = __bfloat1622float2(p[1]);
+  const float2 c = __bfloat1622float2(p[2]), d = __bfloat1622float2(p[3]);
+  float s = a.x * x0.x;
+  s = fmaf(a.y, x0.y, s);
+  s = fmaf(b.x, x0.z, s);
+  s = fmaf(b.y, x0.w, s);
+  s = fmaf(c.x, x1.x, s);
+  s = fmaf(c.y, x1.y, s);
+  s = fmaf(d.x, x1.z, s);
+  s = fmaf(d.y, x1.w, s);
+  return s;
+}
+
+// Eight bf16 weights dotted with eight bf16 activations (one 128-bit load each).
+__device__ __forceinline__ float dot8_bf16_bf16(const uint4& w, const uint4& a) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&w);
+  const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&a);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 wf = __bfloat1622float2(p[i]), af = __bfloat1622float2(q[i]);
+    s = fmaf(wf.x, af.x, s);
+    s = fmaf(wf.y, af.y, s);
+  }
+  return s;
+}
+
+// Four int8 weights packed in a word, sign-extended to fp32.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& a, float& b, float& c, float& d) {
+  a = static_cast<float>(static_cast<int8_t>(w & 0xffu));
+  b = static_cast<float>(static_cast<int8_t>((w >> 8) & 0xffu));
+  c = static_cast<float>(static_cast<int8_t>((w >> 16) & 0xffu));
+  d = static_cast<float>(static_cast<int8_t>(w >> 24));
+}
+
+}  // namespace uocr_b200

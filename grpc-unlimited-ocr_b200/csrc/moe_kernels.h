@@ -1,0 +1,40 @@
+// Kernel launchers of the MoE path (host-callable, stream-ordered, no
+// allocation, no synchronisation). Each returns the launch status.
+#pragma once
+
+#include "moe_common.cuh"
+
+namespace uocr_b200 {
+
+// ---- router (router.cu) ----
+cudaError_t launch_router_decode(const float* x, int T, int H, const float* router, const float* bias, int E, int K,
+                                 int renorm, float* logits, int* ids, float* weights, DecodeRoute* route,
+                                 unsigned* counter, ErrorWord* err, cudaStream_t stream);
+cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,
+                             float* weights, cudaStream_t stream);
+cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int K, int E, DecodeRoute* route,
+                                  ErrorWord* err, cudaStream_t stream);
+
+// ---- decode experts (decode.cu) ----
+// Launches gate/up then down+combine; `between` (optional) is recorded
+// between the two, for per-kernel timing.
+cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int S, const __nv_bfloat16* gate,
+                                       const __nv_bfloat16* up, const __nv_bfloat16* down,
+                                       const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
+                                       const __nv_bfloat16* sdown, const DecodeRoute* route, __nv_bfloat16* act,
+                                       __nv_bfloat16* act_s, const float* resid, float* y, ErrorWord* err,
+                                       int sm_count, cudaStream_t stream, cudaEvent_t between = nullptr);
+cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
+                                     Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown, const DecodeRoute* route,
+                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
+                                     ErrorWord* err, int sm_count, cudaStream_t stream,
+                                     cudaEvent_t between = nullptr);
+
+// ---- weights and synthetic inputs (weights.cu) ----
+cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const void* w, bool bf16, int64_t rows, int64_t cols, int64_t group, int8_t* q,
+                                 float* scales, cudaStream_t stream);
+cudaError_t launch_synth(uint64_t seed, uint64_t stream_id, float sigma, int64_t offset, int64_t n, bool bf16,
+                         void* out, cudaStream_t stream);
+
+}  // namespace uocr_b200

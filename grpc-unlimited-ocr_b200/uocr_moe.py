@@ -1,0 +1,210 @@
+"""Python binding of the C ABI in include/uocr_moe.h (ctypes over libuocr_moe.so).
+
+This is the host-side mirror tests and bench.py call: torch supplies device
+memory and streams; every computation happens in libuocr_moe.so's sm_100a
+kernels. There is no fallback: if the library is missing the import of
+`lib()` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libuocr_moe.so")
+
+UOCR_OK = 0
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARGUMENT", 2: "UNSUPPORTED", 3: "CUDA", 4: "OUT_OF_MEMORY", 5: "DEVICE",
+                6: "TIMEOUT", 7: "COMM"}
+WEIGHT_BF16, WEIGHT_INT8 = 0, 1
+MEMORY_HOST, MEMORY_DEVICE = 0, 1
+DTYPE_F32, DTYPE_BF16 = 0, 1
+PLAN_NO_GRAPHS = 1
+
+# Synthetic tensor kinds (one generator stream per tensor per layer).
+KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KIND_X = 1, 2, 3, 4, 5, 6, 7, 8
+
+# Every symbol include/uocr_moe.h declares.
+EXPORTS = [
+    "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
+    "uocr_moe_set_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
+    "uocr_expert_topk",
+    "uocr_expert_ffn_one", "uocr_expert_ffn_one_q8", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
+]
+
+
+class UocrError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class MoeDesc(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int64), ("routed_experts", ctypes.c_int64),
+                ("experts_per_token", ctypes.c_int64), ("expert_ffn", ctypes.c_int64),
+                ("shared_ffn", ctypes.c_int64), ("layers", ctypes.c_int64), ("max_rows", ctypes.c_int64),
+                ("weight_format", ctypes.c_int32), ("renormalize", ctypes.c_int32),
+                ("router_bias", ctypes.c_int32), ("device", ctypes.c_int32), ("flags", ctypes.c_int32)]
+
+
+class LayerSrc(ctypes.Structure):
+    _fields_ = [("memory", ctypes.c_int32), ("dtype", ctypes.c_int32), ("router", ctypes.c_void_p),
+                ("router_bias", ctypes.c_void_p), ("gate", ctypes.c_void_p), ("up", ctypes.c_void_p),
+                ("down", ctypes.c_void_p), ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p),
+                ("shared_down", ctypes.c_void_p)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built: run grpc-unlimited-ocr_b200/build.py (or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
+        L.uocr_last_error.restype = ctypes.c_char_p
+        L.uocr_moe_plan_create.argtypes = [ctypes.POINTER(MoeDesc), ctypes.POINTER(vp)]
+        L.uocr_moe_plan_destroy.argtypes = [vp]
+        L.uocr_moe_plan_bytes.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.uocr_moe_set_layer.argtypes = [vp, i64, ctypes.POINTER(LayerSrc), vp]
+        L.uocr_moe_forward.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp]
+        L.uocr_moe_forward_stack.argtypes = [vp, vp, i64, vp]
+        L.uocr_moe_check.argtypes = [vp, vp]
+        L.uocr_moe_profile_stack.argtypes = [vp, vp, i64, i32, ctypes.POINTER(f32), vp]
+        L.uocr_expert_topk.argtypes = [vp, i64, i64, i64, i32, vp, vp, vp]
+        L.uocr_expert_ffn_one.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
+        L.uocr_expert_ffn_one_q8.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp]
+        L.uocr_quantize_q8.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp]
+        L.uocr_synth_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64, f32, i64, i64, i32, vp, vp]
+        L.uocr_synth_stream.argtypes = [ctypes.c_uint64] * 3
+        L.uocr_synth_stream.restype = ctypes.c_uint64
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != UOCR_OK:
+        raise UocrError(rc, lib().uocr_last_error().decode())
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+@dataclass
+class Dims:
+    hidden: int
+    experts: int
+    top_k: int
+    ffn: int
+    shared_ffn: int
+    layers: int = 1
+
+
+class Plan:
+    """One MoE stack on one device (uocr_moe_plan)."""
+
+    def __init__(self, dims: Dims, max_rows: int, weight_format: int = WEIGHT_BF16, renormalize: bool = True,
+                 router_bias: bool = False, device: int = 0, flags: int = 0):
+        self.dims = dims
+        self.max_rows = max_rows
+        self.weight_format = weight_format
+        desc = MoeDesc(dims.hidden, dims.experts, dims.top_k, dims.ffn, dims.shared_ffn, dims.layers, max_rows,
+                       weight_format, int(renormalize), int(router_bias), device, flags)
+        h = ctypes.c_void_p()
+        _check(lib().uocr_moe_plan_create(ctypes.byref(desc), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uocr_moe_plan_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def bytes(self):
+        w, a = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib().uocr_moe_plan_bytes(self.h, ctypes.byref(w), ctypes.byref(a)))
+        return w.value, a.value
+
+    def set_layer(self, layer: int, router, gate, up, down, shared_gate=None, shared_up=None, shared_down=None,
+                  router_bias=None, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_F32, stream=None):
+        """Arguments are torch tensors (device memory) or raw addresses."""
+        src = LayerSrc(memory, dtype, _ptr(router), _ptr(router_bias), _ptr(gate), _ptr(up), _ptr(down),
+                       _ptr(shared_gate), _ptr(shared_up), _ptr(shared_down))
+        _check(lib().uocr_moe_set_layer(self.h, layer, ctypes.byref(src), _stream(stream)))
+
+    def forward(self, layer: int, x, y, ids=None, weights=None, stream=None, rows: int | None = None):
+        rows = x.shape[0] if rows is None else rows
+        _check(lib().uocr_moe_forward(self.h, layer, _ptr(x), rows, _ptr(y), _ptr(ids), _ptr(weights),
+                                      _stream(stream)))
+
+    def forward_stack(self, h, stream=None, rows: int | None = None):
+        rows = h.shape[0] if rows is None else rows
+        _check(lib().uocr_moe_forward_stack(self.h, _ptr(h), rows, _stream(stream)))
+
+    def profile_stack(self, h, iters: int, stream=None, rows: int | None = None):
+        """Mean device ms per launch of (router, gate/up, down) and per stack pass."""
+        rows = h.shape[0] if rows is None else rows
+        out = (ctypes.c_float * 4)()
+        _check(lib().uocr_moe_profile_stack(self.h, _ptr(h), rows, iters, out, _stream(stream)))
+        return {"router": out[0], "gate_up": out[1], "down": out[2], "stack": out[3]}
+
+    def check(self, stream=None):
+        _check(lib().uocr_moe_check(self.h, _stream(stream)))
+
+
+def expert_topk(logits, k: int, renormalize: bool, ids, weights, stream=None):
+    rows, experts = logits.shape
+    _check(lib().uocr_expert_topk(_ptr(logits), rows, experts, k, int(renormalize), _ptr(ids), _ptr(weights),
+                                  _stream(stream)))
+
+
+def expert_ffn_one(x, hidden, ffn, gate, up, down, ids, weights, k, out, stream=None):
+    _check(lib().uocr_expert_ffn_one(_ptr(x), hidden, ffn, _ptr(gate), _ptr(up), _ptr(down), _ptr(ids),
+                                     _ptr(weights), k, _ptr(out), _stream(stream)))
+
+
+def expert_ffn_one_q8(x, hidden, ffn, gate_q, gate_s, up_q, up_s, down_q, down_s, ids, weights, k, out,
+                      stream=None):
+    _check(lib().uocr_expert_ffn_one_q8(_ptr(x), hidden, ffn, _ptr(gate_q), _ptr(gate_s), _ptr(up_q), _ptr(up_s),
+                                        _ptr(down_q), _ptr(down_s), _ptr(ids), _ptr(weights), k, _ptr(out),
+                                        _stream(stream)))
+
+
+def quantize_q8(w, q, scales, group: int | None = None, stream=None):
+    rows, cols = w.shape
+    import torch
+    dtype = DTYPE_BF16 if w.dtype == torch.bfloat16 else DTYPE_F32
+    _check(lib().uocr_quantize_q8(_ptr(w), dtype, rows, cols, cols if group is None else group, _ptr(q),
+                                  _ptr(scales), _stream(stream)))
+
+
+def synth_stream(layer: int, kind: int, index: int) -> int:
+    return lib().uocr_synth_stream(layer, kind, index)
+
+
+def synth_fill(out, seed: int, layer: int, kind: int, index: int, sigma: float, offset: int = 0, stream=None):
+    """Fills a contiguous fp32 or bf16 device tensor from the synthetic stream."""
+    import torch
+    dtype = DTYPE_BF16 if out.dtype == torch.bfloat16 else DTYPE_F32
+    _check(lib().uocr_synth_fill(seed, synth_stream(layer, kind, index), sigma, offset, out.numel(), dtype,
+                                 _ptr(out), _stream(stream)))

@@ -1,0 +1,173 @@
+/* uocr_moe.h — C ABI of the B200 (sm_100a) decoder mixture-of-experts path.
+ *
+ * Drop-in for the MoE part of grpc-unlimited-ocr's CUDA backend: the router
+ * gate, softmax/top-k, the routed SwiGLU experts, the shared expert and the
+ * combine. Every entry point takes plain pointers, sizes and a cudaStream_t
+ * passed as void*, enqueues work on that stream and never synchronises it
+ * (uocr_moe_check is the one exception, and says so). Status codes replace the
+ * reference's exceptions (src/backend/cuda/context.cu:24-34, ops.cu:653-655);
+ * the message of the last failure on the calling thread is uocr_last_error().
+ *
+ * Layouts follow the reference (src/backend/cuda/ops.h:3-6): activations are
+ * fp32 row-major [rows, hidden]; expert matrices are stacked by expert —
+ * gate/up [E*F, H], down [E*H, F] (src/model/cuda/cuda_decoder.h:42-47);
+ * the shared expert is one gated MLP of width S: gate/up [S, H], down [H, S]
+ * (src/weights/architecture.cpp:117). The router is fp32 [E, H]
+ * (src/model/cuda/cuda_decoder.cpp:64-67).
+ */
+#ifndef UOCR_MOE_H
+#define UOCR_MOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UOCR_MOE_ABI_VERSION 1
+
+typedef enum uocr_status {
+  UOCR_OK = 0,
+  UOCR_ERR_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+  UOCR_ERR_UNSUPPORTED = 2,      /* a shape or mode this build does not implement */
+  UOCR_ERR_CUDA = 3,             /* reference: std::runtime_error from check() */
+  UOCR_ERR_OUT_OF_MEMORY = 4,
+  UOCR_ERR_DEVICE = 5,           /* a kernel recorded an error word (bad index, capacity) */
+  UOCR_ERR_TIMEOUT = 6,          /* a bounded device-side wait gave up */
+  UOCR_ERR_COMM = 7              /* expert-parallel exchange failure */
+} uocr_status;
+
+/* GRPC_UOCR_WEIGHT_FORMAT (src/service/config.cpp:54-56). INT8 here is
+ * symmetric per-output-channel (one fp32 scale per weight row). */
+typedef enum uocr_weight_format { UOCR_WEIGHT_BF16 = 0, UOCR_WEIGHT_INT8 = 1 } uocr_weight_format;
+typedef enum uocr_memory { UOCR_MEMORY_HOST = 0, UOCR_MEMORY_DEVICE = 1 } uocr_memory;
+typedef enum uocr_dtype { UOCR_DTYPE_F32 = 0, UOCR_DTYPE_BF16 = 1 } uocr_dtype;
+
+/* Message of the last failed call on this thread ("" when none). */
+const char* uocr_last_error(void);
+int uocr_abi_version(void);
+
+/* ---- Plan: one MoE stack with its weights and a preallocated arena -------
+ * Replaces the per-layer state of CudaDecoder (src/model/cuda/cuda_decoder.h:
+ * 25-104: moe_gate_f32, experts, shared) and DecoderDims' MoE fields
+ * (src/weights/architecture.h:26-30). All scratch is carved from an arena
+ * sized at creation for max_rows, so forward never allocates. */
+typedef struct uocr_moe_plan uocr_moe_plan;
+
+typedef struct uocr_moe_desc {
+  int64_t hidden;            /* H */
+  int64_t routed_experts;    /* E, at most 128 (ops.cu:653) */
+  int64_t experts_per_token; /* k */
+  int64_t expert_ffn;        /* F */
+  int64_t shared_ffn;        /* S = shared_experts * expert_ffn; 0 = no shared expert */
+  int64_t layers;
+  int64_t max_rows;          /* largest row count forward accepts */
+  int32_t weight_format;     /* uocr_weight_format */
+  int32_t renormalize;       /* 1: top-k weights divided by their sum; 0: raw softmax (feed_forward.cpp:40) */
+  int32_t router_bias;       /* 1: each layer carries an fp32 [E] bias added to the logits */
+  int32_t device;            /* CUDA device ordinal the plan lives on */
+  int32_t flags;             /* UOCR_PLAN_* bits */
+} uocr_moe_desc;
+
+/* forward_stack replays a CUDA graph it captured on the first call for the
+ * same (h, rows, stream-capturable) — one launch per step instead of three per
+ * layer. This flag turns the cache off. A stream that is already capturing,
+ * or the legacy default stream, always gets plain launches. */
+#define UOCR_PLAN_NO_GRAPHS 1
+
+int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** plan);
+int uocr_moe_plan_destroy(uocr_moe_plan* plan);
+/* Bytes of device memory the plan holds (weights + arena). */
+int uocr_moe_plan_bytes(const uocr_moe_plan* plan, int64_t* weight_bytes, int64_t* arena_bytes);
+
+/* One layer's weights as the reference's WeightSource hands them over (fp32,
+ * src/model/weight_source.h:16-21), or bf16. They are converted on the device
+ * to the plan's format: bf16, or int8 quantised per output channel
+ * (scale = rowmax|w| / 127, src/model/cuda/device_weight.cpp:11-26 with one
+ * group per row). Replaces stacked_weight / device_weight
+ * (src/model/cuda/device_weight.cpp:57-72). Synchronises nothing, but host
+ * sources are copied before the call returns. */
+typedef struct uocr_moe_layer_src {
+  int32_t memory;            /* uocr_memory of every pointer below */
+  int32_t dtype;             /* uocr_dtype of gate/up/down/shared_* (router and bias are always fp32) */
+  const float* router;       /* [E, H] */
+  const float* router_bias;  /* [E], required iff desc.router_bias */
+  const void* gate;          /* [E*F, H] */
+  const void* up;            /* [E*F, H] */
+  const void* down;          /* [E*H, F] */
+  const void* shared_gate;   /* [S, H] (ignored when S == 0) */
+  const void* shared_up;     /* [S, H] */
+  const void* shared_down;   /* [H, S] */
+} uocr_moe_layer_src;
+
+int uocr_moe_set_layer(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_src* src, void* stream);
+
+/* y [rows, H] = MoE_layer(x [rows, H]) — the work of CudaDecoder::moe
+ * (src/model/cuda/cuda_decoder.cpp:137-192) and MixtureOfExperts::forward
+ * (src/model/feed_forward.cpp:36-78): fp32 router, softmax, top-k (lower id on
+ * a tie), optional renormalisation, routed SwiGLU experts on bf16-rounded
+ * inputs, shared expert, and the combine in expert-id order. ids [rows, k]
+ * (int32, rank order) and weights [rows, k] are optional outputs (NULL to
+ * skip). x, y, ids and weights are device pointers; x and y must not overlap. */
+int uocr_moe_forward(uocr_moe_plan* plan, int64_t layer, const float* x, int64_t rows, float* y, int32_t* ids,
+                     float* weights, void* stream);
+
+/* h <- h + MoE_l(h) for l = 0 .. layers-1, in place on device memory h
+ * [rows, H]: the decoder's residual around its feed-forward block
+ * (src/model/decoder.cpp:181,201) with nothing between the layers. */
+int uocr_moe_forward_stack(uocr_moe_plan* plan, float* h, int64_t rows, void* stream);
+
+/* Synchronises `stream`, then reports and clears any error word a kernel of
+ * this plan recorded (bounded waits that gave up, bad indices). */
+int uocr_moe_check(uocr_moe_plan* plan, void* stream);
+
+/* Instrumented forward_stack for measurement: runs `iters` stack passes with
+ * CUDA events between the kernels, synchronises, and writes the mean device
+ * time per launch of each kernel in ms_per_kernel[0..2] (router, gate/up,
+ * down+combine) and the mean time of one whole stack pass in ms_per_kernel[3].
+ * No reference counterpart (the reference has no device timing). */
+int uocr_moe_profile_stack(uocr_moe_plan* plan, float* h, int64_t rows, int32_t iters, float* ms_per_kernel,
+                           void* stream);
+
+/* ---- Op-level mirrors of the reference's uocr::cuda MoE ops -------------- */
+
+/* src/backend/cuda/ops.h:80-81 expert_topk: softmax over each row of
+ * logits [rows, experts <= 128], then the top k (lower index on a tie) as
+ * int64 ids and their scores; renormalize = 1 divides the k scores by their
+ * sum (the reference never does). Device pointers. */
+int uocr_expert_topk(const float* logits, int64_t rows, int64_t experts, int64_t k, int32_t renormalize,
+                     int64_t* ids, float* weights, void* stream);
+
+/* src/backend/cuda/ops.h:87-89 expert_ffn_one: one decode row through its
+ * k routed experts, bf16 stacks gate/up [E*F, H], down [E*H, F]:
+ *   out[c] = sum_j weights[j] * down[ids[j]] (silu(gate[ids[j]] x) * up[ids[j]] x)
+ * with x and the hidden activation rounded to bf16. Like the reference it
+ * takes its [k, F] activation scratch from cudaMallocAsync on the stream. */
+int uocr_expert_ffn_one(const float* x, int64_t hidden, int64_t ffn, const uint16_t* gate, const uint16_t* up,
+                        const uint16_t* down, const int64_t* ids, const float* weights, int64_t k, float* out,
+                        void* stream);
+
+/* src/backend/cuda/gemv_ops.h:33-35 expert_ffn_one_q8 with per-output-channel
+ * int8 stacks: q [rows, cols] int8 and one fp32 scale per row. */
+int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const int8_t* gate_q, const float* gate_s,
+                           const int8_t* up_q, const float* up_s, const int8_t* down_q, const float* down_s,
+                           const int64_t* ids, const float* weights, int64_t k, float* out, void* stream);
+
+/* src/model/cuda/device_weight.cpp:11-26 quantize_q8_rows on the device, with
+ * the group free (group = cols is per output channel). w is fp32 or bf16
+ * (dtype); q [rows, cols], scales [rows, cols/group]. Device pointers. */
+int uocr_quantize_q8(const void* w, int32_t dtype, int64_t rows, int64_t cols, int64_t group, int8_t* q,
+                     float* scales, void* stream);
+
+/* Synthetic inputs (not part of the hot path): fills out[0..n) with the
+ * counter-based N(0, sigma^2)-shaped stream `stream_id` of `seed`, starting
+ * at element `offset`, as fp32 or as bf16 (round to nearest even). The same
+ * values come out of the host generator the tests use. */
+int uocr_synth_fill(uint64_t seed, uint64_t stream_id, float sigma, int64_t offset, int64_t n, int32_t dtype,
+                    void* out, void* stream);
+uint64_t uocr_synth_stream(uint64_t layer, uint64_t kind, uint64_t index);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* UOCR_MOE_H */

@@ -1,0 +1,69 @@
+"""The C ABI without a GPU: the library loads, exports every entry point the
+header declares, and rejects bad arguments with the documented status codes
+before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import uocr_moe as M
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "uocr_moe.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\**\s+\**(uocr_[a-z_0-9]+)\s*\(", text, re.M)))
+
+
+def test_header_and_binding_agree():
+    assert declared_symbols() == sorted(M.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = M.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.uocr_abi_version() == 1
+
+
+def _desc(**kw):
+    d = dict(hidden=64, routed_experts=8, experts_per_token=2, expert_ffn=32, shared_ffn=32, layers=1, max_rows=4,
+             weight_format=0, renormalize=1, router_bias=0, device=0, flags=0)
+    d.update(kw)
+    return M.MoeDesc(**d)
+
+
+@pytest.mark.parametrize("bad", [dict(hidden=0), dict(hidden=40), dict(routed_experts=129), dict(routed_experts=0),
+                                 dict(experts_per_token=9), dict(experts_per_token=9, routed_experts=8),
+                                 dict(expert_ffn=24), dict(shared_ffn=-16), dict(layers=0), dict(max_rows=0),
+                                 dict(weight_format=2)])
+def test_plan_create_rejects_bad_shapes(bad):
+    h = ctypes.c_void_p()
+    rc = M.lib().uocr_moe_plan_create(ctypes.byref(_desc(**bad)), ctypes.byref(h))
+    assert rc == 1 and not h.value
+    assert M.lib().uocr_last_error().decode().startswith("plan_create")
+
+
+def test_null_arguments_are_rejected():
+    lib = M.lib()
+    assert lib.uocr_moe_plan_create(None, None) == 1
+    assert lib.uocr_moe_forward(None, 0, None, 1, None, None, None, None) == 1
+    assert lib.uocr_moe_set_layer(None, 0, None, None) == 1
+    assert lib.uocr_moe_plan_destroy(None) == 0
+
+
+def test_op_mirror_argument_checks():
+    lib = M.lib()
+    # the reference throws invalid_argument above 128 experts (ops.cu:653)
+    assert lib.uocr_expert_topk(None, 1, 129, 2, 1, None, None, None) == 1
+    assert "128" in lib.uocr_last_error().decode()
+    assert lib.uocr_expert_topk(None, 1, 8, 9, 1, None, None, None) == 1
+    assert lib.uocr_quantize_q8(None, 0, 4, 96, 40, None, None, None) == 1
+    assert lib.uocr_expert_ffn_one(None, 40, 32, None, None, None, None, None, 2, None, None) == 1
+    assert lib.uocr_synth_fill(1, 2, 1.0, 0, -1, 0, None, None) == 1
+
+
+def test_synth_stream_layout():
+    assert M.synth_stream(3, M.KIND_DOWN, 17) == (3 << 40) | (M.KIND_DOWN << 32) | 17

@@ -1,0 +1,270 @@
+"""Decode path (rows <= 16) on the GPU, through the C ABI, against the oracle.
+
+Bars: expert ids and their order bit-exact except rows
+whose k-th vs (k+1)-th router-logit margin is below 1e-3 (counted); layer
+output max_rel (max|got-want| / max|want|) <= 2e-2 for bf16, <= 5e-2 for int8.
+"""
+import numpy as np
+import pytest
+
+import moe_configs as C
+import oracle as O
+import uocr_moe as M
+from conftest import max_rel
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+INT8_TOL = 5e-2
+MARGIN = 1e-3
+
+
+def to_np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def host_weights(t: dict) -> O.MoeWeights:
+    H = t["router"].shape[1]
+    z = lambda *s: np.zeros(s, np.float32)  # noqa: E731
+    return O.MoeWeights(
+        router=to_np(t["router"]), gate=to_np(t["gate"]), up=to_np(t["up"]), down=to_np(t["down"]),
+        shared_gate=to_np(t["shared_gate"]) if "shared_gate" in t else z(0, H),
+        shared_up=to_np(t["shared_up"]) if "shared_up" in t else z(0, H),
+        shared_down=to_np(t["shared_down"]) if "shared_down" in t else z(H, 0),
+        router_bias=to_np(t["router_bias"]) if "router_bias" in t else None)
+
+
+def check_ids(got_ids, want: O.MoeResult):
+    """ids and order exact except near-tie rows; returns the number of exempt rows."""
+    exempt = 0
+    for t in range(got_ids.shape[0]):
+        if np.array_equal(got_ids[t], want.ids[t]):
+            continue
+        assert want.margin[t] < MARGIN or want.order_margin[t] < MARGIN, (
+            f"row {t}: ids {got_ids[t]} != {want.ids[t]} with margin {want.margin[t]}")
+        exempt += 1
+    return exempt
+
+
+def run_plan(plan, layer, x, k, torch):
+    T = x.shape[0]
+    y = torch.empty_like(x)
+    ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=x.device)
+    plan.forward(layer, x, y, ids, w)
+    plan.check()
+    return to_np(y), ids.cpu().numpy(), w.cpu().numpy()
+
+
+def test_device_generator_matches_host(cuda):
+    import torch
+    for dt, sigma in ((torch.float32, 0.02), (torch.bfloat16, 1.0)):
+        t = torch.empty(300001, dtype=dt, device=cuda)
+        M.synth_fill(t, 5, 3, M.KIND_UP, 9, sigma, offset=77)
+        want = O.synth(5, 3, M.KIND_UP, 9, 300001, sigma, offset=77)
+        if dt == torch.bfloat16:
+            want = O.round_bf16(want)
+        assert np.array_equal(to_np(t).view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("group", [None, 32])
+def test_device_quantiser_matches_oracle(cuda, group):
+    import torch
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((67, 256)) * 0.05).astype(np.float32)
+    w[5] = 0
+    q = torch.empty(67, 256, dtype=torch.int8, device=cuda)
+    s = torch.empty(67, 256 // (group or 256), dtype=torch.float32, device=cuda)
+    M.quantize_q8(torch.from_numpy(w).to(cuda), q, s, group=group)
+    torch.cuda.synchronize()
+    wq, ws = O.quantize_q8(w, group=group)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ws.view(np.uint32))
+
+
+def _tiny_layer(rng, H, E, F, S, bf16=True):
+    f = lambda *s: (rng.standard_normal(s) * 0.05).astype(np.float32)  # noqa: E731
+    w = O.MoeWeights(f(E, H), f(E * F, H), f(E * F, H), f(E * H, F), f(S, H), f(S, H), f(H, S))
+    if bf16:
+        for name in ("router", "gate", "up", "down", "shared_gate", "shared_up", "shared_down"):
+            setattr(w, name, O.round_bf16(getattr(w, name)).reshape(getattr(w, name).shape))
+    return w
+
+
+def _upload(plan, w: O.MoeWeights, torch, cuda, layer=0):
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    keep = {k: d(getattr(w, k)) for k in ("router", "gate", "up", "down", "shared_gate", "shared_up", "shared_down")}
+    if w.router_bias is not None:
+        keep["router_bias"] = d(w.router_bias)
+    plan.set_layer(layer, keep["router"], keep["gate"], keep["up"], keep["down"], keep["shared_gate"],
+                   keep["shared_up"], keep["shared_down"], router_bias=keep.get("router_bias"))
+    return keep
+
+
+@pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt", [
+    (1, 64, 8, 3, 32, 32, True, 0), (5, 128, 16, 1, 48, 0, True, 0), (16, 256, 128, 8, 64, 64, True, 0),
+    (3, 96, 12, 4, 32, 48, False, 0), (16, 64, 2, 2, 16, 16, True, 0), (7, 128, 32, 6, 64, 128, True, 1),
+    (16, 512, 64, 6, 256, 512, True, 1)])
+def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt):
+    import torch
+    rng = np.random.default_rng(T * 7919 + E)
+    w = _tiny_layer(rng, H, E, F, S)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=16, weight_format=fmt, renormalize=renorm)
+    _upload(plan, w, torch, cuda)
+    y, ids, wts = run_plan(plan, 0, torch.from_numpy(x).to(cuda), K, torch)
+    ww = w
+    if fmt == M.WEIGHT_INT8:
+        ww = O.MoeWeights(w.router, *[O.dequantize_q8(*O.quantize_q8(getattr(w, n))) for n in
+                                      ("gate", "up", "down", "shared_gate", "shared_up")],
+                          O.dequantize_q8(*O.quantize_q8(w.shared_down)) if S else w.shared_down)
+    want = O.moe_forward(ww, x, K, renormalize=renorm)
+    check_ids(ids, want)
+    assert max_rel(y, want.y) <= (INT8_TOL if fmt else BF16_TOL)
+    np.testing.assert_allclose(wts, want.weights, rtol=1e-5, atol=1e-7)
+
+
+def test_tied_router_rows_pick_lower_id(cuda):
+    import torch
+    rng = np.random.default_rng(2)
+    w = _tiny_layer(rng, 64, 8, 32, 32)
+    w.router[6] = w.router[2]
+    w.router[4] = w.router[2]
+    x = rng.standard_normal((9, 64)).astype(np.float32)
+    plan = M.Plan(M.Dims(64, 8, 3, 32, 32), max_rows=16)
+    _upload(plan, w, torch, cuda)
+    _, ids, _ = run_plan(plan, 0, torch.from_numpy(x).to(cuda), 3, torch)
+    want = O.moe_forward(w, x, 3, renormalize=True)
+    assert np.array_equal(ids, want.ids)  # exact ties are not near-ties: no exemption
+
+
+def test_router_bias(cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    w = _tiny_layer(rng, 128, 16, 32, 32)
+    w.router_bias = np.array(C.zipf_bias(16, 1.2), np.float32)
+    x = rng.standard_normal((12, 128)).astype(np.float32)
+    plan = M.Plan(M.Dims(128, 16, 4, 32, 32), max_rows=16, router_bias=True)
+    _upload(plan, w, torch, cuda)
+    y, ids, _ = run_plan(plan, 0, torch.from_numpy(x).to(cuda), 4, torch)
+    want = O.moe_forward(w, x, 4, renormalize=True)
+    check_ids(ids, want)
+    assert max_rel(y, want.y) <= BF16_TOL
+
+
+@pytest.fixture(scope="module")
+def c1_layer(cuda):
+    cfg = C.CONFIGS[1]
+    t = C.device_layer(cfg, 0)
+    return cfg, t, host_weights(t)
+
+
+@pytest.mark.parametrize("T", [1, 4, 8, 16])
+def test_config1_layer_bf16(cuda, c1_layer, T):
+    import torch
+    cfg, t, hw = c1_layer
+    plan = M.Plan(cfg.dims(layers=1), max_rows=16, renormalize=True)
+    C.load_layer(plan, cfg, 0, t)
+    x = C.device_input(cfg, T)
+    y, ids, _ = run_plan(plan, 0, x, cfg.top_k, torch)
+    want = O.moe_forward(hw, to_np(x), cfg.top_k, renormalize=True)
+    exempt = check_ids(ids, want)
+    err = max_rel(y, want.y)
+    print(f"config1 T={T}: max_rel {err:.2e}, exempt rows {exempt}")
+    assert err <= BF16_TOL
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_config2_layer_int8(cuda, c1_layer, T):
+    import torch
+    cfg = C.CONFIGS[2]
+    t = C.device_layer(cfg, 0)
+    hw = host_weights(t)
+    plan = M.Plan(cfg.dims(layers=1), max_rows=16, weight_format=M.WEIGHT_INT8, renormalize=True)
+    C.load_layer(plan, cfg, 0, t)
+    x = C.device_input(cfg, T)
+    y, ids, _ = run_plan(plan, 0, x, cfg.top_k, torch)
+    deq = lambda a: O.dequantize_q8(*O.quantize_q8(a))  # noqa: E731
+    hq = O.MoeWeights(hw.router, deq(hw.gate), deq(hw.up), deq(hw.down), deq(hw.shared_gate), deq(hw.shared_up),
+                      deq(hw.shared_down))
+    want = O.moe_forward(hq, to_np(x), cfg.top_k, renormalize=True)
+    exempt = check_ids(ids, want)
+    err = max_rel(y, want.y)
+    print(f"config2 T={T}: max_rel {err:.2e}, exempt rows {exempt}")
+    assert err <= INT8_TOL
+
+
+def test_stack_residual_two_layers(cuda):
+    import torch
+    cfg = C.CONFIGS[1]
+    layers = [C.device_layer(cfg, l) for l in range(2)]
+    plan = M.Plan(cfg.dims(layers=2), max_rows=8)
+    for l, t in enumerate(layers):
+        C.load_layer(plan, cfg, l, t)
+    x = C.device_input(cfg, 4)
+    h = x.clone()
+    plan.forward_stack(h)
+    plan.check()
+    want = to_np(x)
+    for t in layers:
+        want = want + O.moe_forward(host_weights(t), want, cfg.top_k, renormalize=True).y
+    assert max_rel(to_np(h), want) <= BF16_TOL
+
+
+def test_forward_is_deterministic(cuda, c1_layer):
+    import torch
+    cfg, t, _ = c1_layer
+    plan = M.Plan(cfg.dims(layers=1), max_rows=8)
+    C.load_layer(plan, cfg, 0, t)
+    x = C.device_input(cfg, 8)
+    a, _, _ = run_plan(plan, 0, x, cfg.top_k, torch)
+    b, _, _ = run_plan(plan, 0, x, cfg.top_k, torch)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_op_mirrors(cuda, c1_layer):
+    """uocr_expert_topk / uocr_expert_ffn_one(_q8), the reference's op shapes."""
+    import torch
+    cfg, t, hw = c1_layer
+    H, F, K = cfg.hidden, cfg.ffn, cfg.top_k
+    x = C.device_input(cfg, 1)
+    logits = (x @ t["router"].T).contiguous()
+    ids = torch.empty(1, K, dtype=torch.int64, device=cuda)
+    wts = torch.empty(1, K, dtype=torch.float32, device=cuda)
+    M.expert_topk(logits, K, False, ids, wts)
+    out = torch.empty(H, dtype=torch.float32, device=cuda)
+    M.expert_ffn_one(x, H, F, t["gate"], t["up"], t["down"], ids, wts, K, out)
+    torch.cuda.synchronize()
+    xh = O.round_bf16(to_np(x)[0]).astype(np.float64)
+    want = np.zeros(H)
+    for j, e in enumerate(ids.cpu().numpy()[0]):
+        g = hw.gate[e * F:(e + 1) * F].astype(np.float64) @ xh
+        u = hw.up[e * F:(e + 1) * F].astype(np.float64) @ xh
+        a = O.round_bf16((g / (1 + np.exp(-g)) * u).astype(np.float32)).astype(np.float64)
+        want += wts.cpu().numpy()[0, j] * (hw.down[e * H:(e + 1) * H].astype(np.float64) @ a)
+    assert max_rel(to_np(out), want) <= BF16_TOL
+    sc = torch.softmax(logits.double(), dim=1)
+    top = torch.topk(sc, K, dim=1)
+    assert torch.equal(top.indices, ids)
+    # int8 stacks, per output channel
+    q = {n: torch.empty_like(t[n], dtype=torch.int8) for n in ("gate", "up", "down")}
+    s = {n: torch.empty(t[n].shape[0], 1, dtype=torch.float32, device=cuda) for n in q}
+    for n in q:
+        M.quantize_q8(t[n], q[n], s[n])
+    out8 = torch.empty(H, dtype=torch.float32, device=cuda)
+    M.expert_ffn_one_q8(x, H, F, q["gate"], s["gate"], q["up"], s["up"], q["down"], s["down"], ids, wts, K, out8)
+    torch.cuda.synchronize()
+    assert max_rel(to_np(out8), want) <= INT8_TOL
+
+
+def test_forward_errors(cuda):
+    import torch
+    plan = M.Plan(M.Dims(64, 8, 2, 32, 32), max_rows=32)
+    x = torch.zeros(4, 64, device=cuda)
+    y = torch.zeros(4, 64, device=cuda)
+    with pytest.raises(M.UocrError) as e:
+        plan.forward(0, x, y)  # weights never set
+    assert e.value.code == 1
+    with pytest.raises(M.UocrError) as e:
+        plan.forward(0, x, x)
+    assert e.value.code == 1
