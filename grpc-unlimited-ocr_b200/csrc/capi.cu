@@ -226,12 +226,21 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   int smem_optin = 0;
   UOCR_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device),
            "plan_create: shared memory limit");
-  // The decode kernels stage the batch's rows in shared memory.
+  // The decode kernels stage the batch's rows in shared memory (the router
+  // also holds ~5 KB of static shared memory of its own).
   int dr = static_cast<int>(d.max_rows < kDecodeMaxRows ? d.max_rows : kDecodeMaxRows);
-  while (dr > 0 && (static_cast<size_t>(d.hidden) + static_cast<size_t>(dr) * (d.hidden + 8)) * 4 >
+  while (dr > 0 && (static_cast<size_t>(d.hidden) + static_cast<size_t>(dr) * (d.hidden + 8)) * 4 + 8192 >
                        static_cast<size_t>(smem_optin))
     --dr;
   p->decode_rows = dr;
+  if (dr > 0) {
+    cudaError_t pst = prepare_router_decode();
+    if (pst == cudaSuccess) pst = prepare_decode_experts(dr, static_cast<int>(d.hidden));
+    if (pst != cudaSuccess) {
+      delete p;
+      return cuda_fail(pst, "plan_create: kernel set-up");
+    }
+  }
 
   Carver probe{nullptr};
   LayerDev tmp;

@@ -15,6 +15,10 @@
 // The combine and the shared add happen in the down kernel, in the order the
 // reference adds them (src/model/feed_forward.cpp:65-76), so nothing is
 // accumulated with atomics and the result is the same on every run.
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "moe_kernels.h"
 
 namespace uocr_b200 {
@@ -290,26 +294,38 @@ __global__ void __launch_bounds__(128) down_decode_kernel(int T, int H, int F, i
   }
 }
 
+// Resident gate/up blocks per SM for a shared-memory size, computed once per
+// (device, size) — never inside a stream capture once the plan prepared it.
+template <typename Rows>
+int gate_up_blocks_per_sm(size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, size_t>, int> cache;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return -1;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto it = cache.find({dev, smem});
+  if (it != cache.end()) return it->second;
+  if (!attr_set[dev]) {
+    if (allow_max_dynamic_smem(gate_up_decode_kernel<Rows>) != cudaSuccess) return -1;
+    attr_set[dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gate_up_decode_kernel<Rows>, 256, smem) != cudaSuccess)
+    return -1;
+  per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
+  cache[{dev, smem}] = per_sm;
+  return per_sm;
+}
+
 template <typename Rows>
 cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, Rows gate, Rows up, Rows down,
                                     Rows sgate, Rows sup, Rows sdown, const DecodeRoute* route,
                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                     ErrorWord* err, int sm_count, cudaStream_t stream, cudaEvent_t between) {
   const size_t smem = static_cast<size_t>(T) * H * sizeof(float);
-  // Occupancy for this row count, computed once per device and row count.
-  static int per_sm_cache[kMaxDevices][kDecodeMaxRows + 1] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int per_sm = dev < kMaxDevices ? per_sm_cache[dev][T] : 0;
-  if (per_sm == 0) {
-    cudaError_t st = cudaFuncSetAttribute(gate_up_decode_kernel<Rows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kMaxDynamicSmem);
-    if (st != cudaSuccess) return st;
-    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gate_up_decode_kernel<Rows>, 256, smem);
-    if (st != cudaSuccess) return st;
-    per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
-    if (dev < kMaxDevices) per_sm_cache[dev][T] = per_sm;
-  }
+  const int per_sm = gate_up_blocks_per_sm<Rows>(smem);
+  if (per_sm < 0) return cudaErrorInvalidConfiguration;
   cudaError_t st;
   gate_up_decode_kernel<Rows><<<sm_count * per_sm, 256, smem, stream>>>(x, T, H, F, S, gate, up, sgate, sup, route,
                                                                        act, act_s, err);
@@ -342,6 +358,15 @@ cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S,
                                      ErrorWord* err, int sm_count, cudaStream_t stream, cudaEvent_t between) {
   return launch_decode_experts_t<Q8Rows>(x, T, H, F, S, gate, up, down, sgate, sup, sdown, route, act, act_s, resid,
                                          y, err, sm_count, stream, between);
+}
+
+cudaError_t prepare_decode_experts(int max_rows, int H) {
+  for (int T = 1; T <= max_rows; ++T) {
+    const size_t smem = static_cast<size_t>(T) * H * sizeof(float);
+    if (gate_up_blocks_per_sm<Bf16Rows>(smem) < 0 || gate_up_blocks_per_sm<Q8Rows>(smem) < 0)
+      return cudaErrorInvalidConfiguration;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace uocr_b200

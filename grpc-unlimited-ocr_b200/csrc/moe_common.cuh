@@ -15,7 +15,6 @@ constexpr int kMaxTopK = 8;
 constexpr int kDecodeMaxRows = 16;   // rows at or below this take the weight-streaming decode path
 constexpr int kMaxActive = kDecodeMaxRows * kMaxTopK;  // distinct experts one decode batch can touch
 constexpr int kMaxDevices = 64;
-constexpr int kMaxDynamicSmem = 227 * 1024;  // sm_100 opt-in limit per block
 
 // A kernel that meets a bad index, a capacity overflow or a wait that ran out
 // records it here instead of touching memory it should not; the host reads
@@ -65,6 +64,21 @@ struct Q8Rows {
   const float* scale;
   int64_t cols;
 };
+
+// Opts a kernel into the largest dynamic shared memory the current device
+// allows next to the kernel's own static shared memory.
+template <typename Kernel>
+inline cudaError_t allow_max_dynamic_smem(Kernel kernel) {
+  int dev = 0, optin = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st == cudaSuccess) st = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes attr{};
+  if (st == cudaSuccess) st = cudaFuncGetAttributes(&attr, kernel);
+  if (st == cudaSuccess)
+    st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              optin - static_cast<int>(attr.sharedSizeBytes));
+  return st;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -6,6 +6,11 @@
 
 namespace uocr_b200 {
 
+// One-time per-device set-up (shared-memory opt-in, occupancy) so that later
+// launches, including those inside a stream capture, only launch.
+cudaError_t prepare_router_decode();
+cudaError_t prepare_decode_experts(int max_rows, int hidden);
+
 // ---- router (router.cu) ----
 cudaError_t launch_router_decode(const float* x, int T, int H, const float* router, const float* bias, int E, int K,
                                  int renorm, float* logits, int* ids, float* weights, DecodeRoute* route,

@@ -233,20 +233,26 @@ __global__ void route_from_ids_kernel(const int64_t* ids, const float* weights, 
 
 }  // namespace
 
+cudaError_t prepare_router_decode() {
+  static bool raised[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if (dev < kMaxDevices && !raised[dev]) {
+    st = allow_max_dynamic_smem(router_decode_kernel);
+    if (st != cudaSuccess) return st;
+    raised[dev] = true;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_router_decode(const float* x, int T, int H, const float* router, const float* bias, int E, int K,
                                  int renorm, float* logits, int* ids, float* weights, DecodeRoute* route,
                                  unsigned* counter, ErrorWord* err, cudaStream_t stream) {
   const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
   if (smem > 48 * 1024) {
-    static bool raised[kMaxDevices] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < kMaxDevices && !raised[dev]) {
-      cudaError_t st = cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kMaxDynamicSmem);
-      if (st != cudaSuccess) return st;
-      raised[dev] = true;
-    }
+    const cudaError_t st = prepare_router_decode();
+    if (st != cudaSuccess) return st;
   }
   router_decode_kernel<<<E, 256, smem, stream>>>(x, T, H, router, bias, E, K, renorm, logits, ids, weights, route,
                                                  counter, err);
