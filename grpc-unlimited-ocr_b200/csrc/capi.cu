@@ -89,6 +89,8 @@ class DeviceGuard {
 
 }  // namespace
 
+int uocr_b200::set_last_error(int code, const std::string& what) { return fail(code, what); }
+
 struct uocr_moe_plan {
   uocr_moe_desc d{};
   int sm_count = 0;

@@ -2,9 +2,14 @@
 // allocation, no synchronisation). Each returns the launch status.
 #pragma once
 
+#include <string>
+
 #include "moe_common.cuh"
 
 namespace uocr_b200 {
+
+// Records `what` as uocr_last_error() for this thread and returns `code`.
+int set_last_error(int code, const std::string& what);
 
 // One-time per-device set-up (shared-memory opt-in, occupancy) so that later
 // launches, including those inside a stream capture, only launch.

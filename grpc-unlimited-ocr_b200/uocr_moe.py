@@ -30,7 +30,7 @@ EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
     "uocr_moe_set_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_expert_topk",
-    "uocr_expert_ffn_one", "uocr_expert_ffn_one_q8", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
+    "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
 ]
 
 
@@ -76,7 +76,8 @@ def lib() -> ctypes.CDLL:
         L.uocr_moe_profile_stack.argtypes = [vp, vp, i64, i32, ctypes.POINTER(f32), vp]
         L.uocr_expert_topk.argtypes = [vp, i64, i64, i64, i32, vp, vp, vp]
         L.uocr_expert_ffn_one.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
-        L.uocr_expert_ffn_one_q8.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp]
+        L.uocr_expert_ffn_one_noalloc.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
+        L.uocr_expert_ffn_one_q8.argtypes =[vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp]
         L.uocr_quantize_q8.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp]
         L.uocr_synth_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64, f32, i64, i64, i32, vp, vp]
         L.uocr_synth_stream.argtypes = [ctypes.c_uint64] * 3
@@ -181,6 +182,14 @@ def expert_topk(logits, k: int, renormalize: bool, ids, weights, stream=None):
 def expert_ffn_one(x, hidden, ffn, gate, up, down, ids, weights, k, out, stream=None):
     _check(lib().uocr_expert_ffn_one(_ptr(x), hidden, ffn, _ptr(gate), _ptr(up), _ptr(down), _ptr(ids),
                                      _ptr(weights), k, _ptr(out), _stream(stream)))
+
+
+def expert_ffn_one_noalloc(x, hidden, ffn, gate, up, down, ids, weights, k, out, stream=None):
+    """expert_ffn_one for callers that cannot allocate device memory: its
+    scratch is a static device array shared by every call (k <= 8,
+    ffn <= 8192); calls that overlap on the GPU race."""
+    _check(lib().uocr_expert_ffn_one_noalloc(_ptr(x), hidden, ffn, _ptr(gate), _ptr(up), _ptr(down), _ptr(ids),
+                                             _ptr(weights), k, _ptr(out), _stream(stream)))
 
 
 def expert_ffn_one_q8(x, hidden, ffn, gate_q, gate_s, up_q, up_s, down_q, down_s, ids, weights, k, out,

@@ -147,6 +147,20 @@ int uocr_expert_ffn_one(const float* x, int64_t hidden, int64_t ffn, const uint1
                         const uint16_t* down, const int64_t* ids, const float* weights, int64_t k, float* out,
                         void* stream);
 
+/* uocr_expert_ffn_one without any device allocation. No counterpart in the
+ * reference. For callers that cannot allocate device memory on the call path:
+ * a serving loop whose memory another allocator reserved up front, a decode
+ * step that must not pay cudaMalloc's synchronisation or a pool's bookkeeping,
+ * a runtime that forbids allocations after start-up. Same arguments and
+ * result as uocr_expert_ffn_one; its scratch is one static device array of
+ * about 146 KiB that every GPU loading this library holds until exit, so
+ * k <= 8 and ffn <= 8192 (larger is UOCR_ERR_INVALID_ARGUMENT). The first call
+ * on a device looks the array's address up; make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race. */
+int uocr_expert_ffn_one_noalloc(const float* x, int64_t hidden, int64_t ffn, const uint16_t* gate,
+                                const uint16_t* up, const uint16_t* down, const int64_t* ids, const float* weights,
+                                int64_t k, float* out, void* stream);
+
 /* src/backend/cuda/gemv_ops.h:33-35 expert_ffn_one_q8 with per-output-channel
  * int8 stacks: q [rows, cols] int8 and one fp32 scale per row. */
 int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const int8_t* gate_q, const float* gate_s,
