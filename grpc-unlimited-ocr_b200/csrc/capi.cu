@@ -382,23 +382,25 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
             S = static_cast<int>(d.shared_ffn);
   if (rows > p->decode_rows)
     return fail(UOCR_ERR_UNSUPPORTED, "forward: rows above the decode limit need the prefill path, not built yet");
-  UOCR_TRY(launch_router_decode(x, T, H, L.router, L.bias, E, K, d.renormalize, p->logits, p->ids, p->weights,
-                                p->route, p->counter, p->err, stream),
-           "forward: router");
+  // Programmatic dependent launch chains router -> gate/up -> down (and the
+  // next layer's router); the profiling path records events between them instead.
+  const bool pdl = ev == nullptr;
+  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl), "forward: router");
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
+  const DecodeRouting routing{p->logits, nullptr, E, K, d.renormalize, p->ids, p->weights};
   if (d.weight_format == UOCR_WEIGHT_BF16) {
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
-                                        b(L.sdown), p->route, p->act, p->act_s, resid, y, p->err, p->sm_count,
-                                        stream, between),
+                                        b(L.sdown), routing, p->act, p->act_s, resid, y, p->err, p->sm_count,
+                                        stream, between, pdl),
              "forward: experts");
   } else {
     auto q = [](void* v, float* s, int64_t cols) { return Q8Rows{static_cast<const int8_t*>(v), s, cols}; };
     UOCR_TRY(launch_decode_experts_q8(x, T, H, F, S, q(L.gate, L.gate_s, H), q(L.up, L.up_s, H),
                                       q(L.down, L.down_s, F), q(L.sgate, L.sgate_s, H), q(L.sup, L.sup_s, H),
-                                      q(L.sdown, L.sdown_s, S), p->route, p->act, p->act_s, resid, y, p->err,
-                                      p->sm_count, stream, between),
+                                      q(L.sdown, L.sdown_s, S), routing, p->act, p->act_s, resid, y, p->err,
+                                      p->sm_count, stream, between, pdl),
              "forward: experts");
   }
   return UOCR_OK;
@@ -569,8 +571,10 @@ int uocr_expert_ffn_one(const float* x, int64_t hidden, int64_t ffn, const uint1
   // caller's contract, as in the reference (ops.h:82-89).
   return ffn_one(x, hidden, ffn, ids, weights, k, out, kMaxExperts, stream,
                  [&](DecodeRoute* route, __nv_bfloat16* act, ErrorWord* err) {
+                   const DecodeRouting routing{nullptr, route, kMaxExperts, static_cast<int>(k), 0, nullptr,
+                                               nullptr};
                    return launch_decode_experts_bf16(x, 1, static_cast<int>(hidden), static_cast<int>(ffn), 0,
-                                                     b(gate), b(up), b(down), nullptr, nullptr, nullptr, route, act,
+                                                     b(gate), b(up), b(down), nullptr, nullptr, nullptr, routing, act,
                                                      nullptr, nullptr, out, err, sms, stream);
                  });
 }
@@ -587,9 +591,11 @@ int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const in
   return ffn_one(x, hidden, ffn, ids, weights, k, out, kMaxExperts, stream,
                  [&](DecodeRoute* route, __nv_bfloat16* act, ErrorWord* err) {
                    const Q8Rows none{nullptr, nullptr, 0};
+                   const DecodeRouting routing{nullptr, route, kMaxExperts, static_cast<int>(k), 0, nullptr,
+                                               nullptr};
                    return launch_decode_experts_q8(x, 1, H, F, 0, Q8Rows{gate_q, gate_s, H}, Q8Rows{up_q, up_s, H},
-                                                   Q8Rows{down_q, down_s, F}, none, none, none, route, act, nullptr,
-                                                   nullptr, out, err, sms, stream);
+                                                   Q8Rows{down_q, down_s, F}, none, none, none, routing, act,
+                                                   nullptr, nullptr, out, err, sms, stream);
                  });
 }
 

@@ -11,34 +11,55 @@ namespace uocr_b200 {
 // Records `what` as uocr_last_error() for this thread and returns `code`.
 int set_last_error(int code, const std::string& what);
 
-// One-time per-device set-up (shared-memory opt-in, occupancy) so that later
-// launches, including those inside a stream capture, only launch.
+// One-time per-device set-up (shared-memory opt-in) so that later launches,
+// including those inside a stream capture, only launch.
 cudaError_t prepare_router_decode();
 cudaError_t prepare_decode_experts(int max_rows, int hidden);
 
+// cudaLaunchKernelExC, optionally with programmatic stream serialisation
+// (the kernel may start before the previous grid in the stream finishes and
+// must call griddepcontrol.wait before reading that grid's output).
+cudaError_t launch_maybe_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args,
+                             bool pdl);
+
 // ---- router (router.cu) ----
-cudaError_t launch_router_decode(const float* x, int T, int H, const float* router, const float* bias, int E, int K,
-                                 int renorm, float* logits, int* ids, float* weights, DecodeRoute* route,
-                                 unsigned* counter, ErrorWord* err, cudaStream_t stream);
+// logits [T, E] = x [T, H] . router [E, H]^T (+ bias), the reference's fp32 dot order.
+cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
+                                 float* logits, cudaStream_t stream, bool pdl = false);
 cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,
                              float* weights, cudaStream_t stream);
 cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int K, int E, DecodeRoute* route,
                                   ErrorWord* err, cudaStream_t stream);
 
 // ---- decode experts (decode.cu) ----
+// Where the decode expert kernels take their routing from: the router's
+// logits (each block runs softmax/top-k itself), or, when logits is null, a
+// prepared table. ids_out / weights_out (optional) receive the rank-order
+// selection [T, k].
+struct DecodeRouting {
+  const float* logits;
+  const DecodeRoute* table;
+  int experts;
+  int top_k;
+  int renormalize;
+  int* ids_out;
+  float* weights_out;
+};
+
 // Launches gate/up then down+combine; `between` (optional) is recorded
 // between the two, for per-kernel timing.
 cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int S, const __nv_bfloat16* gate,
                                        const __nv_bfloat16* up, const __nv_bfloat16* down,
                                        const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
-                                       const __nv_bfloat16* sdown, const DecodeRoute* route, __nv_bfloat16* act,
-                                       __nv_bfloat16* act_s, const float* resid, float* y, ErrorWord* err,
-                                       int sm_count, cudaStream_t stream, cudaEvent_t between = nullptr);
+                                       const __nv_bfloat16* sdown, const DecodeRouting& routing,
+                                       __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
+                                       ErrorWord* err, int sm_count, cudaStream_t stream,
+                                       cudaEvent_t between = nullptr, bool pdl = false);
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
-                                     Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown, const DecodeRoute* route,
-                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
-                                     ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between = nullptr);
+                                     Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
+                                     const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
+                                     const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
+                                     cudaEvent_t between = nullptr, bool pdl = false);
 
 // ---- weights and synthetic inputs (weights.cu) ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);

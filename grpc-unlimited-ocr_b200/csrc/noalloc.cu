@@ -94,9 +94,10 @@ extern "C" int uocr_expert_ffn_one_noalloc(const float* x, int64_t hidden, int64
   auto b = [](const uint16_t* v) { return reinterpret_cast<const __nv_bfloat16*>(v); };
   cudaError_t st = cudaMemsetAsync(err, 0, sizeof(ErrorWord), stream);  // the only state that must start at zero
   if (st == cudaSuccess) st = launch_route_from_ids(ids, weights, static_cast<int>(k), kMaxExperts, route, err, stream);
+  const DecodeRouting routing{nullptr, route, kMaxExperts, static_cast<int>(k), 0, nullptr, nullptr};
   if (st == cudaSuccess)
     st = launch_decode_experts_bf16(x, 1, static_cast<int>(hidden), static_cast<int>(ffn), 0, b(gate), b(up),
-                                    b(down), nullptr, nullptr, nullptr, route, act, nullptr, nullptr, out, err,
+                                    b(down), nullptr, nullptr, nullptr, routing, act, nullptr, nullptr, out, err,
                                     sms > 0 ? sms : 1, stream);
   if (st != cudaSuccess)
     return noalloc_fail(UOCR_ERR_CUDA, std::string("expert_ffn_one_noalloc: ") + cudaGetErrorString(st));

@@ -1,4 +1,4 @@
-// Router gate, softmax and top-k selection.
+// Router gate logits, and the standalone top-k op.
 //
 // The logits are computed in fp32 with exactly the reference's summation
 // order — eight lane partial sums over i = 8j + lane, a fixed combine tree,
@@ -6,120 +6,40 @@
 // with every product and sum separately rounded. So the device logits are
 // bit-identical to the oracle's, and the selected expert ids differ from the
 // reference only where its float exp and CUDA's expf round a near-tie apart.
-// Selection follows src/model/feed_forward.cpp:43-48 and
-// src/backend/cuda/ops.cu:598-645: softmax with a double-precision total in
-// index order, then k rounds of "best remaining", lower id on a tie.
+// Softmax and top-k selection live in route.cuh (each expert-kernel block
+// runs them on these logits).
 #include "moe_kernels.h"
+#include "ptx.cuh"
+#include "route.cuh"
 
 namespace uocr_b200 {
 namespace {
 
-// Softmax + top-k of one row by one warp. `ebuf` is per-warp shared scratch
-// of kMaxExperts floats. Lane 0 returns the results through ids/weights.
-template <typename IdT>
-__device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm, float* ebuf, IdT* ids,
-                                  float* weights) {
-  const int lane = threadIdx.x & 31;
-  float v[4];
-  float peak = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? __ldcg(logits + e) : -INFINITY;
-    peak = fmaxf(peak, v[i]);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, off));
-  if (peak == -INFINITY) {
-    // A fully masked row softmaxes to zeros (ops.cpp:175-177).
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = lane + 32 * i < E ? 0.0f : -INFINITY;
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) {
-        v[i] = expf(v[i] - peak);
-        ebuf[e] = v[i];
-      }
-    }
-    __syncwarp();
-    float inv = 0.0f;
-    if (lane == 0) {
-      double total = 0.0;
-      for (int e = 0; e < E; ++e) total += static_cast<double>(ebuf[e]);
-      inv = static_cast<float>(1.0 / total);
-    }
-    inv = __shfl_sync(0xffffffffu, inv, 0);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (lane + 32 * i < E) v[i] = v[i] * inv;
-    __syncwarp();
-  }
-  float sum = 0.0f;
-  float chosen[kMaxTopK];
-  int chosen_id[kMaxTopK];
-  for (int j = 0; j < K; ++j) {
-    float best = -INFINITY;
-    int best_e = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (v[i] > best || (v[i] == best && e < best_e))) {
-        best = v[i];
-        best_e = e;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
-      if (ob > best || (ob == best && oe < best_e)) {
-        best = ob;
-        best_e = oe;
-      }
-    }
-    // Remove the winner from its owner lane (a removed slot can never win again).
-    if ((best_e & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (i == (best_e >> 5)) v[i] = -INFINITY;
-    }
-    chosen[j] = best;
-    chosen_id[j] = best_e;
-    sum += best;
-  }
-  if (lane == 0) {
-    for (int j = 0; j < K; ++j) {
-      ids[j] = static_cast<IdT>(chosen_id[j]);
-      weights[j] = renorm ? chosen[j] / sum : chosen[j];
-    }
-  }
-}
-
 // One block per expert row of the router: logits[t, e] for every row t of
-// the decode batch, in the reference's dot order. The last block to finish
-// runs softmax/top-k for every row and writes the decode routing table.
-__global__ void __launch_bounds__(256) router_decode_kernel(const float* __restrict__ x, int T, int H,
+// the batch, in the reference's dot order. Launched with programmatic
+// dependent launch: the router row is staged before waiting for the previous
+// grid (which writes x).
+__global__ void __launch_bounds__(256) router_logits_kernel(const float* __restrict__ x, int T, int H,
                                                             const float* __restrict__ router,
-                                                            const float* __restrict__ bias, int E, int K,
-                                                            int renorm, float* logits, int* ids, float* weights,
-                                                            DecodeRoute* route, unsigned* counter,
-                                                            ErrorWord* err) {
+                                                            const float* __restrict__ bias, int E,
+                                                            float* __restrict__ logits) {
   extern __shared__ float smem[];
   const int e = blockIdx.x;
+  const int tid = threadIdx.x;
   const int xstride = H + 8;  // rows 8 floats apart: the four rows a warp reads sit in different banks
   float* ws = smem;
   float* xs = smem + H;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) ws[i] = router[static_cast<int64_t>(e) * H + i];
-  for (int i = threadIdx.x; i < T * H; i += blockDim.x) xs[(i / H) * xstride + (i % H)] = x[i];
+  for (int i = tid; i < H; i += blockDim.x) ws[i] = __ldg(router + static_cast<int64_t>(e) * H + i);
+  pdl_wait();  // x is written by the previous grid
+  pdl_launch_dependents();
+  for (int i = tid; i < T * H; i += blockDim.x) xs[(i / H) * xstride + (i % H)] = __ldcg(x + i);
   __syncthreads();
 
-  const int lane8 = threadIdx.x & 7;
+  const int lane8 = tid & 7;
   const int groups = blockDim.x >> 3;
   const int full = H & ~7;
   for (int t0 = 0; t0 < T; t0 += groups) {
-    const int t = t0 + (threadIdx.x >> 3);
+    const int t = t0 + (tid >> 3);
     float acc = 0.0f, tail = 0.0f;
     if (t < T) {
       const float* xr = xs + t * xstride;
@@ -129,7 +49,7 @@ __global__ void __launch_bounds__(256) router_decode_kernel(const float* __restr
         for (int i = full; i < H; ++i) tail = __fadd_rn(tail, __fmul_rn(xr[i], ws[i]));
     }
     float a[8];
-    const int base = (threadIdx.x & 31) & ~7;
+    const int base = (tid & 31) & ~7;
 #pragma unroll
     for (int q = 0; q < 8; ++q) a[q] = __shfl_sync(0xffffffffu, acc, base + q);
     if (t < T && lane8 == 0) {
@@ -139,63 +59,6 @@ __global__ void __launch_bounds__(256) router_decode_kernel(const float* __restr
       if (bias != nullptr) s = __fadd_rn(s, bias[e]);
       logits[static_cast<int64_t>(t) * E + e] = s;
     }
-  }
-
-  __shared__ bool is_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(counter, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-
-  __shared__ float ebuf[8][kMaxExperts];
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  for (int t = warp; t < T; t += nwarps)
-    softmax_topk_warp<int>(logits + static_cast<int64_t>(t) * E, E, K, renorm, ebuf[warp], ids + t * K,
-                           weights + t * K);
-  __threadfence();
-  __syncthreads();
-
-  if (threadIdx.x == 0) {
-    // Experts in ascending id order, each with its rows in row order: the
-    // order the reference adds routed contributions (feed_forward.cpp:66-75).
-    __shared__ int slot_of[kMaxExperts];
-    for (int i = 0; i < E; ++i) slot_of[i] = -1;
-    for (int i = 0; i < T * K; ++i) {
-      const int id = __ldcg(ids + i);
-      if (id < 0 || id >= E) {
-        raise_error(err, kDevBadIndex, 1, i, id);
-        continue;
-      }
-      slot_of[id] = 0;
-    }
-    int U = 0;
-    for (int i = 0; i < E; ++i)
-      if (slot_of[i] == 0) {
-        route->active_expert[U] = i;
-        route->tok_count[U] = 0;
-        slot_of[i] = U++;
-      }
-    route->active_count = U;
-    for (int t = 0; t < T; ++t)
-      for (int j = 0; j < K; ++j) {
-        const int id = __ldcg(ids + t * K + j);
-        if (id < 0 || id >= E) continue;
-        const int u = slot_of[id];
-        const int s = route->tok_count[u]++;
-        route->tok_index[u][s] = t;
-        route->tok_weight[u][s] = __ldcg(weights + t * K + j);
-      }
-    int base = 0;
-    for (int u = 0; u < U; ++u) {
-      route->slot_base[u] = base;
-      base += route->tok_count[u];
-    }
-    route->slot_total = base;
-    __threadfence();
-    *counter = 0u;  // ready for the next launch (and graph replays)
   }
 }
 
@@ -239,24 +102,23 @@ cudaError_t prepare_router_decode() {
   cudaError_t st = cudaGetDevice(&dev);
   if (st != cudaSuccess) return st;
   if (dev < kMaxDevices && !raised[dev]) {
-    st = allow_max_dynamic_smem(router_decode_kernel);
+    st = allow_max_dynamic_smem(router_logits_kernel);
     if (st != cudaSuccess) return st;
     raised[dev] = true;
   }
   return cudaSuccess;
 }
 
-cudaError_t launch_router_decode(const float* x, int T, int H, const float* router, const float* bias, int E, int K,
-                                 int renorm, float* logits, int* ids, float* weights, DecodeRoute* route,
-                                 unsigned* counter, ErrorWord* err, cudaStream_t stream) {
+cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
+                                 float* logits, cudaStream_t stream, bool pdl) {
   const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
   if (smem > 48 * 1024) {
     const cudaError_t st = prepare_router_decode();
     if (st != cudaSuccess) return st;
   }
-  router_decode_kernel<<<E, 256, smem, stream>>>(x, T, H, router, bias, E, K, renorm, logits, ids, weights, route,
-                                                 counter, err);
-  return cudaGetLastError();
+  void* args[] = {&x, &T, &H, &router, &bias, &E, &logits};
+  return launch_maybe_pdl(reinterpret_cast<const void*>(router_logits_kernel), dim3(E), dim3(256), smem, stream, args,
+                          pdl);
 }
 
 cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,
