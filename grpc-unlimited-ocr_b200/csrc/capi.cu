@@ -16,6 +16,7 @@
 
 #include "../../include/uocr_moe.h"
 #include "moe_kernels.h"
+#include "prefill.h"
 
 using namespace uocr_b200;
 
@@ -107,6 +108,10 @@ struct uocr_moe_plan {
   __nv_bfloat16* act_s = nullptr;
   unsigned* counter = nullptr;
   ErrorWord* err = nullptr;
+  // Prefill (rows above decode_rows): tcgen05 grouped GEMM path, bf16 weights.
+  bool prefill = false;
+  PrefillDims pdims{};
+  PrefillScratch pscratch{};
 
   // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
   struct GraphEntry {
@@ -153,6 +158,10 @@ struct uocr_moe_plan {
     act_s = c.take<__nv_bfloat16>(dr * (S > 0 ? S : 1));
     counter = c.take<unsigned>(1);
     err = c.take<ErrorWord>(1);
+    if (prefill) {
+      char* base = c.take<char>(prefill_scratch_bytes(pdims));
+      carve_prefill_scratch(pdims, base, &pscratch);
+    }
   }
 };
 
@@ -243,6 +252,14 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
       return cuda_fail(pst, "plan_create: kernel set-up");
     }
   }
+  // Rows above the decode limit run the prefill path: bf16 weights and the
+  // tile multiples of the tensor-core grouped GEMM.
+  p->prefill = d.max_rows > dr && d.weight_format == UOCR_WEIGHT_BF16 &&
+               prefill_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
+                                 static_cast<int>(d.shared_ffn));
+  p->pdims = PrefillDims{static_cast<int>(d.max_rows), static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
+                         static_cast<int>(d.experts_per_token), static_cast<int>(d.expert_ffn),
+                         static_cast<int>(d.shared_ffn), d.renormalize};
 
   Carver probe{nullptr};
   LayerDev tmp;
@@ -380,8 +397,35 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts),
             K = static_cast<int>(d.experts_per_token), F = static_cast<int>(d.expert_ffn),
             S = static_cast<int>(d.shared_ffn);
-  if (rows > p->decode_rows)
-    return fail(UOCR_ERR_UNSUPPORTED, "forward: rows above the decode limit need the prefill path, not built yet");
+  if (rows > p->decode_rows) {
+    if (!p->prefill)
+      return fail(UOCR_ERR_UNSUPPORTED,
+                  "forward: more than 16 rows needs the prefill path: bf16 weights, hidden % 256 == 0, "
+                  "expert_ffn and shared_ffn % 128 == 0");
+    auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
+    PrefillCall c{};
+    c.dims = p->pdims;
+    c.scratch = p->pscratch;
+    c.rows = T;
+    c.x = x;
+    c.router = L.router;
+    c.bias = L.bias;
+    c.gate = b(L.gate);
+    c.up = b(L.up);
+    c.down = b(L.down);
+    c.sgate = b(L.sgate);
+    c.sup = b(L.sup);
+    c.sdown = b(L.sdown);
+    c.logits = p->logits;
+    c.ids = p->ids;
+    c.weights = p->weights;
+    c.resid = resid;
+    c.y = y;
+    c.err = p->err;
+    c.sm_count = p->sm_count;
+    UOCR_TRY(launch_prefill(c, stream), "forward: prefill");
+    return UOCR_OK;
+  }
   // Programmatic dependent launch chains router -> gate/up -> down (and the
   // next layer's router); the profiling path records events between them instead.
   const bool pdl = ev == nullptr;
@@ -597,6 +641,48 @@ int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const in
                                                    Q8Rows{down_q, down_s, F}, none, none, none, routing, act,
                                                    nullptr, nullptr, out, err, sms, stream);
                  });
+}
+
+int uocr_linear(const float* x, int64_t m, int64_t k, const uint16_t* w_bf16, int64_t n, const float* bias, float* y,
+                void* stream_v) {
+  if (m < 0 || k <= 0 || n <= 0) return fail(UOCR_ERR_INVALID_ARGUMENT, "linear: bad shape");
+  if (k % 64 != 0 || n % 256 != 0)
+    return fail(UOCR_ERR_UNSUPPORTED, "linear: this build needs k % 64 == 0 and n % 256 == 0");
+  if (m == 0) return UOCR_OK;
+  if (x == nullptr || w_bf16 == nullptr || y == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "linear: null pointer");
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const size_t xb_bytes = align_up(static_cast<size_t>(m * k) * 2, 256);
+  char* scratch = nullptr;
+  UOCR_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), xb_bytes + sizeof(ErrorWord), stream),
+           "linear: scratch");
+  auto* xb = reinterpret_cast<__nv_bfloat16*>(scratch);
+  auto* err = reinterpret_cast<ErrorWord*>(scratch + xb_bytes);
+  cudaError_t st = cudaMemsetAsync(err, 0, sizeof(ErrorWord), stream);
+  if (st == cudaSuccess) st = launch_f32_to_bf16(x, xb, m * k, stream);
+  if (st == cudaSuccess) {
+    GroupedGemm g{};
+    g.mode = 1;
+    g.experts = 0;
+    g.k_routed = 64;
+    g.n_cols_routed = 256;
+    g.shared_rows = static_cast<int>(m);
+    g.a_shared = xb;
+    g.k_shared = static_cast<int>(k);
+    g.b0_shared = reinterpret_cast<const __nv_bfloat16*>(w_bf16);
+    g.b1_shared = g.b0_shared;
+    g.b_shared_rows = n;
+    g.n_cols_shared = static_cast<int>(n);
+    g.out_shared = y;
+    g.ld_out_shared = n;
+    g.shared_out_f32 = true;
+    g.err = err;
+    g.blocks = device_sms();
+    st = launch_grouped_gemm(g, stream);
+  }
+  if (st == cudaSuccess && bias != nullptr) st = launch_add_bias(y, bias, m, n, stream);
+  cudaFreeAsync(scratch, stream);
+  if (st != cudaSuccess) return cuda_fail(st, "linear");
+  return UOCR_OK;
 }
 
 int uocr_quantize_q8(const void* w, int32_t dtype, int64_t rows, int64_t cols, int64_t group, int8_t* q,

@@ -92,6 +92,13 @@ __global__ void synth_kernel(uint64_t key, float sigma, int64_t offset, int64_t 
   }
 }
 
+__global__ void add_bias_kernel(float* y, const float* bias, int64_t rows, int64_t cols) {
+  const int64_t n = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = __fadd_rn(y[i], bias[i % cols]);
+}
+
 unsigned grid_for(int64_t n) {
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
@@ -103,6 +110,12 @@ unsigned grid_for(int64_t n) {
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   f32_to_bf16_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_bias(float* y, const float* bias, int64_t rows, int64_t cols, cudaStream_t stream) {
+  if (rows * cols == 0) return cudaSuccess;
+  add_bias_kernel<<<grid_for(rows * cols), 256, 0, stream>>>(y, bias, rows, cols);
   return cudaGetLastError();
 }
 

@@ -30,7 +30,7 @@ EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
     "uocr_moe_set_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_expert_topk",
-    "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
+    "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
 ]
 
 
@@ -79,6 +79,7 @@ def lib() -> ctypes.CDLL:
         L.uocr_expert_ffn_one_noalloc.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
         L.uocr_expert_ffn_one_q8.argtypes =[vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp]
         L.uocr_quantize_q8.argtypes = [vp, i32, i64, i64, i64, vp, vp, vp]
+        L.uocr_linear.argtypes = [vp, i64, i64, vp, i64, vp, vp, vp]
         L.uocr_synth_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64, f32, i64, i64, i32, vp, vp]
         L.uocr_synth_stream.argtypes = [ctypes.c_uint64] * 3
         L.uocr_synth_stream.restype = ctypes.c_uint64
@@ -217,3 +218,10 @@ def synth_fill(out, seed: int, layer: int, kind: int, index: int, sigma: float, 
     dtype = DTYPE_BF16 if out.dtype == torch.bfloat16 else DTYPE_F32
     _check(lib().uocr_synth_fill(seed, synth_stream(layer, kind, index), sigma, offset, out.numel(), dtype,
                                  _ptr(out), _stream(stream)))
+
+
+def linear(x, w_bf16, y, bias=None, stream=None):
+    """y[m, n] = bf16(x)[m, k] . w[n, k]^T (+ bias) on the tensor cores (uocr_linear)."""
+    m, k = x.shape
+    n = w_bf16.shape[0]
+    _check(lib().uocr_linear(_ptr(x), m, k, _ptr(w_bf16), n, _ptr(bias), _ptr(y), _stream(stream)))

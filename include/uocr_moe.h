@@ -167,6 +167,14 @@ int uocr_expert_ffn_one_q8(const float* x, int64_t hidden, int64_t ffn, const in
                            const int8_t* up_q, const float* up_s, const int8_t* down_q, const float* down_s,
                            const int64_t* ids, const float* weights, int64_t k, float* out, void* stream);
 
+/* src/backend/cuda/ops.h:14-17 linear: y[m, n] = x[m, k] w[n, k]^T (+ bias[n]),
+ * x rounded to bf16 for the product, fp32 accumulation — on the tcgen05
+ * tensor cores (the reference calls cublasGemmEx). Like the reference it takes
+ * its bf16 copy of x from cudaMallocAsync on the stream. This build needs
+ * k % 64 == 0 and n % 256 == 0 (UOCR_ERR_UNSUPPORTED otherwise). */
+int uocr_linear(const float* x, int64_t m, int64_t k, const uint16_t* w_bf16, int64_t n, const float* bias, float* y,
+                void* stream);
+
 /* src/model/cuda/device_weight.cpp:11-26 quantize_q8_rows on the device, with
  * the group free (group = cols is per output channel). w is fp32 or bf16
  * (dtype); q [rows, cols], scales [rows, cols/group]. Device pointers. */
