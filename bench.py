@@ -175,6 +175,86 @@ def host_layer_weights(cfg, layer=0):
     return w
 
 
+def measured_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu):
+    """BASELINE config 3 on one GPU: one MoE layer over 32768 rows (8 pages x
+    4096), Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and
+    the gate/up GEMM against the bf16 tensor roofline."""
+    import torch
+    cfg = C.CONFIGS[3]
+    T = cfg.rows[0]
+    plan = M.Plan(cfg.dims(), max_rows=T, router_bias=True, device=dev.index or 0)
+    t = C.device_layer(cfg, 0, device=dev)
+    C.load_layer(plan, cfg, 0, t)
+    x = C.device_input(cfg, T, device=dev)
+    y = torch.empty_like(x)
+    ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            plan.forward(0, x, y, ids, stream=stream)
+        plan.check(stream=stream)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            plan.forward(0, x, y, stream=stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / steps
+        h = x.clone()
+        prof = plan.profile_stack(h, iters=3, stream=stream)
+        plan.check(stream=stream)
+    counts = torch.bincount(ids.view(-1).long(), minlength=cfg.experts).cpu().tolist()
+    H, F, S = cfg.hidden, cfg.ffn, cfg.shared_ffn
+    R = T * cfg.top_k
+    gu_flops = R * 4 * F * H + T * 4 * S * H
+    dn_flops = R * 2 * F * H + T * 2 * S * H
+    total_flops = gu_flops + dn_flops + 2 * T * cfg.experts * H
+    peak, peak_src = measured_tensor_peak()
+    gu_tf = gu_flops / (prof["gate_up_gemm"] * 1e-3) / 1e12
+    dn_tf = dn_flops / (prof["down_gemm"] * 1e-3) / 1e12
+    out = {
+        "workload": f"{cfg.name}: 1 layer, {T} rows (8 pages x 4096), Zipf(1.2)-biased router, bf16",
+        "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_layer": ms,
+        "tflops_per_layer": total_flops / (ms * 1e-3) / 1e12,
+        "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
+        "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (tcgen05 grouped, SwiGLU fused)", "achieved": gu_tf,
+                     "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s", "frac": gu_tf / peak,
+                     "down_gemm_achieved": dn_tf, "down_gemm_frac": dn_tf / peak,
+                     "algorithmic_flops_per_layer": total_flops},
+        "expert_rows": counts, "top_expert_share": max(counts) / R,
+    }
+    if want_cpu:
+        cpu_rows = 512
+        hw = host_layer_weights(cfg)
+        hw.router_bias = t["router_bias"].cpu().numpy()
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        xs = x[:cpu_rows].cpu().numpy()
+        O.moe_forward(hw, xs[:8], cfg.top_k, True)
+        times = []
+        t_end = time.perf_counter() + cpu_budget
+        while time.perf_counter() < t_end or len(times) < 2:
+            t0 = time.perf_counter()
+            O.moe_forward(hw, xs, cfg.top_k, True)
+            times.append(time.perf_counter() - t0)
+        cores = os.cpu_count() or 1
+        out["cpu_baseline"] = {"value": cpu_rows / statistics.median(times), "unit": "tokens/s", "cores": cores,
+                               "kind": "port",
+                               "sample": f"{cpu_rows} of the {T} rows, median of {len(times)} runs (the reference "
+                                         "MoE has no router bias, so the C restatement runs this config)"}
+    plan.close()
+    return out
+
+
 def run_reference_arm(args, cfg, world, rank):
     """--impl reference: the reference's CPU MoE on the host cores, same metric."""
     if rank != 0:
@@ -220,6 +300,7 @@ def main():
     ap.add_argument("--layers", type=int, default=None, help="override the stack depth (default 24)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill section")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -336,6 +417,12 @@ def main():
     step_gbs = step_bytes / (ms_max * 1e-3) / 1e9
     traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
 
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        plan.close()  # free the decode stack's 20 GB first
+        prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
+                              want_cpu=not args.no_cpu_baseline)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host_layer0 = host_layer_weights(cfg)
@@ -373,6 +460,8 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     plan.close()
     if world > 1:

@@ -389,10 +389,14 @@ int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src
 
 namespace {
 
+constexpr int kMaxProfileKernels = 6;
+
 // One layer on `rows` rows: route, then experts. resid != null adds the
-// layer input back (the stack's residual); y may then alias resid.
+// layer input back (the stack's residual); y may then alias resid. For
+// measurement, ev (kMaxProfileKernels events) receives one event after each
+// kernel of the path taken and *nev their count.
 int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows, const float* resid, float* y,
-              cudaStream_t stream, const cudaEvent_t* ev = nullptr) {
+              cudaStream_t stream, cudaEvent_t* ev = nullptr, int* nev = nullptr) {
   const uocr_moe_desc& d = p->d;
   const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts),
             K = static_cast<int>(d.experts_per_token), F = static_cast<int>(d.expert_ffn),
@@ -423,7 +427,9 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
     c.y = y;
     c.err = p->err;
     c.sm_count = p->sm_count;
+    c.events = ev;
     UOCR_TRY(launch_prefill(c, stream), "forward: prefill");
+    if (nev != nullptr) *nev = 6;
     return UOCR_OK;
   }
   // Programmatic dependent launch chains router -> gate/up -> down (and the
@@ -447,6 +453,8 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
                                       p->sm_count, stream, between, pdl),
              "forward: experts");
   }
+  if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[2], stream), "forward: event");
+  if (nev != nullptr) *nev = 3;
   return UOCR_OK;
 }
 
@@ -537,40 +545,36 @@ int uocr_moe_profile_stack(uocr_moe_plan* p, float* h, int64_t rows, int32_t ite
   DeviceGuard guard(p->d.device);
   auto stream = static_cast<cudaStream_t>(stream_v);
   const size_t nl = p->layers.size();
-  // Per layer and pass: start, after router, after gate/up, after down.
-  std::vector<cudaEvent_t> ev(static_cast<size_t>(iters) * nl * 3 + 1);
+  // Per layer pass: a start event, then one event after each kernel.
+  constexpr size_t kSlot = kMaxProfileKernels + 1;
+  const size_t passes = static_cast<size_t>(iters) * nl;
+  std::vector<cudaEvent_t> ev(passes * kSlot);
   for (auto& e : ev) UOCR_TRY(cudaEventCreate(&e), "profile_stack: event");
   int rc = UOCR_OK;
-  size_t k = 0;
-  UOCR_TRY(cudaEventRecord(ev[k++], stream), "profile_stack: event");
-  for (int it = 0; it < iters && rc == UOCR_OK; ++it)
-    for (size_t l = 0; l < nl && rc == UOCR_OK; ++l) {
-      rc = run_layer(p, p->layers[l], h, rows, h, h, stream, &ev[k]);
-      if (rc == UOCR_OK) rc = cudaEventRecord(ev[k + 2], stream) == cudaSuccess ? UOCR_OK : UOCR_ERR_CUDA;
-      k += 3;
-    }
-  double sum[3] = {0, 0, 0};
+  int nk = 0;
+  for (size_t j = 0; j < passes && rc == UOCR_OK; ++j) {
+    rc = cudaEventRecord(ev[j * kSlot], stream) == cudaSuccess ? UOCR_OK : fail(UOCR_ERR_CUDA, "profile_stack: event");
+    if (rc == UOCR_OK) rc = run_layer(p, p->layers[j % nl], h, rows, h, h, stream, &ev[j * kSlot + 1], &nk);
+  }
+  double sum[kMaxProfileKernels] = {};
   float total = 0;
-  if (rc == UOCR_OK && cudaEventSynchronize(ev[k - 1]) == cudaSuccess) {
-    // Layer pass j spans ev[3j] (its start) .. ev[3j+3] (end of its down kernel).
-    for (size_t j = 0; j < static_cast<size_t>(iters) * nl; ++j) {
-      float a = 0, b = 0, c = 0;
-      cudaEventElapsedTime(&a, ev[3 * j], ev[3 * j + 1]);
-      cudaEventElapsedTime(&b, ev[3 * j + 1], ev[3 * j + 2]);
-      cudaEventElapsedTime(&c, ev[3 * j + 2], ev[3 * j + 3]);
-      sum[0] += a;
-      sum[1] += b;
-      sum[2] += c;
-    }
-    cudaEventElapsedTime(&total, ev[0], ev[k - 1]);
+  if (rc == UOCR_OK && cudaEventSynchronize(ev[(passes - 1) * kSlot + nk]) == cudaSuccess) {
+    for (size_t j = 0; j < passes; ++j)
+      for (int i = 0; i < nk; ++i) {
+        float t = 0;
+        cudaEventElapsedTime(&t, ev[j * kSlot + i], ev[j * kSlot + i + 1]);
+        sum[i] += t;
+      }
+    cudaEventElapsedTime(&total, ev[0], ev[(passes - 1) * kSlot + nk]);
   } else if (rc == UOCR_OK) {
     rc = fail(UOCR_ERR_CUDA, "profile_stack: synchronise");
   }
   for (auto& e : ev) cudaEventDestroy(e);
   if (rc != UOCR_OK) return rc;
-  const double n = static_cast<double>(iters) * static_cast<double>(nl);
-  for (int i = 0; i < 3; ++i) ms[i] = static_cast<float>(sum[i] / n);
-  ms[3] = total / static_cast<float>(iters);
+  for (int i = 0; i < 8; ++i) ms[i] = 0.0f;
+  for (int i = 0; i < nk; ++i) ms[i] = static_cast<float>(sum[i] / static_cast<double>(passes));
+  ms[6] = static_cast<float>(nk);
+  ms[7] = total / static_cast<float>(iters);
   return UOCR_OK;
 }
 

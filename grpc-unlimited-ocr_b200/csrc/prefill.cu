@@ -317,10 +317,12 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   const PrefillScratch& s = c.scratch;
   const int T = c.rows, H = d.hidden, E = d.experts, K = d.top_k, F = d.ffn, S = d.shared_ffn;
   if (T <= 0) return cudaSuccess;
+  // Optional per-kernel timing: an event after each stage of the path.
+  auto mark = [&](int i) { return c.events != nullptr ? cudaEventRecord(c.events[i], stream) : cudaSuccess; };
   cudaError_t st = launch_router_logits_rows(c.x, T, H, c.router, c.bias, E, c.logits, stream);
-  if (st != cudaSuccess) return st;
+  if (st != cudaSuccess || (st = mark(0)) != cudaSuccess) return st;
   topk_rows_i32_kernel<<<(T + 7) / 8, 256, 0, stream>>>(c.logits, T, E, K, d.renormalize, c.ids, c.weights);
-  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  if ((st = cudaGetLastError()) != cudaSuccess || (st = mark(1)) != cudaSuccess) return st;
   const int nblk = (T + kPermBlock - 1) / kPermBlock;
   count_kernel<<<nblk, kPermBlock, 0, stream>>>(c.ids, T, K, E, s.block_counts, c.err);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
@@ -328,7 +330,7 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
   scatter_kernel<<<nblk, kPermBlock, 0, stream>>>(c.x, T, H, K, E, c.ids, s.block_offset, s.pos_of, s.xhat,
                                                   s.xperm);
-  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  if ((st = cudaGetLastError()) != cudaSuccess || (st = mark(2)) != cudaSuccess) return st;
 
   const int64_t R = static_cast<int64_t>(T) * K;
   GroupedGemm g1{};
@@ -358,7 +360,7 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   g1.shared_out_f32 = false;
   g1.err = c.err;
   g1.blocks = c.sm_count;
-  if ((st = launch_grouped_gemm(g1, stream)) != cudaSuccess) return st;
+  if ((st = launch_grouped_gemm(g1, stream)) != cudaSuccess || (st = mark(3)) != cudaSuccess) return st;
 
   GroupedGemm g2 = g1;
   g2.mode = 1;
@@ -380,11 +382,12 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   g2.out_shared = s.shared_out;
   g2.ld_out_shared = H;
   g2.shared_out_f32 = true;
-  if ((st = launch_grouped_gemm(g2, stream)) != cudaSuccess) return st;
+  if ((st = launch_grouped_gemm(g2, stream)) != cudaSuccess || (st = mark(4)) != cudaSuccess) return st;
 
   combine_kernel<<<T, 256, 0, stream>>>(T, H, K, c.ids, c.weights, s.pos_of, s.yperm, S > 0 ? s.shared_out : nullptr,
                                         c.resid, c.y);
-  return cudaGetLastError();
+  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  return mark(5);
 }
 
 }  // namespace uocr_b200

@@ -60,6 +60,9 @@ struct PrefillCall {
   float* y;                 // [T, H]
   ErrorWord* err;
   int sm_count;
+  // Optional: 6 events recorded after router, top-k, permutation, gate/up
+  // GEMM, down GEMM and combine (null: none).
+  cudaEvent_t* events;
 };
 
 cudaError_t launch_router_logits_rows(const float* x, int T, int H, const float* router, const float* bias, int E,

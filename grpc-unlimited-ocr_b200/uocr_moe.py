@@ -163,12 +163,18 @@ class Plan:
         rows = h.shape[0] if rows is None else rows
         _check(lib().uocr_moe_forward_stack(self.h, _ptr(h), rows, _stream(stream)))
 
+    DECODE_KERNELS = ("router", "gate_up", "down")
+    PREFILL_KERNELS = ("router", "topk", "permute", "gate_up_gemm", "down_gemm", "combine")
+
     def profile_stack(self, h, iters: int, stream=None, rows: int | None = None):
-        """Mean device ms per launch of (router, gate/up, down) and per stack pass."""
+        """Mean device ms per launch of each kernel of the path, and per stack pass."""
         rows = h.shape[0] if rows is None else rows
-        out = (ctypes.c_float * 4)()
+        out = (ctypes.c_float * 8)()
         _check(lib().uocr_moe_profile_stack(self.h, _ptr(h), rows, iters, out, _stream(stream)))
-        return {"router": out[0], "gate_up": out[1], "down": out[2], "stack": out[3]}
+        names = self.DECODE_KERNELS if int(out[6]) == 3 else self.PREFILL_KERNELS
+        res = {n: out[i] for i, n in enumerate(names)}
+        res["stack"] = out[7]
+        return res
 
     def check(self, stream=None):
         _check(lib().uocr_moe_check(self.h, _stream(stream)))

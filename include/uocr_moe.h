@@ -122,10 +122,12 @@ int uocr_moe_forward_stack(uocr_moe_plan* plan, float* h, int64_t rows, void* st
 int uocr_moe_check(uocr_moe_plan* plan, void* stream);
 
 /* Instrumented forward_stack for measurement: runs `iters` stack passes with
- * CUDA events between the kernels, synchronises, and writes the mean device
- * time per launch of each kernel in ms_per_kernel[0..2] (router, gate/up,
- * down+combine) and the mean time of one whole stack pass in ms_per_kernel[3].
- * No reference counterpart (the reference has no device timing). */
+ * CUDA events between the kernels, synchronises, and writes ms_per_kernel[8]:
+ * [0..5] the mean device time per launch of each kernel in launch order —
+ * decode rows (<= 16): router, gate/up, down+combine; prefill rows: router,
+ * top-k, permutation, gate/up GEMM, down GEMM, combine — [6] how many of those
+ * entries are used, [7] the mean time of one whole stack pass (events between
+ * kernels: no overlap between them). No reference counterpart. */
 int uocr_moe_profile_stack(uocr_moe_plan* plan, float* h, int64_t rows, int32_t iters, float* ms_per_kernel,
                            void* stream);
 
