@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "../../include/uocr_moe.h"
+#include "decode_tc.h"
 #include "moe_kernels.h"
 #include "prefill.h"
 
@@ -112,6 +113,9 @@ struct uocr_moe_plan {
   bool prefill = false;
   PrefillDims pdims{};
   PrefillScratch pscratch{};
+  // bf16 decode batches on the tensor cores.
+  bool decode_tc = false;
+  DecodeTcScratch dtc{};
 
   // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
   struct GraphEntry {
@@ -161,6 +165,11 @@ struct uocr_moe_plan {
     if (prefill) {
       char* base = c.take<char>(prefill_scratch_bytes(pdims));
       carve_prefill_scratch(pdims, base, &pscratch);
+    }
+    if (decode_tc) {
+      const int H = static_cast<int>(d.hidden), F = static_cast<int>(d.expert_ffn), S = static_cast<int>(d.shared_ffn);
+      char* base = c.take<char>(decode_tc_scratch_bytes(H, F, S));
+      carve_decode_tc_scratch(H, F, S, base, &dtc);
     }
   }
 };
@@ -260,6 +269,9 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   p->pdims = PrefillDims{static_cast<int>(d.max_rows), static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
                          static_cast<int>(d.experts_per_token), static_cast<int>(d.expert_ffn),
                          static_cast<int>(d.shared_ffn), d.renormalize};
+  p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
+                 decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
+                                     static_cast<int>(d.shared_ffn));
 
   Carver probe{nullptr};
   LayerDev tmp;
@@ -439,7 +451,31 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
   const DecodeRouting routing{p->logits, nullptr, E, K, d.renormalize, p->ids, p->weights};
-  if (d.weight_format == UOCR_WEIGHT_BF16) {
+  if (p->decode_tc) {
+    auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
+    DecodeTcCall c{};
+    c.x = x;
+    c.T = T;
+    c.H = H;
+    c.F = F;
+    c.S = S;
+    c.E = E;
+    c.gate = b(L.gate);
+    c.up = b(L.up);
+    c.down = b(L.down);
+    c.sgate = b(L.sgate);
+    c.sup = b(L.sup);
+    c.sdown = b(L.sdown);
+    c.routing = routing;
+    c.resid = resid;
+    c.y = y;
+    c.scratch = p->dtc;
+    c.err = p->err;
+    c.sm_count = p->sm_count;
+    c.pdl = pdl;
+    c.between = between;
+    UOCR_TRY(launch_decode_tc(c, stream), "forward: experts (tensor cores)");
+  } else if (d.weight_format == UOCR_WEIGHT_BF16) {
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
                                         b(L.sdown), routing, p->act, p->act_s, resid, y, p->err, p->sm_count,

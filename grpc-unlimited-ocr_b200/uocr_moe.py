@@ -21,6 +21,7 @@ WEIGHT_BF16, WEIGHT_INT8 = 0, 1
 MEMORY_HOST, MEMORY_DEVICE = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
+PLAN_TENSOR_DECODE = 2
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).
 KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KIND_X = 1, 2, 3, 4, 5, 6, 7, 8

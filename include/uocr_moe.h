@@ -74,6 +74,12 @@ typedef struct uocr_moe_desc {
  * layer. This flag turns the cache off. A stream that is already capturing,
  * or the legacy default stream, always gets plain launches. */
 #define UOCR_PLAN_NO_GRAPHS 1
+/* Decode batches (rows <= 16) stream the selected experts' weights through
+ * the CUDA cores by default. This flag runs bf16 decode batches on the
+ * tensor cores instead (tcgen05, weights as the 128-row operand, split-K);
+ * hidden, expert_ffn and shared_ffn must be multiples of 128, hidden <= 8192,
+ * else the flag is ignored. The int8 format always streams. */
+#define UOCR_PLAN_TENSOR_DECODE 2
 
 int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** plan);
 int uocr_moe_plan_destroy(uocr_moe_plan* plan);

@@ -101,16 +101,23 @@ def _upload(plan, w: O.MoeWeights, torch, cuda, layer=0):
     return keep
 
 
-@pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt", [
+SMALL_SHAPES = [
     (1, 64, 8, 3, 32, 32, True, 0), (5, 128, 16, 1, 48, 0, True, 0), (16, 256, 128, 8, 64, 64, True, 0),
     (3, 96, 12, 4, 32, 48, False, 0), (16, 64, 2, 2, 16, 16, True, 0), (7, 128, 32, 6, 64, 128, True, 1),
-    (16, 512, 64, 6, 256, 512, True, 1)])
-def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt):
+    (16, 512, 64, 6, 256, 512, True, 1), (2, 1024, 16, 2, 1536, 2560, True, 0), (9, 2048, 16, 4, 2560, 128, True, 1)]
+# shapes the tensor-core decode takes (hidden, ffn, shared all multiples of 128)
+TC_SHAPES = [(1, 256, 8, 3, 128, 128, True, 0), (5, 128, 128, 8, 128, 0, True, 0),
+             (16, 512, 64, 6, 256, 256, False, 0), (11, 384, 24, 5, 384, 128, True, 0)]
+
+
+@pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt,flags",
+                         [s + (0,) for s in SMALL_SHAPES + TC_SHAPES] + [s + (M.PLAN_TENSOR_DECODE,) for s in TC_SHAPES])
+def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt, flags):
     import torch
     rng = np.random.default_rng(T * 7919 + E)
     w = _tiny_layer(rng, H, E, F, S)
     x = rng.standard_normal((T, H)).astype(np.float32)
-    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=16, weight_format=fmt, renormalize=renorm)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=16, weight_format=fmt, renormalize=renorm, flags=flags)
     _upload(plan, w, torch, cuda)
     y, ids, wts = run_plan(plan, 0, torch.from_numpy(x).to(cuda), K, torch)
     ww = w
@@ -159,11 +166,12 @@ def c1_layer(cuda):
     return cfg, t, host_weights(t)
 
 
+@pytest.mark.parametrize("tc", [False, True], ids=["cuda_cores", "tensor_cores"])
 @pytest.mark.parametrize("T", [1, 4, 8, 16])
-def test_config1_layer_bf16(cuda, c1_layer, T):
+def test_config1_layer_bf16(cuda, c1_layer, T, tc):
     import torch
     cfg, t, hw = c1_layer
-    plan = M.Plan(cfg.dims(layers=1), max_rows=16, renormalize=True)
+    plan = M.Plan(cfg.dims(layers=1), max_rows=16, renormalize=True, flags=M.PLAN_TENSOR_DECODE if tc else 0)
     C.load_layer(plan, cfg, 0, t)
     x = C.device_input(cfg, T)
     y, ids, _ = run_plan(plan, 0, x, cfg.top_k, torch)
@@ -209,6 +217,36 @@ def test_stack_residual_two_layers(cuda):
     for t in layers:
         want = want + O.moe_forward(host_weights(t), want, cfg.top_k, renormalize=True).y
     assert max_rel(to_np(h), want) <= BF16_TOL
+
+
+@pytest.mark.parametrize("tc", [False, True], ids=["cuda_cores", "tensor_cores"])
+def test_stack_graph_replay_matches_plain_launches(cuda, tc):
+    """forward_stack on a capturable stream is captured once (with programmatic
+    dependent launches between the kernels) and replayed; the replays give the
+    bits of plain stream-ordered launches."""
+    import torch
+    cfg = C.CONFIGS[1]
+    layers = [C.device_layer(cfg, l) for l in range(3)]
+    extra = M.PLAN_TENSOR_DECODE if tc else 0
+    graphed = M.Plan(cfg.dims(layers=3), max_rows=8, flags=extra)
+    plain = M.Plan(cfg.dims(layers=3), max_rows=8, flags=extra | M.PLAN_NO_GRAPHS)
+    for l, t in enumerate(layers):
+        C.load_layer(graphed, cfg, l, t)
+        C.load_layer(plain, cfg, l, t)
+    x = C.device_input(cfg, 8)
+    s = torch.cuda.Stream()
+    h1 = x.clone()
+    h2 = x.clone()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for h in (h1, h2):
+            for _ in range(3):  # capture, then two replays on the same buffer
+                h.copy_(x)
+                graphed.forward_stack(h, stream=s) if h is h1 else plain.forward_stack(h, stream=s)
+    torch.cuda.synchronize()
+    graphed.check()
+    plain.check()
+    assert torch.equal(h1, h2)
 
 
 def test_forward_is_deterministic(cuda, c1_layer):
