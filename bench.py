@@ -184,56 +184,90 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu):
-    """BASELINE config 3 on one GPU: one MoE layer over 32768 rows (8 pages x
-    4096), Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and
-    the gate/up GEMM against the bf16 tensor roofline."""
+def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0):
+    """one MoE layer over 32768 rows (8 pages x 4096),
+    Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and the
+    gate/up GEMM against the bf16 tensor roofline. With world > 1 the layer
+    runs expert-parallel: each rank holds 64 / world experts and 32768 / world
+    rows (strong scaling), and the time is the max over ranks. `rows` shrinks
+    the batch (profiling captures only)."""
     import torch
     cfg = C.CONFIGS[3]
-    T = cfg.rows[0]
-    plan = M.Plan(cfg.dims(), max_rows=T, router_bias=True, device=dev.index or 0)
+    total = rows or cfg.rows[0]
+    import ep
+    start, T = ep.rows_of(total, world, rank)
+    plan = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0,
+                  ep_world=world if world > 1 else 0, ep_rank=rank)
     t = C.device_layer(cfg, 0, device=dev)
     C.load_layer(plan, cfg, 0, t)
-    x = C.device_input(cfg, T, device=dev)
+    if world > 1:
+        ep.connect(plan)
+    x = C.device_input(cfg, total, device=dev)[start:start + T].contiguous()
     y = torch.empty_like(x)
     ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
+    if world > 1:
+        import torch.distributed as dist
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             plan.forward(0, x, y, ids, stream=stream)
         plan.check(stream=stream)
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start_ev = torch.cuda.Event(enable_timing=True)
+        end_ev = torch.cuda.Event(enable_timing=True)
+        start_ev.record(stream)
         for _ in range(steps):
             plan.forward(0, x, y, stream=stream)
-        end.record(stream)
+        end_ev.record(stream)
         torch.cuda.synchronize()
-        ms = start.elapsed_time(end) / steps
+        ms = start_ev.elapsed_time(end_ev) / steps
+        if world > 1:
+            dist.barrier()
         h = x.clone()
         prof = plan.profile_stack(h, iters=3, stream=stream)
         plan.check(stream=stream)
-    counts = torch.bincount(ids.view(-1).long(), minlength=cfg.experts).cpu().tolist()
+    counts_t = torch.bincount(ids.view(-1).long(), minlength=cfg.experts)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(counts_t)
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms = float(ms_t[0])
+    counts = counts_t.cpu().tolist()
     H, F, S = cfg.hidden, cfg.ffn, cfg.shared_ffn
-    R = T * cfg.top_k
-    gu_flops = R * 4 * F * H + T * 4 * S * H
-    dn_flops = R * 2 * F * H + T * 2 * S * H
-    total_flops = gu_flops + dn_flops + 2 * T * cfg.experts * H
+    R = total * cfg.top_k
+    gu_flops = R * 4 * F * H + total * 4 * S * H
+    dn_flops = R * 2 * F * H + total * 2 * S * H
+    total_flops = gu_flops + dn_flops + 2 * total * cfg.experts * H
     peak, peak_src = measured_tensor_peak()
-    gu_tf = gu_flops / (prof["gate_up_gemm"] * 1e-3) / 1e12
-    dn_tf = dn_flops / (prof["down_gemm"] * 1e-3) / 1e12
     out = {
-        "workload": f"{cfg.name}: 1 layer, {T} rows (8 pages x 4096), Zipf(1.2)-biased router, bf16",
-        "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_layer": ms,
+        "workload": f"{cfg.name}: 1 layer, {total} rows" + (" (8 pages x 4096)" if total == 32768 else "")
+                    + ", Zipf(1.2)-biased router, bf16",
+        "value": total / (ms * 1e-3), "unit": "tokens/s", "ms_per_layer": ms, "n_gpus": world,
+        "scaling": "strong" if world > 1 else None,
         "tflops_per_layer": total_flops / (ms * 1e-3) / 1e12,
         "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
-        "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (tcgen05 grouped, SwiGLU fused)", "achieved": gu_tf,
-                     "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s", "frac": gu_tf / peak,
-                     "down_gemm_achieved": dn_tf, "down_gemm_frac": dn_tf / peak,
-                     "algorithmic_flops_per_layer": total_flops},
         "expert_rows": counts, "top_expert_share": max(counts) / R,
     }
+    if world == 1:
+        gu_tf = gu_flops / (prof["gate_up_gemm"] * 1e-3) / 1e12
+        dn_tf = dn_flops / (prof["down_gemm"] * 1e-3) / 1e12
+        out["roofline"] = {"bound": "tensor", "kernel": "gate_up_gemm (tcgen05 grouped, SwiGLU fused)",
+                           "achieved": gu_tf, "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
+                           "frac": gu_tf / peak, "down_gemm_achieved": dn_tf, "down_gemm_frac": dn_tf / peak,
+                           "algorithmic_flops_per_layer": total_flops}
+    else:
+        per_gpu = total_flops / (ms * 1e-3) / 1e12 / world
+        owner_rows = [sum(counts[e] for e in ep.local_experts(r, cfg.experts, world)) for r in range(world)]
+        out["parallelism"] = f"expert-parallel x{world}: {cfg.experts // world} experts and {total // world} rows " \
+                             "per GPU; rows and outputs pulled over NVLink by peer loads"
+        out["roofline"] = {"bound": "tensor", "kernel": "whole layer per GPU", "achieved": per_gpu, "peak": peak,
+                           "peak_source": peak_src, "unit": "TFLOP/s", "frac": per_gpu / peak,
+                           "algorithmic_flops_per_layer": total_flops}
+        out["rows_received_per_rank"] = owner_rows
     if want_cpu:
-        cpu_rows = 512
+        cpu_rows = min(512, T)
         hw = host_layer_weights(cfg)
         hw.router_bias = t["router_bias"].cpu().numpy()
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -301,6 +335,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill section")
+    ap.add_argument("--prefill-rows", type=int, default=None, help="shrink the prefill batch (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -418,10 +453,11 @@ def main():
     traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
 
     prefill = None
-    if world == 1 and not args.no_prefill:
+    if not args.no_prefill:
         plan.close()  # free the decode stack's 20 GB first
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
-                              want_cpu=not args.no_cpu_baseline)
+                              want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
+                              rows=args.prefill_rows, world=world, rank=rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

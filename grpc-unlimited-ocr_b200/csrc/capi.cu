@@ -16,6 +16,7 @@
 
 #include "../../include/uocr_moe.h"
 #include "decode_tc.h"
+#include "ep.h"
 #include "moe_kernels.h"
 #include "prefill.h"
 
@@ -116,6 +117,17 @@ struct uocr_moe_plan {
   // bf16 decode batches on the tensor cores.
   bool decode_tc = false;
   DecodeTcScratch dtc{};
+  // Expert parallelism (ep_world > 1): this rank's exchange region, the peers'
+  // (IPC mappings, closed on destroy) and the EP scratch in the arena.
+  bool ep = false;
+  EpMap emap{};
+  EpLayout elay{};
+  EpScratch escr{};
+  EpPeers epeers{};
+  char* exchange = nullptr;
+  std::vector<char*> opened;
+  bool ep_connected = false;
+  bool ep_local_group = false;
 
   // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
   struct GraphEntry {
@@ -131,10 +143,14 @@ struct uocr_moe_plan {
 
   size_t elem_bytes() const { return d.weight_format == UOCR_WEIGHT_INT8 ? 1 : 2; }
 
+  // Routed experts whose weights this plan holds (its own under expert parallelism).
+  int64_t held_experts() const { return ep ? emap.local : d.routed_experts; }
+
   void carve_layer(Carver& c, LayerDev& L) const {
-    const size_t H = d.hidden, E = d.routed_experts, F = d.expert_ffn, S = d.shared_ffn, eb = elem_bytes();
-    L.router = c.take<float>(E * H);
-    L.bias = d.router_bias ? c.take<float>(E) : nullptr;
+    const size_t H = d.hidden, F = d.expert_ffn, S = d.shared_ffn, eb = elem_bytes();
+    const size_t E = static_cast<size_t>(held_experts());
+    L.router = c.take<float>(static_cast<size_t>(d.routed_experts) * H);
+    L.bias = d.router_bias ? c.take<float>(static_cast<size_t>(d.routed_experts)) : nullptr;
     L.gate = c.take<char>(E * F * H * eb);
     L.up = c.take<char>(E * F * H * eb);
     L.down = c.take<char>(E * H * F * eb);
@@ -163,8 +179,12 @@ struct uocr_moe_plan {
     counter = c.take<unsigned>(1);
     err = c.take<ErrorWord>(1);
     if (prefill) {
-      char* base = c.take<char>(prefill_scratch_bytes(pdims));
-      carve_prefill_scratch(pdims, base, &pscratch);
+      char* base = c.take<char>(prefill_scratch_bytes(pdims, !ep));
+      carve_prefill_scratch(pdims, base, &pscratch, !ep);
+    }
+    if (ep) {
+      char* base = c.take<char>(ep_scratch_bytes(pdims, elay, emap));
+      carve_ep_scratch(pdims, elay, emap, base, &escr);
     }
     if (decode_tc) {
       const int H = static_cast<int>(d.hidden), F = static_cast<int>(d.expert_ffn), S = static_cast<int>(d.shared_ffn);
@@ -235,6 +255,20 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: layers and max_rows must be positive");
   if (d.weight_format != UOCR_WEIGHT_BF16 && d.weight_format != UOCR_WEIGHT_INT8)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: weight_format must be bf16 (0) or int8 (1)");
+  const bool ep = d.ep_world > 1;
+  if (d.ep_world < 0 || d.ep_world > kMaxEpRanks)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: ep_world must be in [0, 8]");
+  if (ep) {
+    if (d.ep_rank < 0 || d.ep_rank >= d.ep_world)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: ep_rank must be in [0, ep_world)");
+    if (d.routed_experts % d.ep_world != 0)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: routed_experts must be a multiple of ep_world");
+    if (d.weight_format != UOCR_WEIGHT_BF16 ||
+        !prefill_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn), static_cast<int>(d.shared_ffn)))
+      return fail(UOCR_ERR_UNSUPPORTED,
+                  "plan_create: expert parallelism runs the prefill path: bf16 weights, hidden % 256 == 0, "
+                  "expert_ffn and shared_ffn % 128 == 0");
+  }
   int ndev = 0;
   UOCR_TRY(cudaGetDeviceCount(&ndev), "plan_create: cudaGetDeviceCount");
   if (d.device < 0 || d.device >= ndev) return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: no such device");
@@ -248,7 +282,8 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
            "plan_create: shared memory limit");
   // The decode kernels stage the batch's rows in shared memory (the router
   // also holds ~5 KB of static shared memory of its own).
-  int dr = static_cast<int>(d.max_rows < kDecodeMaxRows ? d.max_rows : kDecodeMaxRows);
+  // (An expert-parallel plan runs every row count through the prefill path.)
+  int dr = ep ? 0 : static_cast<int>(d.max_rows < kDecodeMaxRows ? d.max_rows : kDecodeMaxRows);
   while (dr > 0 && (static_cast<size_t>(d.hidden) + static_cast<size_t>(dr) * (d.hidden + 8)) * 4 + 8192 >
                        static_cast<size_t>(smem_optin))
     --dr;
@@ -269,6 +304,13 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   p->pdims = PrefillDims{static_cast<int>(d.max_rows), static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
                          static_cast<int>(d.experts_per_token), static_cast<int>(d.expert_ffn),
                          static_cast<int>(d.shared_ffn), d.renormalize};
+  if (ep) {
+    p->ep = true;
+    const int W = d.ep_world;
+    p->emap = EpMap{W, d.ep_rank, static_cast<int>(d.routed_experts), static_cast<int>(d.routed_experts) / W,
+                    (d.flags & UOCR_PLAN_EP_STRIDED) != 0 ? 1 : 0};
+    p->elay = ep_layout(p->pdims, p->emap);
+  }
   p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
                  decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
                                      static_cast<int>(d.shared_ffn));
@@ -304,6 +346,20 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     uocr_moe_plan_destroy(p);
     return cuda_fail(st, "plan_create: arena clear");
   }
+  if (p->ep) {
+    // A block of its own: CUDA IPC exports whole cudaMalloc allocations.
+    st = cudaMalloc(&p->exchange, p->elay.bytes);
+    if (st == cudaSuccess) st = cudaMemset(p->exchange, 0, p->elay.bytes);
+    if (st != cudaSuccess) {
+      uocr_moe_plan_destroy(p);
+      return cuda_fail(st, "plan_create: exchange region");
+    }
+    p->arena_bytes += p->elay.bytes;
+    p->pscratch.seg_count = reinterpret_cast<int*>(p->exchange + p->elay.seg_count);
+    p->pscratch.seg_start = reinterpret_cast<int*>(p->exchange + p->elay.seg_start);
+    p->pscratch.xperm = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.xperm);
+    p->epeers.base[p->emap.rank] = p->exchange;
+  }
   *out = p;
   return UOCR_OK;
 }
@@ -315,6 +371,8 @@ int uocr_moe_plan_destroy(uocr_moe_plan* p) {
   for (auto& L : p->layers)
     if (L.block != nullptr) cudaFree(L.block);
   if (p->arena != nullptr) cudaFree(p->arena);
+  for (char* q : p->opened) cudaIpcCloseMemHandle(q);
+  if (p->exchange != nullptr) cudaFree(p->exchange);
   delete p;
   return UOCR_OK;
 }
@@ -385,9 +443,29 @@ int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src
   const int64_t H = p->d.hidden, E = p->d.routed_experts, F = p->d.expert_ffn, S = p->d.shared_ffn;
   int rc = copy_f32(*src, src->router, L.router, static_cast<size_t>(E * H), stream, "router");
   if (rc == UOCR_OK && p->d.router_bias) rc = copy_f32(*src, src->router_bias, L.bias, E, stream, "router_bias");
-  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->gate, E * F, H, L.gate, L.gate_s, stream, "gate");
-  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->up, E * F, H, L.up, L.up_s, stream, "up");
-  if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->down, E * H, F, L.down, L.down_s, stream, "down");
+  if (!p->ep) {
+    if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->gate, E * F, H, L.gate, L.gate_s, stream, "gate");
+    if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->up, E * F, H, L.up, L.up_s, stream, "up");
+    if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->down, E * H, F, L.down, L.down_s, stream, "down");
+  } else {
+    // Expert parallelism: only this rank's experts, from the full stacks.
+    const size_t sb = src->dtype == UOCR_DTYPE_BF16 ? 2 : 4, eb = p->elem_bytes();
+    auto at = [](const void* base, size_t bytes) {
+      return base == nullptr ? nullptr : static_cast<const char*>(base) + bytes;
+    };
+    for (int i = 0; i < p->emap.local && rc == UOCR_OK; ++i) {
+      const int64_t e = p->emap.global(p->emap.rank, i);
+      char* g = static_cast<char*>(L.gate) + static_cast<size_t>(i * F * H) * eb;
+      char* u = static_cast<char*>(L.up) + static_cast<size_t>(i * F * H) * eb;
+      char* dn = static_cast<char*>(L.down) + static_cast<size_t>(i * H * F) * eb;
+      rc = upload_matrix(p, *src, at(src->gate, static_cast<size_t>(e * F * H) * sb), F, H, g, nullptr, stream, "gate");
+      if (rc == UOCR_OK)
+        rc = upload_matrix(p, *src, at(src->up, static_cast<size_t>(e * F * H) * sb), F, H, u, nullptr, stream, "up");
+      if (rc == UOCR_OK)
+        rc = upload_matrix(p, *src, at(src->down, static_cast<size_t>(e * H * F) * sb), H, F, dn, nullptr, stream,
+                           "down");
+    }
+  }
   if (rc == UOCR_OK && S > 0) {
     rc = upload_matrix(p, *src, src->shared_gate, S, H, L.sgate, L.sgate_s, stream, "shared_gate");
     if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->shared_up, S, H, L.sup, L.sup_s, stream, "shared_up");
@@ -403,6 +481,47 @@ namespace {
 
 constexpr int kMaxProfileKernels = 6;
 
+const __nv_bfloat16* as_bf16(void* v) { return static_cast<const __nv_bfloat16*>(v); }
+
+PrefillCall prefill_call(const uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows, const float* resid,
+                         float* y) {
+  PrefillCall c{};
+  c.dims = p->pdims;
+  c.scratch = p->pscratch;
+  c.rows = static_cast<int>(rows);
+  c.x = x;
+  c.router = L.router;
+  c.bias = L.bias;
+  c.gate = as_bf16(L.gate);
+  c.up = as_bf16(L.up);
+  c.down = as_bf16(L.down);
+  c.sgate = as_bf16(L.sgate);
+  c.sup = as_bf16(L.sup);
+  c.sdown = as_bf16(L.sdown);
+  c.logits = p->logits;
+  c.ids = p->ids;
+  c.weights = p->weights;
+  c.resid = resid;
+  c.y = y;
+  c.err = p->err;
+  c.sm_count = p->sm_count;
+  c.events = nullptr;
+  return c;
+}
+
+EpCall ep_call(const uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows, const float* resid, float* y) {
+  EpCall c{};
+  c.pc = prefill_call(p, L, x, rows, resid, y);
+  c.map = p->emap;
+  c.peers = p->epeers;
+  c.lay = p->elay;
+  c.es = p->escr;
+  c.gate_local = as_bf16(L.gate);
+  c.up_local = as_bf16(L.up);
+  c.down_local = as_bf16(L.down);
+  return c;
+}
+
 // One layer on `rows` rows: route, then experts. resid != null adds the
 // layer input back (the stack's residual); y may then alias resid. For
 // measurement, ev (kMaxProfileKernels events) receives one event after each
@@ -413,32 +532,18 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts),
             K = static_cast<int>(d.experts_per_token), F = static_cast<int>(d.expert_ffn),
             S = static_cast<int>(d.shared_ffn);
+  if (p->ep) {
+    EpCall c = ep_call(p, L, x, rows, resid, y);
+    UOCR_TRY(ep_forward(c, stream, ev), "forward: expert-parallel prefill");
+    if (nev != nullptr) *nev = 5;
+    return UOCR_OK;
+  }
   if (rows > p->decode_rows) {
     if (!p->prefill)
       return fail(UOCR_ERR_UNSUPPORTED,
                   "forward: more than 16 rows needs the prefill path: bf16 weights, hidden % 256 == 0, "
                   "expert_ffn and shared_ffn % 128 == 0");
-    auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
-    PrefillCall c{};
-    c.dims = p->pdims;
-    c.scratch = p->pscratch;
-    c.rows = T;
-    c.x = x;
-    c.router = L.router;
-    c.bias = L.bias;
-    c.gate = b(L.gate);
-    c.up = b(L.up);
-    c.down = b(L.down);
-    c.sgate = b(L.sgate);
-    c.sup = b(L.sup);
-    c.sdown = b(L.sdown);
-    c.logits = p->logits;
-    c.ids = p->ids;
-    c.weights = p->weights;
-    c.resid = resid;
-    c.y = y;
-    c.err = p->err;
-    c.sm_count = p->sm_count;
+    PrefillCall c = prefill_call(p, L, x, rows, resid, y);
     c.events = ev;
     UOCR_TRY(launch_prefill(c, stream), "forward: prefill");
     if (nev != nullptr) *nev = 6;
@@ -496,14 +601,30 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
 
 }  // namespace
 
+namespace {
+
+// An expert-parallel plan forwards only once connected, and virtual ranks of
+// a local group only through uocr_moe_ep_forward_local.
+int ep_ready(const uocr_moe_plan* p, const char* what) {
+  if (!p->ep) return UOCR_OK;
+  if (!p->ep_connected)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, std::string(what) + ": expert-parallel plan not connected");
+  if (p->ep_local_group)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, std::string(what) + ": local-group ranks run through ep_forward_local");
+  return UOCR_OK;
+}
+
+}  // namespace
+
 int uocr_moe_forward(uocr_moe_plan* p, int64_t layer, const float* x, int64_t rows, float* y, int32_t* ids,
                      float* weights, void* stream_v) {
   if (p == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null plan");
   if (layer < 0 || layer >= p->d.layers) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: layer out of range");
   if (rows < 0 || rows > p->d.max_rows) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: rows outside [0, max_rows]");
-  if (rows == 0) return UOCR_OK;
-  if (x == nullptr || y == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null x or y");
-  if (x == y) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: x and y must not overlap");
+  if (int rc = ep_ready(p, "forward"); rc != UOCR_OK) return rc;
+  if (rows == 0 && !p->ep) return UOCR_OK;  // an expert-parallel rank takes part with no rows
+  if (rows > 0 && (x == nullptr || y == nullptr)) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null x or y");
+  if (rows > 0 && x == y) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: x and y must not overlap");
   const LayerDev& L = p->layers[static_cast<size_t>(layer)];
   if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: layer weights not set");
   DeviceGuard guard(p->d.device);
@@ -519,10 +640,12 @@ int uocr_moe_forward(uocr_moe_plan* p, int64_t layer, const float* x, int64_t ro
 }
 
 int uocr_moe_forward_stack(uocr_moe_plan* p, float* h, int64_t rows, void* stream_v) {
-  if (p == nullptr || h == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: null argument");
+  if (p == nullptr || (h == nullptr && rows > 0))
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: null argument");
   if (rows < 0 || rows > p->d.max_rows)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: rows outside [0, max_rows]");
-  if (rows == 0) return UOCR_OK;
+  if (int rc = ep_ready(p, "forward_stack"); rc != UOCR_OK) return rc;
+  if (rows == 0 && !p->ep) return UOCR_OK;
   for (const auto& L : p->layers)
     if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: a layer's weights are not set");
   DeviceGuard guard(p->d.device);
@@ -578,6 +701,7 @@ int uocr_moe_profile_stack(uocr_moe_plan* p, float* h, int64_t rows, int32_t ite
     return fail(UOCR_ERR_INVALID_ARGUMENT, "profile_stack: rows outside [1, max_rows]");
   for (const auto& L : p->layers)
     if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "profile_stack: a layer's weights are not set");
+  if (int rc = ep_ready(p, "profile_stack"); rc != UOCR_OK) return rc;
   DeviceGuard guard(p->d.device);
   auto stream = static_cast<cudaStream_t>(stream_v);
   const size_t nl = p->layers.size();
@@ -625,6 +749,154 @@ int uocr_moe_check(uocr_moe_plan* p, void* stream_v) {
   char buf[160];
   std::snprintf(buf, sizeof(buf), "device error %d at site %d (%d, %d)", e.code, e.where, e.a, e.b);
   return fail(e.code == kDevWaitTimeout ? UOCR_ERR_TIMEOUT : UOCR_ERR_DEVICE, buf);
+}
+
+// ---- expert parallelism ----------------------------------------------------
+
+namespace {
+
+constexpr uint32_t kEpMagic = 0x31504555u;  // "UEP1"
+
+// What a rank's handle carries besides its IPC handle: enough to refuse
+// plans that do not fit together.
+struct EpFingerprint {
+  uint32_t magic;
+  int32_t world, rank, strided;
+  unsigned char uuid[16];
+  int64_t hidden, experts, top_k, ffn, shared_ffn, max_rows, layers;
+  uint64_t region_bytes;
+};
+static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(EpFingerprint) <= sizeof(uocr_ep_handle), "handle size");
+
+EpFingerprint fingerprint(const uocr_moe_plan* p) {
+  EpFingerprint f{};
+  f.magic = kEpMagic;
+  f.world = p->emap.world;
+  f.rank = p->emap.rank;
+  f.strided = p->emap.strided;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, p->d.device) == cudaSuccess) std::memcpy(f.uuid, &prop.uuid, 16);
+  f.hidden = p->d.hidden;
+  f.experts = p->d.routed_experts;
+  f.top_k = p->d.experts_per_token;
+  f.ffn = p->d.expert_ffn;
+  f.shared_ffn = p->d.shared_ffn;
+  f.max_rows = p->d.max_rows;
+  f.layers = p->d.layers;
+  f.region_bytes = p->elay.bytes;
+  return f;
+}
+
+bool same_shape(const EpFingerprint& a, const EpFingerprint& b) {
+  return a.magic == b.magic && a.world == b.world && a.strided == b.strided && a.hidden == b.hidden &&
+         a.experts == b.experts && a.top_k == b.top_k && a.ffn == b.ffn && a.shared_ffn == b.shared_ffn &&
+         a.max_rows == b.max_rows && a.layers == b.layers && a.region_bytes == b.region_bytes;
+}
+
+}  // namespace
+
+int uocr_moe_ep_handle(uocr_moe_plan* p, uocr_ep_handle* out) {
+  if (p == nullptr || out == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_handle: null argument");
+  if (!p->ep) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_handle: the plan has ep_world <= 1");
+  DeviceGuard guard(p->d.device);
+  std::memset(out, 0, sizeof(*out));
+  cudaIpcMemHandle_t h{};
+  UOCR_TRY(cudaIpcGetMemHandle(&h, p->exchange), "ep_handle: cudaIpcGetMemHandle");
+  const EpFingerprint f = fingerprint(p);
+  std::memcpy(out->bytes, &h, sizeof(h));
+  std::memcpy(out->bytes + sizeof(h), &f, sizeof(f));
+  return UOCR_OK;
+}
+
+int uocr_moe_ep_connect(uocr_moe_plan* p, const uocr_ep_handle* handles) {
+  if (p == nullptr || handles == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect: null argument");
+  if (!p->ep) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect: the plan has ep_world <= 1");
+  if (p->ep_connected) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect: already connected");
+  DeviceGuard guard(p->d.device);
+  const EpFingerprint mine = fingerprint(p);
+  const int W = p->emap.world;
+  for (int s = 0; s < W; ++s) {
+    EpFingerprint f{};
+    std::memcpy(&f, handles[s].bytes + sizeof(cudaIpcMemHandle_t), sizeof(f));
+    if (!same_shape(f, mine) || f.rank != s)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect: handle " + std::to_string(s) +
+                                                 " is not rank " + std::to_string(s) + " of a plan of the same shape");
+    if (s != p->emap.rank && std::memcmp(f.uuid, mine.uuid, 16) == 0)
+      return fail(UOCR_ERR_UNSUPPORTED, "ep_connect: ranks " + std::to_string(s) + " and " +
+                                            std::to_string(p->emap.rank) +
+                                            " share a GPU; use uocr_moe_ep_connect_local for virtual ranks");
+  }
+  EpPeers peers = p->epeers;
+  std::vector<char*> opened;
+  for (int s = 0; s < W; ++s) {
+    if (s == p->emap.rank) continue;
+    cudaIpcMemHandle_t h{};
+    std::memcpy(&h, handles[s].bytes, sizeof(h));
+    void* q = nullptr;
+    const cudaError_t st = cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess);
+    if (st != cudaSuccess) {
+      for (char* o : opened) cudaIpcCloseMemHandle(o);
+      return fail(UOCR_ERR_COMM, std::string("ep_connect: opening rank ") + std::to_string(s) +
+                                     "'s memory: " + cudaGetErrorString(st));
+    }
+    opened.push_back(static_cast<char*>(q));
+    peers.base[s] = static_cast<char*>(q);
+  }
+  p->opened = std::move(opened);
+  p->epeers = peers;
+  p->ep_connected = true;
+  return UOCR_OK;
+}
+
+int uocr_moe_ep_connect_local(uocr_moe_plan* const* plans, int32_t n) {
+  if (plans == nullptr || n < 2 || n > kMaxEpRanks)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect_local: need 2..8 plans");
+  for (int i = 0; i < n; ++i) {
+    const uocr_moe_plan* q = plans[i];
+    if (q == nullptr || !q->ep || q->emap.world != n || q->emap.rank != i || q->ep_connected)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect_local: plan " + std::to_string(i) +
+                                                 " is not an unconnected rank " + std::to_string(i) + " of " +
+                                                 std::to_string(n));
+    if (q->d.device != plans[0]->d.device || !same_shape(fingerprint(q), fingerprint(plans[0])))
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_connect_local: plans differ in device or shape");
+  }
+  EpPeers peers{};
+  for (int i = 0; i < n; ++i) peers.base[i] = plans[i]->exchange;
+  for (int i = 0; i < n; ++i) {
+    plans[i]->epeers = peers;
+    plans[i]->ep_connected = true;
+    plans[i]->ep_local_group = true;
+  }
+  return UOCR_OK;
+}
+
+int uocr_moe_ep_forward_local(uocr_moe_plan* const* plans, int32_t n, int64_t layer, const float* const* x,
+                              const int64_t* rows, float* const* y, void* stream_v) {
+  if (plans == nullptr || x == nullptr || rows == nullptr || y == nullptr || n < 2 || n > kMaxEpRanks)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: bad argument");
+  std::vector<EpCall> calls;
+  for (int i = 0; i < n; ++i) {
+    uocr_moe_plan* q = plans[i];
+    if (q == nullptr || !q->ep_local_group || q->emap.rank != i || q->emap.world != n)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: plans are not one local group in rank order");
+    if (layer < 0 || layer >= q->d.layers) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: bad layer");
+    if (rows[i] < 0 || rows[i] > q->d.max_rows)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: rows outside [0, max_rows]");
+    if (rows[i] > 0 && (x[i] == nullptr || y[i] == nullptr || x[i] == y[i]))
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: null or overlapping x, y");
+    const LayerDev& L = q->layers[static_cast<size_t>(layer)];
+    if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: layer weights not set");
+    calls.push_back(ep_call(q, L, x[i], rows[i], nullptr, y[i]));
+  }
+  DeviceGuard guard(plans[0]->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  // Each phase for every rank before the next phase: stream order stands in
+  // for the barriers.
+  for (auto& c : calls) UOCR_TRY(ep_route(c, stream), "ep_forward_local: route");
+  for (auto& c : calls) UOCR_TRY(ep_experts(c, stream), "ep_forward_local: experts");
+  for (auto& c : calls) UOCR_TRY(ep_shared(c, stream), "ep_forward_local: shared");
+  for (auto& c : calls) UOCR_TRY(ep_combine(c, stream), "ep_forward_local: combine");
+  return UOCR_OK;
 }
 
 // ---- op-level mirrors ----------------------------------------------------

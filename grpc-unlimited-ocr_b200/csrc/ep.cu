@@ -1,0 +1,353 @@
+// Expert-parallel prefill: the exchange between the route and expert phases,
+// the combine over the owners' outputs, and the barrier between the ranks'
+// exchange regions. Everything crosses NVLink as plain peer loads (and the
+// barrier's peer stores); no TMA reads peer memory — the grouped GEMMs read
+// only this GPU's xrecv / act.
+#include "ep.h"
+
+#include "moe_kernels.h"
+#include "ptx.cuh"
+
+namespace uocr_b200 {
+namespace {
+
+constexpr uint64_t kEpWaitNs = 20ull * 1000 * 1000 * 1000;
+constexpr uint32_t kEpWaitPolls = 1u << 27;
+
+__device__ __forceinline__ int ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_cg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Every rank's per-expert counts and starts (peer loads), the receive layout
+// of every rank's experts, and where this rank's selections land in the
+// owners' yrecv. One block.
+__global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es,
+                                                         ErrorWord* err) {
+  __shared__ int cnt[kMaxEpRanks][kMaxExperts];
+  __shared__ int tot[kMaxExperts];     // [d * local + i] rows expert i of rank d receives
+  __shared__ int rstart[kMaxExperts];  // [d * local + i] its first row in rank d's yrecv
+  __shared__ int overflow;
+  const int W = m.world, E = m.experts, L = m.local;
+  if (threadIdx.x == 0) overflow = 0;
+  for (int idx = threadIdx.x; idx < W * E; idx += blockDim.x) {
+    const int s = idx / E, e = idx % E;
+    const int c = ld_relaxed_sys(reinterpret_cast<const int*>(peers.base[s] + lay.seg_count) + e);
+    const int st = ld_relaxed_sys(reinterpret_cast<const int*>(peers.base[s] + lay.seg_start) + e);
+    cnt[s][e] = c;
+    es.cnt_all[idx] = c;
+    es.seg_start_all[idx] = st;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < W * L; q += blockDim.x) {
+    const int e = m.global(q / L, q % L);
+    int t = 0;
+    for (int s = 0; s < W; ++s) t += cnt[s][e];
+    tot[q] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < W) {
+    const int d = threadIdx.x;
+    int64_t acc = 0;
+    for (int i = 0; i < L; ++i) {
+      rstart[d * L + i] = static_cast<int>(acc);
+      acc += tot[d * L + i];
+    }
+    if (acc > lay.max_recv) {
+      raise_error(err, kDevCapacity, 60, d, static_cast<int>(acc));
+      atomicExch(&overflow, 1);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    // On overflow nothing is received (the error word reports it).
+    es.recv_count[i] = overflow ? 0 : tot[m.rank * L + i];
+    es.recv_start[i] = overflow ? 0 : rstart[m.rank * L + i];
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int d = m.owner(e), i = m.local_index(e);
+    int b = rstart[d * L + i];
+    for (int s = 0; s < m.rank; ++s) b += cnt[s][e];
+    es.remote_base[e] = b - es.seg_start_all[m.rank * E + e];
+  }
+}
+
+// xrecv rows of this rank's experts: expert-major, then source rank, each
+// (expert, source) segment a contiguous run of the source's xperm. One warp
+// per row, grid-stride; 16-byte peer loads, all of a row in flight at once.
+__global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es, int H) {
+  __shared__ int seg_dst[kMaxExperts];
+  __shared__ int seg_src[kMaxExperts];
+  __shared__ int seg_rank[kMaxExperts];
+  __shared__ int total;
+  const int W = m.world, L = m.local, E = m.experts, n = W * L;
+  for (int q = threadIdx.x; q < n; q += blockDim.x) {
+    const int i = q / W, s = q % W, e = m.global(m.rank, i);
+    int d = es.recv_start[i];
+    for (int s2 = 0; s2 < s; ++s2) d += es.cnt_all[s2 * E + e];
+    seg_dst[q] = d;
+    seg_src[q] = es.seg_start_all[s * E + e];
+    seg_rank[q] = s;
+  }
+  if (threadIdx.x == 0) total = es.recv_start[L - 1] + es.recv_count[L - 1];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int nch = H / 8;  // 16-byte chunks per row
+  for (int r = warp; r < total; r += nwarps) {
+    int lo = 0, hi = n - 1;  // last segment starting at or before r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seg_dst[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t src_row = seg_src[lo] + (r - seg_dst[lo]);
+    const uint4* src = reinterpret_cast<const uint4*>(peers.base[seg_rank[lo]] + lay.xperm) + src_row * nch;
+    uint4* dst = reinterpret_cast<uint4*>(es.xrecv) + static_cast<int64_t>(r) * nch;
+    for (int c0 = 0; c0 < nch; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = c0 + lane + 32 * u;
+        if (idx < nch) v[u] = ld_cg16(src + idx);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = c0 + lane + 32 * u;
+        if (idx < nch) dst[idx] = v[u];
+      }
+    }
+  }
+}
+
+// y[t, c] = shared[t, c] + sum over t's experts in ascending id of w * (the
+// owner's yrecv row), + resid: the single-GPU combine's additions in the same
+// order, with the rows read from the owners. One block per row.
+__global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, EpMap m, EpPeers peers, EpLayout lay,
+                                                         const int* __restrict__ ids,
+                                                         const float* __restrict__ weights,
+                                                         const int* __restrict__ pos_of,
+                                                         const int* __restrict__ remote_base,
+                                                         const float* shared_out, const float* resid, float* y) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  int eid[kMaxTopK];
+  int64_t row[kMaxTopK];
+  float w[kMaxTopK];
+  for (int j = 0; j < K; ++j) {
+    eid[j] = ids[static_cast<int64_t>(t) * K + j];
+    w[j] = weights[static_cast<int64_t>(t) * K + j];
+    const int p = pos_of[static_cast<int64_t>(t) * K + j];
+    row[j] = (p < 0 || eid[j] < 0 || eid[j] >= m.experts) ? -1 : static_cast<int64_t>(remote_base[eid[j]]) + p;
+  }
+  for (int a = 1; a < K; ++a)
+    for (int b = a; b > 0 && eid[b] < eid[b - 1]; --b) {
+      const int te = eid[b];
+      const int64_t tr = row[b];
+      const float tw = w[b];
+      eid[b] = eid[b - 1];
+      row[b] = row[b - 1];
+      w[b] = w[b - 1];
+      eid[b - 1] = te;
+      row[b - 1] = tr;
+      w[b - 1] = tw;
+    }
+  const __nv_bfloat16* src[kMaxTopK];
+  for (int j = 0; j < K; ++j)
+    src[j] = row[j] < 0 ? nullptr
+                        : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner(eid[j])] + lay.yrecv) + row[j] * H;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 pk[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+      if (j < K && src[j] != nullptr) pk[j] = ld_cg16(src[j] + c);
+    float routed[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j >= K || src[j] == nullptr) continue;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        routed[2 * q] = __fadd_rn(routed[2 * q], __fmul_rn(w[j], f.x));
+        routed[2 * q + 1] = __fadd_rn(routed[2 * q + 1], __fmul_rn(w[j], f.y));
+      }
+    }
+    const int64_t o = static_cast<int64_t>(t) * H + c;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float sh = shared_out != nullptr ? shared_out[o + q] : 0.0f;
+      float out = __fadd_rn(sh, routed[q]);
+      if (resid != nullptr) out = __fadd_rn(resid[o + q], out);
+      y[o + q] = out;
+    }
+  }
+}
+
+__global__ void ep_arrive_kernel(EpPeers peers, EpLayout lay, int rank, int world, unsigned* epoch) {
+  unsigned e = 0;
+  if (threadIdx.x == 0) {
+    e = *epoch + 1;
+    *epoch = e;
+  }
+  e = __shfl_sync(0xffffffffu, e, 0);
+  __threadfence_system();
+  if (static_cast<int>(threadIdx.x) < world)
+    st_release_sys(reinterpret_cast<unsigned*>(peers.base[threadIdx.x] + lay.flags) + rank, e);
+}
+
+__global__ void ep_wait_kernel(const unsigned* flags, int world, const unsigned* epoch, ErrorWord* err, int site) {
+  if (static_cast<int>(threadIdx.x) >= world) return;
+  const unsigned target = *epoch;
+  const unsigned* f = flags + threadIdx.x;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (static_cast<int>(ld_acquire_sys(f) - target) >= 0) break;
+    if (i >= kEpWaitPolls || ((i & 63u) == 63u && global_timer_ns() - start > kEpWaitNs)) {
+      raise_error(err, kDevWaitTimeout, site, static_cast<int>(threadIdx.x), static_cast<int>(target));
+      break;
+    }
+    __nanosleep(200);
+  }
+  __threadfence_system();
+}
+
+}  // namespace
+
+EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
+  EpLayout l{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    off = align256(off);
+    const size_t at = off;
+    off += bytes;
+    return at;
+  };
+  const size_t T = static_cast<size_t>(d.max_rows), K = d.top_k, E = d.experts, H = d.hidden;
+  l.flags = take(kMaxEpRanks * sizeof(unsigned));
+  l.seg_count = take(E * 4);
+  l.seg_start = take(E * 4);
+  l.xperm = take(T * K * H * 2);
+  l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) * (K < static_cast<size_t>(m.local)
+                                                                            ? static_cast<int64_t>(K)
+                                                                            : static_cast<int64_t>(m.local));
+  l.yrecv = take(static_cast<size_t>(l.max_recv) * H * 2);
+  l.bytes = align256(off);
+  return l;
+}
+
+size_t ep_scratch_bytes(const PrefillDims& d, const EpLayout& lay, const EpMap& m) {
+  EpScratch s{};
+  carve_ep_scratch(d, lay, m, nullptr, &s);
+  return s.bytes;
+}
+
+void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m, void* base, EpScratch* s) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> char* {
+    off = align256(off);
+    char* p = base == nullptr ? nullptr : static_cast<char*>(base) + off;
+    off += bytes;
+    return p;
+  };
+  const size_t W = m.world, E = d.experts, L = m.local, H = d.hidden, F = d.ffn, R = lay.max_recv;
+  s->cnt_all = reinterpret_cast<int*>(take(W * E * 4));
+  s->seg_start_all = reinterpret_cast<int*>(take(W * E * 4));
+  s->recv_count = reinterpret_cast<int*>(take(L * 4));
+  s->recv_start = reinterpret_cast<int*>(take(L * 4));
+  s->remote_base = reinterpret_cast<int*>(take(E * 4));
+  s->epoch = reinterpret_cast<unsigned*>(take(sizeof(unsigned)));
+  s->xrecv = reinterpret_cast<__nv_bfloat16*>(take(R * H * 2));
+  s->act = reinterpret_cast<__nv_bfloat16*>(take(R * F * 2));
+  s->bytes = align256(off);
+}
+
+cudaError_t ep_route(const EpCall& c, cudaStream_t stream) { return launch_prefill_route(c.pc, stream); }
+
+cudaError_t ep_experts(const EpCall& c, cudaStream_t stream) {
+  const PrefillDims& d = c.pc.dims;
+  ep_prepare_kernel<<<1, 256, 0, stream>>>(c.map, c.peers, c.lay, c.es, c.pc.err);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return st;
+  ep_pull_kernel<<<c.pc.sm_count * 4, 256, 0, stream>>>(c.map, c.peers, c.lay, c.es, d.hidden);
+  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  const int L = c.map.local;
+  GroupedGemm g1 = prefill_gate_up_gemm(c.pc, true, false);
+  g1.experts = L;
+  g1.seg_count = c.es.recv_count;
+  g1.seg_start = c.es.recv_start;
+  g1.a_routed = c.es.xrecv;
+  g1.a_routed_rows = c.lay.max_recv;
+  g1.b0_routed = c.gate_local;
+  g1.b1_routed = c.up_local;
+  g1.b_routed_rows = static_cast<int64_t>(L) * d.ffn;
+  g1.out_routed = c.es.act;
+  if ((st = launch_grouped_gemm(g1, stream)) != cudaSuccess) return st;
+  GroupedGemm g2 = prefill_down_gemm(c.pc, true, false);
+  g2.experts = L;
+  g2.seg_count = c.es.recv_count;
+  g2.seg_start = c.es.recv_start;
+  g2.a_routed = c.es.act;
+  g2.a_routed_rows = c.lay.max_recv;
+  g2.b0_routed = c.down_local;
+  g2.b1_routed = c.down_local;
+  g2.b_routed_rows = static_cast<int64_t>(L) * d.hidden;
+  g2.out_routed = c.peers.base[c.map.rank] + c.lay.yrecv;
+  return launch_grouped_gemm(g2, stream);
+}
+
+cudaError_t ep_shared(const EpCall& c, cudaStream_t stream) {
+  if (c.pc.rows <= 0 || c.pc.dims.shared_ffn <= 0) return cudaSuccess;
+  cudaError_t st = launch_grouped_gemm(prefill_gate_up_gemm(c.pc, false, true), stream);
+  if (st != cudaSuccess) return st;
+  return launch_grouped_gemm(prefill_down_gemm(c.pc, false, true), stream);
+}
+
+cudaError_t ep_combine(const EpCall& c, cudaStream_t stream) {
+  const PrefillCall& p = c.pc;
+  if (p.rows <= 0) return cudaSuccess;
+  ep_combine_kernel<<<p.rows, 256, 0, stream>>>(p.rows, p.dims.hidden, p.dims.top_k, c.map, c.peers, c.lay, p.ids,
+                                                p.weights, p.scratch.pos_of, c.es.remote_base,
+                                                p.dims.shared_ffn > 0 ? p.scratch.shared_out : nullptr, p.resid, p.y);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream) {
+  ep_arrive_kernel<<<1, 32, 0, stream>>>(c.peers, c.lay, c.map.rank, c.map.world, c.es.epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_wait(const EpCall& c, int site, cudaStream_t stream) {
+  const auto* flags = reinterpret_cast<const unsigned*>(c.peers.base[c.map.rank] + c.lay.flags);
+  ep_wait_kernel<<<1, 32, 0, stream>>>(flags, c.map.world, c.es.epoch, c.pc.err, site);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_forward(const EpCall& c, cudaStream_t stream, cudaEvent_t* ev) {
+  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], stream) : cudaSuccess; };
+  cudaError_t st;
+  if ((st = ep_route(c, stream)) != cudaSuccess || (st = mark(0)) != cudaSuccess) return st;
+  if ((st = ep_arrive(c, stream)) != cudaSuccess || (st = ep_wait(c, 61, stream)) != cudaSuccess ||
+      (st = mark(1)) != cudaSuccess)
+    return st;
+  if ((st = ep_experts(c, stream)) != cudaSuccess || (st = mark(2)) != cudaSuccess) return st;
+  if ((st = ep_arrive(c, stream)) != cudaSuccess) return st;
+  if ((st = ep_shared(c, stream)) != cudaSuccess || (st = mark(3)) != cudaSuccess) return st;
+  if ((st = ep_wait(c, 62, stream)) != cudaSuccess) return st;
+  if ((st = ep_combine(c, stream)) != cudaSuccess) return st;
+  return mark(4);
+}
+
+}  // namespace uocr_b200

@@ -1,0 +1,99 @@
+// Expert-parallel prefill across the GPUs of one node (ep.cu): one process
+// per GPU, each owning a slice of the rows and routed_experts / world of the
+// experts. The reference has no multi-GPU path (no NCCL or MPI anywhere in
+// its src/); this is the dispatch/combine exchange that expert sharding needs.
+//
+// Every rank holds one exchange region (a cudaMalloc block shared through
+// CUDA IPC) with the same layout on every rank:
+//   flags     [kMaxEpRanks] u32   barrier epochs, flags[s] written by rank s
+//   seg_count [E] i32, seg_start [E] i32   this rank's rows per global expert
+//   xperm     [max_rows*k, H] bf16        this rank's rows grouped by expert
+//   yrecv     [max_recv, H] bf16          outputs of this rank's experts
+// Per layer, on rank r:
+//   route    router + top-k + permutation of its own rows into xperm (the
+//            single-GPU prefill stages)
+//   barrier  (arrive, wait)
+//   experts  for each of its experts, the segments of every rank's xperm are
+//            pulled over NVLink (peer loads) into xrecv, source rank order, so
+//            an expert's rows are in global row order as on one GPU; the
+//            grouped GEMMs write yrecv
+//   arrive   then the shared expert on its own rows while the others finish
+//   wait     then the combine pulls each selection's output row from the
+//            expert owner's yrecv and adds them in ascending expert id.
+// Each output row of the grouped GEMM depends on its own input row only, so
+// the result is bitwise the single-GPU result for the same rows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "prefill.h"
+
+namespace uocr_b200 {
+
+constexpr int kMaxEpRanks = 8;
+
+// Which rank owns expert e: contiguous ranges (e / local) or strided (e % world).
+struct EpMap {
+  int world, rank, experts, local, strided;
+  __host__ __device__ int owner(int e) const { return strided ? e % world : e / local; }
+  __host__ __device__ int local_index(int e) const { return strided ? e / world : e % local; }
+  __host__ __device__ int global(int d, int i) const { return strided ? i * world + d : d * local + i; }
+};
+
+// Exchange region base of every rank (this rank's own included).
+struct EpPeers {
+  char* base[kMaxEpRanks];
+};
+
+struct EpLayout {
+  size_t flags, seg_count, seg_start, xperm, yrecv, bytes;
+  int64_t max_recv;  // rows one rank's experts can receive: world * max_rows * min(k, local)
+};
+EpLayout ep_layout(const PrefillDims& d, const EpMap& m);
+
+// Per-rank scratch outside the exchange region.
+struct EpScratch {
+  int* cnt_all;      // [world, E] every rank's rows per global expert, read after the first barrier
+  int* seg_start_all;  // [world, E] and where they start in that rank's xperm
+  int* recv_count;   // [local] rows each local expert receives
+  int* recv_start;   // [local] its first row in xrecv / yrecv
+  int* remote_base;  // [E] row of this rank's first selection of e in the owner's yrecv, minus seg_start[e]
+  unsigned* epoch;   // barrier epoch counter
+  __nv_bfloat16* xrecv;  // [max_recv, H]
+  __nv_bfloat16* act;    // [max_recv, F]
+  size_t bytes;
+};
+size_t ep_scratch_bytes(const PrefillDims& d, const EpLayout& lay, const EpMap& m);
+void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m, void* base, EpScratch* s);
+
+struct EpCall {
+  PrefillCall pc;  // this rank's rows; pc.scratch's seg_count/seg_start/xperm point into its exchange region
+  EpMap map;
+  EpPeers peers;
+  EpLayout lay;
+  EpScratch es;
+  // This rank's experts only: gate/up [local*F, H], down [local*H, F].
+  const __nv_bfloat16* gate_local;
+  const __nv_bfloat16* up_local;
+  const __nv_bfloat16* down_local;
+};
+
+// The phases of one layer; ep_forward runs them with the barriers between.
+cudaError_t ep_route(const EpCall& c, cudaStream_t stream);
+cudaError_t ep_experts(const EpCall& c, cudaStream_t stream);
+cudaError_t ep_shared(const EpCall& c, cudaStream_t stream);
+cudaError_t ep_combine(const EpCall& c, cudaStream_t stream);
+// Barrier over the ranks' exchange regions: arrive publishes this rank's
+// next epoch to every rank; wait spins (bounded: ~20 s, then an error word)
+// until every rank published it. Data written before arrive on any rank is
+// visible to every rank's kernels after its wait.
+cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream);
+cudaError_t ep_wait(const EpCall& c, int site, cudaStream_t stream);
+// Optional events (5): after route, wait 1, experts, shared, combine.
+cudaError_t ep_forward(const EpCall& c, cudaStream_t stream, cudaEvent_t* events = nullptr);
+
+}  // namespace uocr_b200

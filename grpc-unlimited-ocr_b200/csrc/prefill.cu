@@ -273,13 +273,13 @@ __global__ void __launch_bounds__(256) combine_kernel(int T, int H, int K, const
 
 }  // namespace
 
-size_t prefill_scratch_bytes(const PrefillDims& d) {
+size_t prefill_scratch_bytes(const PrefillDims& d, bool routed_buffers) {
   PrefillScratch s{};
-  carve_prefill_scratch(d, nullptr, &s);
+  carve_prefill_scratch(d, nullptr, &s, routed_buffers);
   return s.bytes;
 }
 
-void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s) {
+void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s, bool routed_buffers) {
   size_t off = 0;
   auto take = [&](size_t bytes) -> char* {
     off = (off + 255) / 256 * 256;
@@ -290,17 +290,20 @@ void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s) 
   const size_t T = static_cast<size_t>(d.max_rows), K = d.top_k, E = d.experts, H = d.hidden, F = d.ffn,
                S = d.shared_ffn;
   const size_t nblk = (T + kPermBlock - 1) / kPermBlock;
+  *s = PrefillScratch{};
   s->block_counts = reinterpret_cast<int*>(take(nblk * E * 4));
   s->block_offset = reinterpret_cast<int*>(take(nblk * E * 4));
-  s->seg_count = reinterpret_cast<int*>(take(E * 4));
-  s->seg_start = reinterpret_cast<int*>(take(E * 4));
   s->pos_of = reinterpret_cast<int*>(take(T * K * 4));
   s->xhat = reinterpret_cast<__nv_bfloat16*>(take(T * H * 2));
-  s->xperm = reinterpret_cast<__nv_bfloat16*>(take(T * K * H * 2));
-  s->act = reinterpret_cast<__nv_bfloat16*>(take(T * K * F * 2));
   s->act_s = reinterpret_cast<__nv_bfloat16*>(take(T * (S > 0 ? S : 1) * 2));
-  s->yperm = reinterpret_cast<__nv_bfloat16*>(take(T * K * H * 2));
   s->shared_out = reinterpret_cast<float*>(take(T * H * 4));
+  if (routed_buffers) {
+    s->seg_count = reinterpret_cast<int*>(take(E * 4));
+    s->seg_start = reinterpret_cast<int*>(take(E * 4));
+    s->xperm = reinterpret_cast<__nv_bfloat16*>(take(T * K * H * 2));
+    s->act = reinterpret_cast<__nv_bfloat16*>(take(T * K * F * 2));
+    s->yperm = reinterpret_cast<__nv_bfloat16*>(take(T * K * H * 2));
+  }
   s->bytes = off;
 }
 
@@ -312,13 +315,16 @@ cudaError_t launch_router_logits_rows(const float* x, int T, int H, const float*
   return cudaGetLastError();
 }
 
-cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
+cudaError_t launch_prefill_route(const PrefillCall& c, cudaStream_t stream) {
   const PrefillDims& d = c.dims;
   const PrefillScratch& s = c.scratch;
-  const int T = c.rows, H = d.hidden, E = d.experts, K = d.top_k, F = d.ffn, S = d.shared_ffn;
-  if (T <= 0) return cudaSuccess;
-  // Optional per-kernel timing: an event after each stage of the path.
+  const int T = c.rows, H = d.hidden, E = d.experts, K = d.top_k;
   auto mark = [&](int i) { return c.events != nullptr ? cudaEventRecord(c.events[i], stream) : cudaSuccess; };
+  if (T <= 0) {
+    // An empty batch still publishes empty segments (expert-parallel peers read them).
+    cudaError_t st = cudaMemsetAsync(s.seg_count, 0, static_cast<size_t>(E) * sizeof(int), stream);
+    return st == cudaSuccess ? cudaMemsetAsync(s.seg_start, 0, static_cast<size_t>(E) * sizeof(int), stream) : st;
+  }
   cudaError_t st = launch_router_logits_rows(c.x, T, H, c.router, c.bias, E, c.logits, stream);
   if (st != cudaSuccess || (st = mark(0)) != cudaSuccess) return st;
   topk_rows_i32_kernel<<<(T + 7) / 8, 256, 0, stream>>>(c.logits, T, E, K, d.renormalize, c.ids, c.weights);
@@ -330,60 +336,86 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
   scatter_kernel<<<nblk, kPermBlock, 0, stream>>>(c.x, T, H, K, E, c.ids, s.block_offset, s.pos_of, s.xhat,
                                                   s.xperm);
-  if ((st = cudaGetLastError()) != cudaSuccess || (st = mark(2)) != cudaSuccess) return st;
+  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  return mark(2);
+}
 
-  const int64_t R = static_cast<int64_t>(T) * K;
-  GroupedGemm g1{};
-  g1.mode = 0;
-  g1.experts = E;
-  g1.seg_count = s.seg_count;
-  g1.seg_start = s.seg_start;
-  g1.a_routed = s.xperm;
-  g1.a_routed_rows = R;
-  g1.k_routed = H;
-  g1.b0_routed = c.gate;
-  g1.b1_routed = c.up;
-  g1.b_routed_rows = static_cast<int64_t>(E) * F;
-  g1.b_rows_per_expert = F;
-  g1.n_cols_routed = F;
-  g1.out_routed = s.act;
-  g1.ld_out_routed = F;
-  g1.shared_rows = S > 0 ? T : 0;
-  g1.a_shared = s.xhat;
-  g1.k_shared = H;
-  g1.b0_shared = c.sgate;
-  g1.b1_shared = c.sup;
-  g1.b_shared_rows = S;
-  g1.n_cols_shared = S > 0 ? S : 128;
-  g1.out_shared = s.act_s;
-  g1.ld_out_shared = S;
-  g1.shared_out_f32 = false;
-  g1.err = c.err;
-  g1.blocks = c.sm_count;
-  if ((st = launch_grouped_gemm(g1, stream)) != cudaSuccess || (st = mark(3)) != cudaSuccess) return st;
+GroupedGemm prefill_gate_up_gemm(const PrefillCall& c, bool routed, bool shared) {
+  const PrefillDims& d = c.dims;
+  const PrefillScratch& s = c.scratch;
+  const int T = c.rows, H = d.hidden, E = d.experts, K = d.top_k, F = d.ffn, S = d.shared_ffn;
+  GroupedGemm g{};
+  g.mode = 0;
+  g.experts = routed ? E : 0;
+  g.seg_count = s.seg_count;
+  g.seg_start = s.seg_start;
+  g.a_routed = s.xperm;
+  g.a_routed_rows = static_cast<int64_t>(T) * K;
+  g.k_routed = H;
+  g.b0_routed = c.gate;
+  g.b1_routed = c.up;
+  g.b_routed_rows = static_cast<int64_t>(E) * F;
+  g.b_rows_per_expert = F;
+  g.n_cols_routed = F;
+  g.out_routed = s.act;
+  g.ld_out_routed = F;
+  g.shared_rows = shared && S > 0 ? T : 0;
+  g.a_shared = s.xhat;
+  g.k_shared = H;
+  g.b0_shared = c.sgate;
+  g.b1_shared = c.sup;
+  g.b_shared_rows = S;
+  g.n_cols_shared = S > 0 ? S : 128;
+  g.out_shared = s.act_s;
+  g.ld_out_shared = S;
+  g.shared_out_f32 = false;
+  g.err = c.err;
+  g.blocks = c.sm_count;
+  return g;
+}
 
-  GroupedGemm g2 = g1;
-  g2.mode = 1;
-  g2.a_routed = s.act;
-  g2.k_routed = F;
-  g2.b0_routed = c.down;
-  g2.b1_routed = c.down;
-  g2.b_routed_rows = static_cast<int64_t>(E) * H;
-  g2.b_rows_per_expert = H;
-  g2.n_cols_routed = H;
-  g2.out_routed = s.yperm;
-  g2.ld_out_routed = H;
-  g2.a_shared = s.act_s;
-  g2.k_shared = S > 0 ? S : 64;
-  g2.b0_shared = c.sdown;
-  g2.b1_shared = c.sdown;
-  g2.b_shared_rows = H;
-  g2.n_cols_shared = H;
-  g2.out_shared = s.shared_out;
-  g2.ld_out_shared = H;
-  g2.shared_out_f32 = true;
-  if ((st = launch_grouped_gemm(g2, stream)) != cudaSuccess || (st = mark(4)) != cudaSuccess) return st;
+GroupedGemm prefill_down_gemm(const PrefillCall& c, bool routed, bool shared) {
+  const PrefillDims& d = c.dims;
+  const PrefillScratch& s = c.scratch;
+  const int H = d.hidden, E = d.experts, F = d.ffn, S = d.shared_ffn;
+  GroupedGemm g = prefill_gate_up_gemm(c, routed, shared);
+  g.mode = 1;
+  g.a_routed = s.act;
+  g.k_routed = F;
+  g.b0_routed = c.down;
+  g.b1_routed = c.down;
+  g.b_routed_rows = static_cast<int64_t>(E) * H;
+  g.b_rows_per_expert = H;
+  g.n_cols_routed = H;
+  g.out_routed = s.yperm;
+  g.ld_out_routed = H;
+  g.a_shared = s.act_s;
+  g.k_shared = S > 0 ? S : 64;
+  g.b0_shared = c.sdown;
+  g.b1_shared = c.sdown;
+  g.b_shared_rows = H;
+  g.n_cols_shared = H;
+  g.out_shared = s.shared_out;
+  g.ld_out_shared = H;
+  g.shared_out_f32 = true;
+  return g;
+}
 
+cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
+  const PrefillDims& d = c.dims;
+  const PrefillScratch& s = c.scratch;
+  const int T = c.rows, H = d.hidden, K = d.top_k, S = d.shared_ffn;
+  if (T <= 0) return cudaSuccess;
+  // Optional per-kernel timing: an event after each stage of the path.
+  auto mark = [&](int i) { return c.events != nullptr ? cudaEventRecord(c.events[i], stream) : cudaSuccess; };
+  cudaError_t st = launch_prefill_route(c, stream);
+  if (st != cudaSuccess) return st;
+  if ((st = launch_grouped_gemm(prefill_gate_up_gemm(c, true, true), stream)) != cudaSuccess ||
+      (st = mark(3)) != cudaSuccess)
+    return st;
+  if ((st = launch_grouped_gemm(prefill_down_gemm(c, true, true), stream)) != cudaSuccess ||
+      (st = mark(4)) != cudaSuccess)
+    return st;
   combine_kernel<<<T, 256, 0, stream>>>(T, H, K, c.ids, c.weights, s.pos_of, s.yperm, S > 0 ? s.shared_out : nullptr,
                                         c.resid, c.y);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;

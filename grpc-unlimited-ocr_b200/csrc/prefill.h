@@ -42,8 +42,10 @@ inline bool prefill_shapes_ok(int hidden, int ffn, int shared_ffn) {
   return hidden % 256 == 0 && ffn % 128 == 0 && shared_ffn % 128 == 0;
 }
 
-size_t prefill_scratch_bytes(const PrefillDims& d);
-void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s);
+// routed_buffers = false leaves seg_count, seg_start, xperm, act and yperm
+// null: the expert-parallel path keeps those in its exchange region.
+size_t prefill_scratch_bytes(const PrefillDims& d, bool routed_buffers = true);
+void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s, bool routed_buffers = true);
 
 struct PrefillCall {
   PrefillDims dims;
@@ -68,5 +70,12 @@ struct PrefillCall {
 cudaError_t launch_router_logits_rows(const float* x, int T, int H, const float* router, const float* bias, int E,
                                       float* logits, cudaStream_t stream);
 cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream);
+
+// The stages of launch_prefill, for the expert-parallel path (ep.cu):
+// router + top-k + permutation (an empty batch writes empty segments), and
+// the two grouped GEMM descriptions with the routed and/or shared groups.
+cudaError_t launch_prefill_route(const PrefillCall& c, cudaStream_t stream);
+GroupedGemm prefill_gate_up_gemm(const PrefillCall& c, bool routed, bool shared);
+GroupedGemm prefill_down_gemm(const PrefillCall& c, bool routed, bool shared);
 
 }  // namespace uocr_b200

@@ -22,6 +22,8 @@ MEMORY_HOST, MEMORY_DEVICE = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
 PLAN_TENSOR_DECODE = 2
+PLAN_EP_STRIDED = 4
+EP_HANDLE_BYTES = 256
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).
 KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KIND_X = 1, 2, 3, 4, 5, 6, 7, 8
@@ -30,6 +32,7 @@ KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KI
 EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
     "uocr_moe_set_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
+    "uocr_moe_ep_handle", "uocr_moe_ep_connect", "uocr_moe_ep_connect_local", "uocr_moe_ep_forward_local",
     "uocr_expert_topk",
     "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
 ]
@@ -46,7 +49,12 @@ class MoeDesc(ctypes.Structure):
                 ("experts_per_token", ctypes.c_int64), ("expert_ffn", ctypes.c_int64),
                 ("shared_ffn", ctypes.c_int64), ("layers", ctypes.c_int64), ("max_rows", ctypes.c_int64),
                 ("weight_format", ctypes.c_int32), ("renormalize", ctypes.c_int32),
-                ("router_bias", ctypes.c_int32), ("device", ctypes.c_int32), ("flags", ctypes.c_int32)]
+                ("router_bias", ctypes.c_int32), ("device", ctypes.c_int32), ("flags", ctypes.c_int32),
+                ("ep_world", ctypes.c_int32), ("ep_rank", ctypes.c_int32)]
+
+
+class EpHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * EP_HANDLE_BYTES)]
 
 
 class LayerSrc(ctypes.Structure):
@@ -75,6 +83,11 @@ def lib() -> ctypes.CDLL:
         L.uocr_moe_forward_stack.argtypes = [vp, vp, i64, vp]
         L.uocr_moe_check.argtypes = [vp, vp]
         L.uocr_moe_profile_stack.argtypes = [vp, vp, i64, i32, ctypes.POINTER(f32), vp]
+        L.uocr_moe_ep_handle.argtypes = [vp, ctypes.POINTER(EpHandle)]
+        L.uocr_moe_ep_connect.argtypes = [vp, ctypes.POINTER(EpHandle)]
+        L.uocr_moe_ep_connect_local.argtypes = [ctypes.POINTER(vp), i32]
+        L.uocr_moe_ep_forward_local.argtypes = [ctypes.POINTER(vp), i32, i64, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                                                ctypes.POINTER(vp), vp]
         L.uocr_expert_topk.argtypes = [vp, i64, i64, i64, i32, vp, vp, vp]
         L.uocr_expert_ffn_one.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
         L.uocr_expert_ffn_one_noalloc.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
@@ -122,12 +135,15 @@ class Plan:
     """One MoE stack on one device (uocr_moe_plan)."""
 
     def __init__(self, dims: Dims, max_rows: int, weight_format: int = WEIGHT_BF16, renormalize: bool = True,
-                 router_bias: bool = False, device: int = 0, flags: int = 0):
+                 router_bias: bool = False, device: int = 0, flags: int = 0, ep_world: int = 0, ep_rank: int = 0):
+        """ep_world > 1 makes this plan rank ep_rank of an expert-parallel
+        group (one process per GPU); connect it with ep_connect (see ep.py)."""
         self.dims = dims
         self.max_rows = max_rows
         self.weight_format = weight_format
+        self.ep_world, self.ep_rank = ep_world, ep_rank
         desc = MoeDesc(dims.hidden, dims.experts, dims.top_k, dims.ffn, dims.shared_ffn, dims.layers, max_rows,
-                       weight_format, int(renormalize), int(router_bias), device, flags)
+                       weight_format, int(renormalize), int(router_bias), device, flags, ep_world, ep_rank)
         h = ctypes.c_void_p()
         _check(lib().uocr_moe_plan_create(ctypes.byref(desc), ctypes.byref(h)))
         self.h = h
@@ -172,13 +188,46 @@ class Plan:
         rows = h.shape[0] if rows is None else rows
         out = (ctypes.c_float * 8)()
         _check(lib().uocr_moe_profile_stack(self.h, _ptr(h), rows, iters, out, _stream(stream)))
-        names = self.DECODE_KERNELS if int(out[6]) == 3 else self.PREFILL_KERNELS
+        names = {3: self.DECODE_KERNELS, 5: self.EP_PHASES}.get(int(out[6]), self.PREFILL_KERNELS)
         res = {n: out[i] for i, n in enumerate(names)}
         res["stack"] = out[7]
         return res
 
     def check(self, stream=None):
         _check(lib().uocr_moe_check(self.h, _stream(stream)))
+
+    # ---- expert parallelism
+    EP_PHASES = ("route", "exchange_wait", "experts", "shared", "combine")
+
+    def ep_handle(self) -> bytes:
+        h = EpHandle()
+        _check(lib().uocr_moe_ep_handle(self.h, ctypes.byref(h)))
+        return bytes(h.bytes)
+
+    def ep_connect(self, handles: list[bytes]):
+        arr = (EpHandle * len(handles))()
+        for i, b in enumerate(handles):
+            if len(b) != EP_HANDLE_BYTES:
+                raise ValueError("an EP handle is 256 bytes")
+            ctypes.memmove(arr[i].bytes, b, EP_HANDLE_BYTES)
+        _check(lib().uocr_moe_ep_connect(self.h, arr))
+
+
+def ep_connect_local(plans: list[Plan]):
+    """Joins plans on one GPU into a group of virtual expert-parallel ranks."""
+    arr = (ctypes.c_void_p * len(plans))(*[p.h for p in plans])
+    _check(lib().uocr_moe_ep_connect_local(arr, len(plans)))
+
+
+def ep_forward_local(plans: list[Plan], layer: int, xs, ys, stream=None, rows=None):
+    """One layer over a local group: rank i maps xs[i] [rows_i, H] to ys[i]."""
+    n = len(plans)
+    rows = [x.shape[0] for x in xs] if rows is None else rows
+    parr = (ctypes.c_void_p * n)(*[p.h for p in plans])
+    xarr = (ctypes.c_void_p * n)(*[_ptr(x) for x in xs])
+    yarr = (ctypes.c_void_p * n)(*[_ptr(y) for y in ys])
+    rarr = (ctypes.c_int64 * n)(*rows)
+    _check(lib().uocr_moe_ep_forward_local(parr, n, layer, xarr, rarr, yarr, _stream(stream)))
 
 
 def expert_topk(logits, k: int, renormalize: bool, ids, weights, stream=None):

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define UOCR_MOE_ABI_VERSION 1
+#define UOCR_MOE_ABI_VERSION 2
 
 typedef enum uocr_status {
   UOCR_OK = 0,
@@ -67,6 +67,8 @@ typedef struct uocr_moe_desc {
   int32_t router_bias;       /* 1: each layer carries an fp32 [E] bias added to the logits */
   int32_t device;            /* CUDA device ordinal the plan lives on */
   int32_t flags;             /* UOCR_PLAN_* bits */
+  int32_t ep_world;          /* expert parallelism: ranks (GPUs) sharing the experts; 0 or 1 = none */
+  int32_t ep_rank;           /* this plan's rank in [0, ep_world) */
 } uocr_moe_desc;
 
 /* forward_stack replays a CUDA graph it captured on the first call for the
@@ -80,6 +82,9 @@ typedef struct uocr_moe_desc {
  * hidden, expert_ffn and shared_ffn must be multiples of 128, hidden <= 8192,
  * else the flag is ignored. The int8 format always streams. */
 #define UOCR_PLAN_TENSOR_DECODE 2
+/* Expert parallelism: expert e lives on rank e % ep_world instead of the
+ * default contiguous ranges (rank e / (routed_experts / ep_world)). */
+#define UOCR_PLAN_EP_STRIDED 4
 
 int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** plan);
 int uocr_moe_plan_destroy(uocr_moe_plan* plan);
@@ -136,6 +141,42 @@ int uocr_moe_check(uocr_moe_plan* plan, void* stream);
  * kernels: no overlap between them). No reference counterpart. */
 int uocr_moe_profile_stack(uocr_moe_plan* plan, float* h, int64_t rows, int32_t iters, float* ms_per_kernel,
                            void* stream);
+
+/* ---- Expert parallelism across the GPUs of one node ----------------------
+ * No reference counterpart (the reference has no multi-GPU path). A plan with
+ * ep_world = G > 1 is one rank of G processes, one per GPU: it holds
+ * routed_experts / G of the experts (set_layer still takes the full stacks
+ * and keeps its own experts) and forwards its own rows. Every forward call on
+ * such a plan is collective: all G ranks make the same calls in the same
+ * order, any row count including 0. Layers run the prefill path (bf16,
+ * hidden % 256 == 0, expert_ffn and shared_ffn % 128 == 0) whatever the row
+ * count. Between the phases the ranks pull rows and expert outputs from each
+ * other's memory over NVLink (CUDA IPC mappings) and meet at device-side
+ * barriers; a rank that does not arrive within ~20 s makes uocr_moe_check
+ * report UOCR_ERR_TIMEOUT, after which the ranks' plans must be recreated.
+ * The result equals, bit for bit, a single-GPU plan's on the same rows.
+ *
+ * Setup: each rank gets its handle, the ranks exchange them (any transport:
+ * torch.distributed all_gather, a file, a socket), each calls
+ * uocr_moe_ep_connect with all G handles in rank order, and the ranks meet
+ * (a host barrier) before the first forward. Destroy after a host barrier,
+ * when no rank is inside a forward. */
+typedef struct uocr_ep_handle {
+  unsigned char bytes[256]; /* IPC handle of the rank's exchange memory + a fingerprint of its plan */
+} uocr_ep_handle;
+int uocr_moe_ep_handle(uocr_moe_plan* plan, uocr_ep_handle* out);
+/* handles[ep_world] in rank order (this rank's own included). Fails with
+ * UOCR_ERR_INVALID_ARGUMENT when the plans differ in shape or rank, and
+ * UOCR_ERR_UNSUPPORTED when two ranks share a GPU (device-side waits between
+ * processes on one GPU are not allowed: use the local group below). */
+int uocr_moe_ep_connect(uocr_moe_plan* plan, const uocr_ep_handle* handles);
+/* Test harness for one GPU: n plans on the same device, created with
+ * ep_world = n and ep_rank = 0..n-1, become one group of virtual ranks.
+ * Such plans run only through uocr_moe_ep_forward_local, which runs each
+ * phase for every rank in turn on one stream (no barriers are needed). */
+int uocr_moe_ep_connect_local(uocr_moe_plan* const* plans, int32_t n);
+int uocr_moe_ep_forward_local(uocr_moe_plan* const* plans, int32_t n, int64_t layer, const float* const* x,
+                              const int64_t* rows, float* const* y, void* stream);
 
 /* ---- Op-level mirrors of the reference's uocr::cuda MoE ops -------------- */
 

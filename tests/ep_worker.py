@@ -1,0 +1,61 @@
+"""One rank of the multi-GPU expert-parallel check (run by torchrun from
+test_ep_multi_gpu.py, one process per GPU): config-3 shapes, this rank's
+slice of the rows through an expert-parallel plan, compared bitwise with a
+single-GPU plan over the same rows on the same GPU."""
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(os.path.dirname(HERE), "grpc-unlimited-ocr_b200"))
+
+
+def main():
+    import torch
+    import torch.distributed as dist
+
+    import ep
+    import moe_configs as C
+    import uocr_moe as M
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    strided = os.environ.get("EP_STRIDED", "0") == "1"
+    total = int(os.environ.get("EP_ROWS", "4096"))
+    cfg = C.CONFIGS[3]
+    start, count = ep.rows_of(total, world, rank)
+    t = C.device_layer(cfg, 0, device=dev)
+    plan = M.Plan(cfg.dims(), max_rows=max(count, 1), router_bias=True, device=local,
+                  flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank)
+    C.load_layer(plan, cfg, 0, t)
+    ep.connect(plan)
+    x = C.device_input(cfg, total, device=dev)[start:start + count].contiguous()
+    y = torch.empty_like(x)
+    for _ in range(3):  # repeated calls reuse the exchange buffers
+        plan.forward(0, x, y)
+    plan.check()
+    single = M.Plan(cfg.dims(), max_rows=max(count, 17), router_bias=True, device=local)
+    C.load_layer(single, cfg, 0, t)
+    y1 = torch.empty_like(x)
+    if count > 16:
+        single.forward(0, x, y1)
+        single.check()
+        ok = torch.equal(y, y1)
+    else:
+        ok = True
+    flag = torch.tensor([0 if ok else 1], device=dev)
+    dist.all_reduce(flag)
+    dist.barrier()
+    plan.close()
+    single.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(f"EP world {world} strided {strided} rows {total}: {'EP_OK' if flag.item() == 0 else 'EP_MISMATCH'}")
+    sys.exit(0 if flag.item() == 0 else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = M.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.uocr_abi_version() == 1
+    assert lib.uocr_abi_version() == 2
 
 
 def _desc(**kw):
@@ -44,6 +44,26 @@ def test_plan_create_rejects_bad_shapes(bad):
     rc = M.lib().uocr_moe_plan_create(ctypes.byref(_desc(**bad)), ctypes.byref(h))
     assert rc == 1 and not h.value
     assert M.lib().uocr_last_error().decode().startswith("plan_create")
+
+
+@pytest.mark.parametrize("bad,code", [
+    (dict(ep_world=9, ep_rank=0), 1), (dict(ep_world=-1), 1), (dict(ep_world=2, ep_rank=2), 1),
+    (dict(ep_world=3, ep_rank=0), 1),  # 8 experts do not split over 3 ranks
+    (dict(ep_world=2, ep_rank=0), 2),  # hidden 64: not a prefill shape
+    (dict(ep_world=2, ep_rank=1, hidden=256, expert_ffn=128, shared_ffn=128, weight_format=1), 2)])
+def test_plan_create_rejects_bad_expert_parallel_setups(bad, code):
+    h = ctypes.c_void_p()
+    rc = M.lib().uocr_moe_plan_create(ctypes.byref(_desc(**bad)), ctypes.byref(h))
+    assert rc == code and not h.value
+
+
+def test_ep_entry_points_reject_bad_arguments():
+    lib = M.lib()
+    assert lib.uocr_moe_ep_handle(None, None) == 1
+    assert lib.uocr_moe_ep_connect(None, None) == 1
+    assert lib.uocr_moe_ep_connect_local(None, 2) == 1
+    assert lib.uocr_moe_ep_forward_local(None, 2, 0, None, None, None, None) == 1
+    assert ctypes.sizeof(M.EpHandle) == 256
 
 
 def test_null_arguments_are_rejected():

@@ -1,0 +1,175 @@
+"""Expert-parallel host logic on the CPU: row and expert ownership, the
+exchange arithmetic (restated here in numpy: each rank's per-expert segments,
+the receive layout of every rank's experts, and where each selection's output
+lands) checked against the single-GPU permutation, and the same arithmetic
+run by two gloo ranks that exchange their counts as the GPUs do."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import ep
+
+
+def test_rows_of_partitions_every_row_once():
+    for total in (0, 1, 7, 32768, 32769):
+        for world in (1, 2, 3, 8):
+            spans = [ep.rows_of(total, world, r) for r in range(world)]
+            assert sum(c for _, c in spans) == total
+            pos = 0
+            for s, c in spans:
+                assert s == pos
+                pos += c
+            assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_expert_ownership(strided):
+    for E, W in ((64, 1), (64, 2), (64, 8), (16, 4), (128, 8)):
+        owned = [ep.local_experts(r, E, W, strided) for r in range(W)]
+        assert sorted(e for o in owned for e in o) == list(range(E))
+        for r, o in enumerate(owned):
+            assert o == sorted(o) and len(o) == E // W
+            assert all(ep.expert_owner(e, E, W, strided) == r for e in o)
+
+
+# ---- the exchange arithmetic -------------------------------------------------
+
+def permute(ids, E):
+    """The single-GPU stable permutation: (seg_count, seg_start, pos_of)."""
+    flat = ids.ravel()
+    seg_count = np.bincount(flat, minlength=E)
+    seg_start = np.concatenate([[0], np.cumsum(seg_count)[:-1]])
+    order = np.argsort(flat, kind="stable")
+    pos = np.empty(flat.size, np.int64)
+    pos[order] = np.arange(flat.size)
+    return seg_count, seg_start, pos.reshape(ids.shape)
+
+
+def receive_layout(cnt_all, W, E, strided):
+    """rstart[d][i]: first row of rank d's local expert i in d's receive
+    buffer; tot[d][i] its row count (the prepare kernel's tables)."""
+    L = E // W
+    tot = np.zeros((W, L), np.int64)
+    for d in range(W):
+        for i, e in enumerate(ep.local_experts(d, E, W, strided)):
+            tot[d, i] = cnt_all[:, e].sum()
+    rstart = np.concatenate([np.zeros((W, 1), np.int64), np.cumsum(tot, axis=1)[:, :-1]], axis=1)
+    return tot, rstart
+
+
+def remote_base(rank, cnt_all, seg_start_own, rstart, W, E, strided):
+    out = np.zeros(E, np.int64)
+    for e in range(E):
+        d = ep.expert_owner(e, E, W, strided)
+        i = ep.local_experts(d, E, W, strided).index(e)
+        out[e] = rstart[d, i] + cnt_all[:rank, e].sum() - seg_start_own[e]
+    return out
+
+
+def simulate(ids_per_rank, W, E, strided):
+    """Per-rank permutations, the pulls into every owner's receive rows, and
+    each selection's remote row. Returns, per owner, the (source rank, row)
+    of each received row, and per source the remote row of each selection."""
+    perms = [permute(ids, E) for ids in ids_per_rank]
+    cnt_all = np.stack([p[0] for p in perms])
+    tot, rstart = receive_layout(cnt_all, W, E, strided)
+    recv = []
+    for d in range(W):
+        rows = []
+        for i, e in enumerate(ep.local_experts(d, E, W, strided)):
+            for s in range(W):
+                seg_count, seg_start, pos = perms[s]
+                # rows of s's xperm segment e, in segment order = token order
+                toks = np.argsort(ids_per_rank[s].ravel(), kind="stable")[seg_start[e]:seg_start[e] + seg_count[e]]
+                rows += [(s, int(t) // ids_per_rank[s].shape[1]) for t in toks]
+        assert len(rows) == tot[d].sum()
+        recv.append(rows)
+    remote = []
+    for s in range(W):
+        rb = remote_base(s, cnt_all, perms[s][1], rstart, W, E, strided)
+        remote.append(rb[ids_per_rank[s]] + perms[s][2])
+    return recv, remote
+
+
+@pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False), (8, True)])
+def test_exchange_arithmetic_reproduces_single_gpu_order(W, strided):
+    rng = np.random.default_rng(W)
+    E, K = 32, 4
+    rows = rng.integers(0, 50, size=W)
+    rows[0] = 0  # an empty rank still takes part
+    p = 1.0 / np.arange(1, E + 1) ** 1.2
+    ids_per_rank = [np.stack([rng.choice(E, K, replace=False, p=p / p.sum()) for _ in range(n)]).astype(np.int64)
+                    if n else np.zeros((0, K), np.int64) for n in rows]
+    recv, remote = simulate(ids_per_rank, W, E, strided)
+    offsets = np.concatenate([[0], np.cumsum(rows)])
+    glob_ids = np.concatenate(ids_per_rank)
+    for d in range(W):
+        # Each expert's received rows are its selections in global row order,
+        # exactly the rows a single GPU puts in that expert's segment.
+        got = [offsets[s] + t for s, t in recv[d]]
+        want = []
+        for e in ep.local_experts(d, E, W, strided):
+            want += [t for t in range(len(glob_ids)) if e in glob_ids[t]]
+        assert got == want
+    for s in range(W):
+        for t in range(rows[s]):
+            for j in range(K):
+                e = ids_per_rank[s][t, j]
+                d = ep.expert_owner(e, E, W, strided)
+                assert recv[d][remote[s][t, j]] == (s, t)
+
+
+# ---- two gloo ranks ----------------------------------------------------------
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _gloo_rank(rank, world, port, E, K, strided, result_q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(100 + rank)
+        n = [37, 0, 12][rank % 3]
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(n)]).astype(np.int64) if n else \
+            np.zeros((0, K), np.int64)
+        seg_count, seg_start, pos = permute(ids, E)
+        # the counts exchange the prepare kernel does with peer loads
+        allc = [torch.zeros(E, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(allc, torch.from_numpy(seg_count))
+        cnt_all = torch.stack(allc).numpy()
+        _, rstart = receive_layout(cnt_all, world, E, strided)
+        rb = remote_base(rank, cnt_all, seg_start, rstart, world, E, strided)
+        # handles travel as opaque bytes, in rank order
+        handles = ep.exchange_handles(bytes([rank]) * 256)
+        assert [h[0] for h in handles] == list(range(world))
+        obj = [None] * world
+        dist.all_gather_object(obj, (ids, rb[ids] + pos if n else np.zeros((0, K), np.int64)))
+        if rank == 0:
+            ids_all = [o[0] for o in obj]
+            _, remote = simulate(ids_all, world, E, strided)
+            ok = all(np.array_equal(remote[s], obj[s][1]) for s in range(world))
+            result_q.put(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_two_gloo_ranks_agree_with_one_process(strided):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, 16, 3, strided, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs)
+    assert q.get(timeout=5) is True

@@ -1,0 +1,36 @@
+"""Expert parallelism across real GPUs: tests/ep_worker.py under torchrun on
+2 (and up to 8) GPUs of one box, each rank's output bitwise equal to a
+single-GPU plan's on the same rows. Skipped on a box with one GPU (the
+one-GPU local-group tests cover the same data path)."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world,strided,rows", [(2, False, 4096), (2, True, 1000), (4, False, 8192),
+                                                (8, False, 32768)])
+def test_ep_ranks_equal_single_gpu(world, strided, rows):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    env = dict(os.environ, EP_STRIDED="1" if strided else "0", EP_ROWS=str(rows), NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.join(HERE, "ep_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    print(r.stdout[-2000:], r.stderr[-4000:])
+    assert r.returncode == 0
+    assert "EP_OK" in r.stdout
