@@ -25,6 +25,7 @@
 
 #include "moe_kernels.h"
 #include "ptx.cuh"
+#include "decode_fmt.cuh"
 #include "route.cuh"
 
 namespace uocr_b200 {
@@ -39,81 +40,11 @@ constexpr int kThreads = (kWorkers + 1) * 32;  // + the routing warp
 template <int MaxT>
 constexpr int chunk_count() { return MaxT <= 4 ? 8 : 4; }
 
-__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-template <typename Rows>
-struct Fmt;
-
-template <>
-struct Fmt<Bf16Rows> {
-  static constexpr int kElemBytes = 2;
-  static constexpr int kPerChunk = 8;  // weights per 16 bytes
-  __device__ static const uint4* row(const Bf16Rows& r, int64_t i) {
-    return reinterpret_cast<const uint4*>(r.w + i * r.cols);
-  }
-  __device__ static float scale(const Bf16Rows&, int64_t) { return 1.0f; }
-  // 16 bytes of weights against fp32 inputs in shared memory
-  __device__ static float dot_x(const uint4& w, const float* x) {
-    const float4 x0 = reinterpret_cast<const float4*>(x)[0];
-    const float4 x1 = reinterpret_cast<const float4*>(x)[1];
-    return dot8_bf16(w, x0, x1);
-  }
-  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
-    return dot8_bf16_bf16(w, __ldg(reinterpret_cast<const uint4*>(act)));
-  }
-};
-
-template <>
-struct Fmt<Q8Rows> {
-  static constexpr int kElemBytes = 1;
-  static constexpr int kPerChunk = 16;
-  __device__ static const uint4* row(const Q8Rows& r, int64_t i) {
-    return reinterpret_cast<const uint4*>(r.q + i * r.cols);
-  }
-  __device__ static float scale(const Q8Rows& r, int64_t i) { return __ldg(r.scale + i); }
-  __device__ static float dot_x(const uint4& w, const float* x) {
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    float s = 0.0f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float a, b, c, d;
-      i8x4_to_f32(words[q], a, b, c, d);
-      const float4 xv = reinterpret_cast<const float4*>(x)[q];
-      s = fmaf(a, xv.x, s);
-      s = fmaf(b, xv.y, s);
-      s = fmaf(c, xv.z, s);
-      s = fmaf(d, xv.w, s);
-    }
-    return s;
-  }
-  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(act));
-    const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(act) + 1);
-    const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&a0);
-    const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&a1);
-    float s = 0.0f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float a, b, c, d;
-      i8x4_to_f32(words[q], a, b, c, d);
-      const __nv_bfloat162* p = q < 2 ? p0 : p1;
-      const float2 f0 = __bfloat1622float2(p[(q & 1) * 2]);
-      const float2 f1 = __bfloat1622float2(p[(q & 1) * 2 + 1]);
-      s = fmaf(a, f0.x, s);
-      s = fmaf(b, f0.y, s);
-      s = fmaf(c, f1.x, s);
-      s = fmaf(d, f1.y, s);
-    }
-    return s;
-  }
-};
+// L2 prefetch: how many of its own units ahead a warp keeps on their way, and
+// how many bytes of down rows the gate/up kernel brings in for the down
+// kernel (more would push the gate/up rows still in use out of L2).
+constexpr int kPrefetchUnits = 4;
+constexpr int64_t kDownPrefetchBytes = 48ll << 20;
 
 // Routing source: the router's logits (plan path) or a prepared table (the
 // op-level mirrors of expert_ffn_one).
@@ -151,7 +82,7 @@ __device__ __forceinline__ bool wait_ready(uint64_t* ready, ErrorWord* err, int 
 template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     gate_up_decode_kernel(const float* __restrict__ x, int T, int H, int F, int S, Rows gate, Rows up, Rows sgate,
-                          Rows sup, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
+                          Rows sup, Rows down, Rows sdown, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
                           __nv_bfloat16* __restrict__ act_s, ErrorWord* err) {
   using Fm = Fmt<Rows>;
   constexpr int kChunkMax = chunk_count<MaxT>();
@@ -195,17 +126,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < MaxT; ++j) {
         if (j >= ntok) break;
         const float* xr = xs + static_cast<size_t>(toks == nullptr ? j : toks[j]) * H;
-        float pg = 0.0f, pu = 0.0f;
 #pragma unroll
         for (int c = 0; c < kChunkMax; ++c) {
           const int idx = pass + lane + 32 * c;
           if (idx < nchunks) {
-            pg += Fm::dot_x(wg[c], xr + idx * Fm::kPerChunk);
-            pu += Fm::dot_x(wu[c], xr + idx * Fm::kPerChunk);
+            gacc[j] += Fm::dot_x(wg[c], xr + idx * Fm::kPerChunk);
+            uacc[j] += Fm::dot_x(wu[c], xr + idx * Fm::kPerChunk);
           }
         }
-        gacc[j] += pg;
-        uacc[j] += pu;
       }
     }
 #pragma unroll
@@ -217,17 +145,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
 
+  const uint32_t xrow_bytes = static_cast<uint32_t>(H) * Fm::kElemBytes;
   for (int f = gw; f < S; f += GW)
     unit(Fm::row(sgate, f), Fm::row(sup, f), Fm::scale(sgate, f), Fm::scale(sup, f), T, nullptr, act_s + f, S);
   if (!wait_ready(&route_ready, err, 12)) return;
   pdl_launch_dependents();
   const int U = sroute.count;
+  auto routed_row = [&](int q) { return static_cast<int64_t>(sroute.expert[q / F]) * F + q % F; };
+  if (lane == 0)
+    for (int k = 0; k < kPrefetchUnits; ++k) {
+      const int q = gw + k * GW;
+      if (q >= U * F) break;
+      prefetch_l2(Fm::row(gate, routed_row(q)), xrow_bytes);
+      prefetch_l2(Fm::row(up, routed_row(q)), xrow_bytes);
+    }
   for (int q = gw; q < U * F; q += GW) {
+    const int qn = q + kPrefetchUnits * GW;
+    if (lane == 0 && qn < U * F) {
+      prefetch_l2(Fm::row(gate, routed_row(qn)), xrow_bytes);
+      prefetch_l2(Fm::row(up, routed_row(qn)), xrow_bytes);
+    }
     const int u = q / F, f = q % F;
     const int64_t row = static_cast<int64_t>(sroute.expert[u]) * F + f;
     const int base = sroute.base[u];
     unit(Fm::row(gate, row), Fm::row(up, row), Fm::scale(gate, row), Fm::scale(up, row), sroute.ntok[u],
          sroute.slot_tok + base, act + static_cast<int64_t>(base) * F + f, F);
+  }
+  // The down kernel's warp gw takes output channels gw, gw + GW, ...: bring
+  // their shared and expert rows into L2 now, while the other warps finish.
+  if (lane == 0) {
+    const int64_t per_expert = static_cast<int64_t>(H) * F * Fm::kElemBytes;
+    const int64_t shared_bytes = static_cast<int64_t>(H) * S * Fm::kElemBytes;
+    int ucap = static_cast<int>((kDownPrefetchBytes - shared_bytes) / (per_expert > 0 ? per_expert : 1));
+    ucap = ucap < 0 ? 0 : (ucap > U ? U : ucap);
+    for (int ch = gw; ch < H; ch += GW) {
+      if (S > 0) prefetch_l2(Fm::row(sdown, ch), static_cast<uint32_t>(S) * Fm::kElemBytes);
+      for (int u = 0; u < ucap; ++u)
+        prefetch_l2(Fm::row(down, static_cast<int64_t>(sroute.expert[u]) * H + ch),
+                    static_cast<uint32_t>(F) * Fm::kElemBytes);
+    }
   }
 }
 
@@ -241,7 +197,7 @@ template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     down_decode_kernel(int T, int H, int F, int S, Rows down, Rows sdown, RouteSrc rsrc,
                        const __nv_bfloat16* __restrict__ act, const __nv_bfloat16* __restrict__ act_s,
-                       const float* resid, float* y, ErrorWord* err) {
+                       const float* resid, float* y, ErrorWord* err, DecodeNext next) {
   using Fm = Fmt<Rows>;
   constexpr int kChunkMax = chunk_count<MaxT>();
   constexpr int kHalf = kChunkMax / 2;
@@ -289,13 +245,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < MaxT; ++t) {
           if (t >= T) break;
           const __nv_bfloat16* ar = act_s + static_cast<int64_t>(t) * S;
-          float p = 0.0f;
 #pragma unroll
           for (int q = 0; q < kChunkMax; ++q) {
             const int idx = pass + lane + 32 * q;
-            if (idx < nch_s) p += Fm::dot_act(w[q], ar + idx * Fm::kPerChunk);
+            if (idx < nch_s) acc[t] += Fm::dot_act(w[q], ar + idx * Fm::kPerChunk);
           }
-          acc[t] += p;
         }
       }
       const float sc = Fm::scale(sdown, c);
@@ -340,25 +294,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < MaxT; ++j) {
           if (j >= n0) break;
           const __nv_bfloat16* ar = act + static_cast<int64_t>(b0 + j) * F;
-          float p = 0.0f;
 #pragma unroll
           for (int q = 0; q < kHalf; ++q) {
             const int idx = pass + lane + 32 * q;
-            if (idx < nch_f) p += Fm::dot_act(w0[q], ar + idx * Fm::kPerChunk);
+            if (idx < nch_f) a0[j] += Fm::dot_act(w0[q], ar + idx * Fm::kPerChunk);
           }
-          a0[j] += p;
         }
 #pragma unroll
         for (int j = 0; j < MaxT; ++j) {
           if (j >= n1) break;
           const __nv_bfloat16* ar = act + static_cast<int64_t>(b1 + j) * F;
-          float p = 0.0f;
 #pragma unroll
           for (int q = 0; q < kHalf; ++q) {
             const int idx = pass + lane + 32 * q;
-            if (idx < nch_f) p += Fm::dot_act(w1[q], ar + idx * Fm::kPerChunk);
+            if (idx < nch_f) a1[j] += Fm::dot_act(w1[q], ar + idx * Fm::kPerChunk);
           }
-          a1[j] += p;
         }
       }
       const float s0 = Fm::scale(down, r0), s1 = Fm::scale(down, r1);
@@ -387,6 +337,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       y[o] = resid != nullptr ? __fadd_rn(resid[o], sum[t]) : sum[t];
     }
     __syncwarp();
+  }
+  // The next layer of a stack: its router rows and shared gate/up rows start
+  // towards L2 now, ahead of its router and gate/up kernels.
+  if (lane == 0 && next.router != nullptr) {
+    for (int e = gw; e < rsrc.E; e += GW)
+      prefetch_l2(next.router + static_cast<int64_t>(e) * H, static_cast<uint32_t>(H) * 4);
+    for (int f = gw; f < S; f += GW) {
+      prefetch_l2(static_cast<const char*>(next.sgate) + f * next.srow_bytes, static_cast<uint32_t>(next.srow_bytes));
+      prefetch_l2(static_cast<const char*>(next.sup) + f * next.srow_bytes, static_cast<uint32_t>(next.srow_bytes));
+    }
   }
 }
 
@@ -431,7 +391,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
                                     Rows sgate, Rows sup, Rows sdown, const DecodeRouting& routing,
                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                     ErrorWord* err, int sm_count, cudaStream_t stream, cudaEvent_t between,
-                                    bool pdl) {
+                                    bool pdl, const DecodeNext* next) {
   cudaError_t st = prepare_kernels<Rows>();
   if (st != cudaSuccess) return st;
   RouteSrc rs{routing.logits, routing.table, routing.experts, routing.top_k, routing.renormalize, routing.ids_out,
@@ -441,7 +401,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   const void* dn = nullptr;
   pick_kernels<Rows>(T, &gu, &dn);
   {
-    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &rs, &act, &act_s, &err};
+    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &down, &sdown, &rs, &act, &act_s, &err};
     st = launch_maybe_pdl(gu, dim3(sm_count),
                           dim3(kThreads), smem, stream, args, pdl);
     if (st != cudaSuccess) return st;
@@ -452,7 +412,8 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   }
   rs.ids_out = nullptr;
   rs.w_out = nullptr;
-  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err};
+  DecodeNext nx = next != nullptr ? *next : DecodeNext{nullptr, nullptr, nullptr, 0};
+  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err, &nx};
   return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), 0,
                           stream, args, pdl && between == nullptr);
 }
@@ -479,19 +440,20 @@ cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int 
                                        const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
                                        const __nv_bfloat16* sdown, const DecodeRouting& routing, __nv_bfloat16* act,
                                        __nv_bfloat16* act_s, const float* resid, float* y, ErrorWord* err,
-                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl) {
+                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl,
+                                       const DecodeNext* next) {
   return launch_decode_experts_t<Bf16Rows>(x, T, H, F, S, Bf16Rows{gate, H}, Bf16Rows{up, H}, Bf16Rows{down, F},
                                            Bf16Rows{sgate, H}, Bf16Rows{sup, H}, Bf16Rows{sdown, S}, routing, act,
-                                           act_s, resid, y, err, sm_count, stream, between, pdl);
+                                           act_s, resid, y, err, sm_count, stream, between, pdl, next);
 }
 
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
                                      Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
                                      const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
                                      const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between, bool pdl) {
+                                     cudaEvent_t between, bool pdl, const DecodeNext* next) {
   return launch_decode_experts_t<Q8Rows>(x, T, H, F, S, gate, up, down, sgate, sup, sdown, routing, act, act_s,
-                                         resid, y, err, sm_count, stream, between, pdl);
+                                         resid, y, err, sm_count, stream, between, pdl, next);
 }
 
 cudaError_t prepare_decode_experts(int max_rows, int H) {

@@ -1,0 +1,108 @@
+// Weight-row access shared by the decode kernels (decode.cu,
+// decode_persistent.cu): streaming 16-byte loads and the dot products of one
+// chunk of bf16 or per-channel int8 weights against fp32 or bf16 inputs.
+#pragma once
+
+#include "moe_common.cuh"
+
+namespace uocr_b200 {
+
+// Weights are read once per step and never reused from L1.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Asks the TMA unit to bring `bytes` (a multiple of 16, 16-byte aligned
+// address) from HBM into L2: no registers or shared memory held, so a warp can
+// keep many rows on their way while it works on earlier ones.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <bool Cg>
+__device__ __forceinline__ uint4 ld_act(const uint4* p) {
+  if constexpr (Cg)
+    return __ldcg(p);
+  else
+    return __ldg(p);
+}
+
+// How the decode kernels read one weight format: rows of 16-byte chunks
+// (8 bf16 or 16 int8 weights) and the per-row scale.
+template <typename Rows>
+struct Fmt;
+
+template <>
+struct Fmt<Bf16Rows> {
+  static constexpr int kElemBytes = 2;
+  static constexpr int kPerChunk = 8;  // weights per 16 bytes
+  __device__ static const uint4* row(const Bf16Rows& r, int64_t i) {
+    return reinterpret_cast<const uint4*>(r.w + i * r.cols);
+  }
+  __device__ static float scale(const Bf16Rows&, int64_t) { return 1.0f; }
+  // 16 bytes of weights against fp32 inputs in shared memory
+  __device__ static float dot_x(const uint4& w, const float* x) {
+    const float4 x0 = reinterpret_cast<const float4*>(x)[0];
+    const float4 x1 = reinterpret_cast<const float4*>(x)[1];
+    return dot8_bf16(w, x0, x1);
+  }
+  // 16 bytes of weights against bf16 activations in global memory; Cg reads
+  // them through L2 only (activations written earlier in the same kernel).
+  template <bool Cg = false>
+  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
+    return dot8_bf16_bf16(w, ld_act<Cg>(reinterpret_cast<const uint4*>(act)));
+  }
+};
+
+template <>
+struct Fmt<Q8Rows> {
+  static constexpr int kElemBytes = 1;
+  static constexpr int kPerChunk = 16;
+  __device__ static const uint4* row(const Q8Rows& r, int64_t i) {
+    return reinterpret_cast<const uint4*>(r.q + i * r.cols);
+  }
+  __device__ static float scale(const Q8Rows& r, int64_t i) { return __ldg(r.scale + i); }
+  __device__ static float dot_x(const uint4& w, const float* x) {
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    float s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float a, b, c, d;
+      i8x4_to_f32(words[q], a, b, c, d);
+      const float4 xv = reinterpret_cast<const float4*>(x)[q];
+      s = fmaf(a, xv.x, s);
+      s = fmaf(b, xv.y, s);
+      s = fmaf(c, xv.z, s);
+      s = fmaf(d, xv.w, s);
+    }
+    return s;
+  }
+  template <bool Cg = false>
+  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    const uint4 a0 = ld_act<Cg>(reinterpret_cast<const uint4*>(act));
+    const uint4 a1 = ld_act<Cg>(reinterpret_cast<const uint4*>(act) + 1);
+    const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&a0);
+    const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&a1);
+    float s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float a, b, c, d;
+      i8x4_to_f32(words[q], a, b, c, d);
+      const __nv_bfloat162* p = q < 2 ? p0 : p1;
+      const float2 f0 = __bfloat1622float2(p[(q & 1) * 2]);
+      const float2 f1 = __bfloat1622float2(p[(q & 1) * 2 + 1]);
+      s = fmaf(a, f0.x, s);
+      s = fmaf(b, f0.y, s);
+      s = fmaf(c, f1.x, s);
+      s = fmaf(d, f1.y, s);
+    }
+    return s;
+  }
+};
+
+}  // namespace uocr_b200

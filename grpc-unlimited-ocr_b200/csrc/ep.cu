@@ -5,6 +5,7 @@
 // only this GPU's xrecv / act.
 #include "ep.h"
 
+#include "combine.cuh"
 #include "moe_kernels.h"
 #include "ptx.cuh"
 
@@ -133,8 +134,8 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
 }
 
 // y[t, c] = shared[t, c] + sum over t's experts in ascending id of w * (the
-// owner's yrecv row), + resid: the single-GPU combine's additions in the same
-// order, with the rows read from the owners. One block per row.
+// owner's yrecv row), + resid: the single-GPU combine (combine.cuh) with the
+// rows read from the owners. One block per row.
 __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, EpMap m, EpPeers peers, EpLayout lay,
                                                          const int* __restrict__ ids,
                                                          const float* __restrict__ weights,
@@ -143,57 +144,25 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, Ep
                                                          const float* shared_out, const float* resid, float* y) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  int eid[kMaxTopK];
-  int64_t row[kMaxTopK];
-  float w[kMaxTopK];
-  for (int j = 0; j < K; ++j) {
-    eid[j] = ids[static_cast<int64_t>(t) * K + j];
-    w[j] = weights[static_cast<int64_t>(t) * K + j];
+  CombineRow r;
+  r.n = K;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j >= K) break;
+    const int e = ids[static_cast<int64_t>(t) * K + j];
     const int p = pos_of[static_cast<int64_t>(t) * K + j];
-    row[j] = (p < 0 || eid[j] < 0 || eid[j] >= m.experts) ? -1 : static_cast<int64_t>(remote_base[eid[j]]) + p;
+    r.eid[j] = e;
+    r.w[j] = weights[static_cast<int64_t>(t) * K + j];
+    r.src[j] = (p < 0 || e < 0 || e >= m.experts)
+                   ? nullptr
+                   : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner(e)] + lay.yrecv) +
+                         (static_cast<int64_t>(remote_base[e]) + p) * H;
   }
-  for (int a = 1; a < K; ++a)
-    for (int b = a; b > 0 && eid[b] < eid[b - 1]; --b) {
-      const int te = eid[b];
-      const int64_t tr = row[b];
-      const float tw = w[b];
-      eid[b] = eid[b - 1];
-      row[b] = row[b - 1];
-      w[b] = w[b - 1];
-      eid[b - 1] = te;
-      row[b - 1] = tr;
-      w[b - 1] = tw;
-    }
-  const __nv_bfloat16* src[kMaxTopK];
-  for (int j = 0; j < K; ++j)
-    src[j] = row[j] < 0 ? nullptr
-                        : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner(eid[j])] + lay.yrecv) + row[j] * H;
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-    uint4 pk[kMaxTopK];
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-      if (j < K && src[j] != nullptr) pk[j] = ld_cg16(src[j] + c);
-    float routed[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j >= K || src[j] == nullptr) continue;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(h[q]);
-        routed[2 * q] = __fadd_rn(routed[2 * q], __fmul_rn(w[j], f.x));
-        routed[2 * q + 1] = __fadd_rn(routed[2 * q + 1], __fmul_rn(w[j], f.y));
-      }
-    }
-    const int64_t o = static_cast<int64_t>(t) * H + c;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float sh = shared_out != nullptr ? shared_out[o + q] : 0.0f;
-      float out = __fadd_rn(sh, routed[q]);
-      if (resid != nullptr) out = __fadd_rn(resid[o + q], out);
-      y[o + q] = out;
-    }
-  }
+  sort_selections(r);
+  const int64_t o = static_cast<int64_t>(t) * H;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+    combine_cols8(r, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
+                  y + o);
 }
 
 __global__ void ep_arrive_kernel(EpPeers peers, EpLayout lay, int rank, int world, unsigned* epoch) {

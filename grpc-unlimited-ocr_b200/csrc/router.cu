@@ -15,6 +15,8 @@
 namespace uocr_b200 {
 namespace {
 
+constexpr int kStageUnroll = 4;  // float4 loads in flight per thread while staging
+
 // One block per expert row of the router: logits[t, e] for every row t of
 // the batch, in the reference's dot order. Launched with programmatic
 // dependent launch: the router row is staged before waiting for the previous
@@ -29,10 +31,36 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
   const int xstride = H + 8;  // rows 8 floats apart: the four rows a warp reads sit in different banks
   float* ws = smem;
   float* xs = smem + H;
-  for (int i = tid; i < H; i += blockDim.x) ws[i] = __ldg(router + static_cast<int64_t>(e) * H + i);
+  // 16-byte loads, all of a thread's issued before any is stored: one DRAM
+  // round trip for the row instead of one per element step.
+  const int h4 = H / 4;
+  {
+    const float4* src = reinterpret_cast<const float4*>(router + static_cast<int64_t>(e) * H);
+    float4 v[kStageUnroll];
+    for (int i0 = tid; i0 < h4; i0 += blockDim.x * kStageUnroll) {
+#pragma unroll
+      for (int u = 0; u < kStageUnroll; ++u)
+        if (i0 + u * static_cast<int>(blockDim.x) < h4) v[u] = __ldg(src + i0 + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < kStageUnroll; ++u)
+        if (i0 + u * static_cast<int>(blockDim.x) < h4) reinterpret_cast<float4*>(ws)[i0 + u * blockDim.x] = v[u];
+    }
+  }
   pdl_wait();  // x is written by the previous grid
   pdl_launch_dependents();
-  for (int i = tid; i < T * H; i += blockDim.x) xs[(i / H) * xstride + (i % H)] = __ldcg(x + i);
+  for (int i0 = tid; i0 < T * h4; i0 += blockDim.x * kStageUnroll) {
+    float4 v[kStageUnroll];
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < T * h4) v[u] = __ldcg(reinterpret_cast<const float4*>(x) + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kStageUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < T * h4) reinterpret_cast<float4*>(xs + (i / h4) * xstride)[i % h4] = v[u];
+    }
+  }
   __syncthreads();
 
   const int lane8 = tid & 7;

@@ -111,7 +111,8 @@ TC_SHAPES = [(1, 256, 8, 3, 128, 128, True, 0), (5, 128, 128, 8, 128, 0, True, 0
 
 
 @pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt,flags",
-                         [s + (0,) for s in SMALL_SHAPES + TC_SHAPES] + [s + (M.PLAN_TENSOR_DECODE,) for s in TC_SHAPES])
+                         [s + (0,) for s in SMALL_SHAPES + TC_SHAPES] + [s + (M.PLAN_TENSOR_DECODE,) for s in TC_SHAPES]
+                         + [s + (M.PLAN_PERSISTENT_DECODE,) for s in SMALL_SHAPES])
 def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt, flags):
     import torch
     rng = np.random.default_rng(T * 7919 + E)
@@ -166,12 +167,17 @@ def c1_layer(cuda):
     return cfg, t, host_weights(t)
 
 
-@pytest.mark.parametrize("tc", [False, True], ids=["cuda_cores", "tensor_cores"])
+# The decode kernel sets: per-layer launches (default), one persistent launch,
+# and the tensor-core GEMV variant.
+DECODE_PATHS = {"layered": 0, "persistent": M.PLAN_PERSISTENT_DECODE, "tensor_cores": M.PLAN_TENSOR_DECODE}
+
+
+@pytest.mark.parametrize("path", list(DECODE_PATHS))
 @pytest.mark.parametrize("T", [1, 4, 8, 16])
-def test_config1_layer_bf16(cuda, c1_layer, T, tc):
+def test_config1_layer_bf16(cuda, c1_layer, T, path):
     import torch
     cfg, t, hw = c1_layer
-    plan = M.Plan(cfg.dims(layers=1), max_rows=16, renormalize=True, flags=M.PLAN_TENSOR_DECODE if tc else 0)
+    plan = M.Plan(cfg.dims(layers=1), max_rows=16, renormalize=True, flags=DECODE_PATHS[path])
     C.load_layer(plan, cfg, 0, t)
     x = C.device_input(cfg, T)
     y, ids, _ = run_plan(plan, 0, x, cfg.top_k, torch)
@@ -182,13 +188,15 @@ def test_config1_layer_bf16(cuda, c1_layer, T, tc):
     assert err <= BF16_TOL
 
 
+@pytest.mark.parametrize("path", ["persistent", "layered"])
 @pytest.mark.parametrize("T", [1, 8])
-def test_config2_layer_int8(cuda, c1_layer, T):
+def test_config2_layer_int8(cuda, c1_layer, T, path):
     import torch
     cfg = C.CONFIGS[2]
     t = C.device_layer(cfg, 0)
     hw = host_weights(t)
-    plan = M.Plan(cfg.dims(layers=1), max_rows=16, weight_format=M.WEIGHT_INT8, renormalize=True)
+    plan = M.Plan(cfg.dims(layers=1), max_rows=16, weight_format=M.WEIGHT_INT8, renormalize=True,
+                  flags=DECODE_PATHS[path])
     C.load_layer(plan, cfg, 0, t)
     x = C.device_input(cfg, T)
     y, ids, _ = run_plan(plan, 0, x, cfg.top_k, torch)
@@ -202,11 +210,12 @@ def test_config2_layer_int8(cuda, c1_layer, T):
     assert err <= INT8_TOL
 
 
-def test_stack_residual_two_layers(cuda):
+@pytest.mark.parametrize("path", ["persistent", "layered"])
+def test_stack_residual_two_layers(cuda, path):
     import torch
     cfg = C.CONFIGS[1]
     layers = [C.device_layer(cfg, l) for l in range(2)]
-    plan = M.Plan(cfg.dims(layers=2), max_rows=8)
+    plan = M.Plan(cfg.dims(layers=2), max_rows=8, flags=DECODE_PATHS[path])
     for l, t in enumerate(layers):
         C.load_layer(plan, cfg, l, t)
     x = C.device_input(cfg, 4)
@@ -219,15 +228,46 @@ def test_stack_residual_two_layers(cuda):
     assert max_rel(to_np(h), want) <= BF16_TOL
 
 
-@pytest.mark.parametrize("tc", [False, True], ids=["cuda_cores", "tensor_cores"])
-def test_stack_graph_replay_matches_plain_launches(cuda, tc):
+@pytest.mark.parametrize("fmt", [M.WEIGHT_BF16, M.WEIGHT_INT8])
+@pytest.mark.parametrize("T", [1, 3, 8, 16])
+def test_persistent_stack_equals_layered_launches(cuda, T, fmt):
+    """The one-launch stack and the per-layer kernels do the same arithmetic in
+    the same order: bitwise equal outputs, and the same last-layer ids."""
+    import torch
+    cfg = C.CONFIGS[1 if fmt == M.WEIGHT_BF16 else 2]
+    layers = [C.device_layer(cfg, l) for l in range(3)]
+    plans = [M.Plan(cfg.dims(layers=3), max_rows=16, weight_format=fmt, flags=f)
+             for f in (M.PLAN_PERSISTENT_DECODE, M.PLAN_NO_GRAPHS)]
+    for p in plans:
+        for l, t in enumerate(layers):
+            C.load_layer(p, cfg, l, t)
+    x = C.device_input(cfg, T)
+    outs = []
+    for p in plans:
+        h = x.clone()
+        for _ in range(2):
+            h.copy_(x)
+            p.forward_stack(h)
+        p.check()
+        y = torch.empty_like(x)
+        ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=cuda)
+        p.forward(2, h, y, ids)
+        p.check()
+        outs.append((h, y, ids))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(outs[0][2], outs[1][2])
+
+
+@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
+def test_stack_graph_replay_matches_plain_launches(cuda, path):
     """forward_stack on a capturable stream is captured once (with programmatic
     dependent launches between the kernels) and replayed; the replays give the
     bits of plain stream-ordered launches."""
     import torch
     cfg = C.CONFIGS[1]
     layers = [C.device_layer(cfg, l) for l in range(3)]
-    extra = M.PLAN_TENSOR_DECODE if tc else 0
+    extra = DECODE_PATHS[path]
     graphed = M.Plan(cfg.dims(layers=3), max_rows=8, flags=extra)
     plain = M.Plan(cfg.dims(layers=3), max_rows=8, flags=extra | M.PLAN_NO_GRAPHS)
     for l, t in enumerate(layers):
