@@ -184,20 +184,21 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0):
+def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0, strided=False):
     """one MoE layer over 32768 rows (8 pages x 4096),
     Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and the
     gate/up GEMM against the bf16 tensor roofline. With world > 1 the layer
     runs expert-parallel: each rank holds 64 / world experts and 32768 / world
     rows (strong scaling), and the time is the max over ranks. `rows` shrinks
-    the batch (profiling captures only)."""
+    the batch (profiling captures only); `strided` assigns expert e to rank
+    e % world instead of contiguous ranges."""
     import torch
     cfg = C.CONFIGS[3]
     total = rows or cfg.rows[0]
     import ep
     start, T = ep.rows_of(total, world, rank)
     plan = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0,
-                  ep_world=world if world > 1 else 0, ep_rank=rank)
+                  ep_world=world if world > 1 else 0, ep_rank=rank, flags=M.PLAN_EP_STRIDED if strided else 0)
     t = C.device_layer(cfg, 0, device=dev)
     C.load_layer(plan, cfg, 0, t)
     if world > 1:
@@ -259,9 +260,10 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
                            "algorithmic_flops_per_layer": total_flops}
     else:
         per_gpu = total_flops / (ms * 1e-3) / 1e12 / world
-        owner_rows = [sum(counts[e] for e in ep.local_experts(r, cfg.experts, world)) for r in range(world)]
-        out["parallelism"] = f"expert-parallel x{world}: {cfg.experts // world} experts and {total // world} rows " \
-                             "per GPU; rows and outputs pulled over NVLink by peer loads"
+        owner_rows = [sum(counts[e] for e in ep.local_experts(r, cfg.experts, world, strided)) for r in range(world)]
+        out["parallelism"] = f"expert-parallel x{world}: {cfg.experts // world} experts " \
+                             f"({'e % G' if strided else 'contiguous ranges'}) and {total // world} rows per GPU; " \
+                             "rows and outputs pulled over NVLink by peer loads"
         out["roofline"] = {"bound": "tensor", "kernel": "whole layer per GPU", "achieved": per_gpu, "peak": peak,
                            "peak_source": peak_src, "unit": "TFLOP/s", "frac": per_gpu / peak,
                            "algorithmic_flops_per_layer": total_flops}
@@ -464,6 +466,12 @@ def main():
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
                               want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
                               rows=args.prefill_rows, world=world, rank=rank)
+        if world > 1:
+            # Ablation: the Zipf-hot experts spread over the ranks (e % G).
+            alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
+                              rows=args.prefill_rows, world=world, rank=rank, strided=True)
+            prefill["ablation_strided_experts"] = {k: alt[k] for k in ("value", "ms_per_layer", "kernel_ms",
+                                                                     "rows_received_per_rank", "parallelism")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -623,13 +623,6 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
   const DecodeRouting routing{p->logits, nullptr, E, K, d.renormalize, p->ids, p->weights};
-  // In a stack, the down kernel starts the next layer's router and shared
-  // rows towards L2.
-  DecodeNext next{nullptr, nullptr, nullptr, 0};
-  if (resid != nullptr && li + 1 < static_cast<int64_t>(p->layers.size())) {
-    const LayerDev& N = p->layers[static_cast<size_t>(li + 1)];
-    next = DecodeNext{N.router, N.sgate, N.sup, static_cast<int64_t>(d.hidden) * static_cast<int64_t>(p->elem_bytes())};
-  }
   if (p->decode_tc) {
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     DecodeTcCall c{};
@@ -658,14 +651,14 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
                                         b(L.sdown), routing, p->act, p->act_s, resid, y, p->err, p->sm_count,
-                                        stream, between, pdl, &next),
+                                        stream, between, pdl),
              "forward: experts");
   } else {
     auto q = [](void* v, float* s, int64_t cols) { return Q8Rows{static_cast<const int8_t*>(v), s, cols}; };
     UOCR_TRY(launch_decode_experts_q8(x, T, H, F, S, q(L.gate, L.gate_s, H), q(L.up, L.up_s, H),
                                       q(L.down, L.down_s, F), q(L.sgate, L.sgate_s, H), q(L.sup, L.sup_s, H),
                                       q(L.sdown, L.sdown_s, S), routing, p->act, p->act_s, resid, y, p->err,
-                                      p->sm_count, stream, between, pdl, &next),
+                                      p->sm_count, stream, between, pdl),
              "forward: experts");
   }
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[2], stream), "forward: event");

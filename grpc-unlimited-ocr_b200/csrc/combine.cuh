@@ -43,10 +43,21 @@ __device__ __forceinline__ void sort_selections(CombineRow& r) {
 // any is added (src[j] null: a dropped selection).
 __device__ __forceinline__ void combine_cols8(const CombineRow& r, int64_t c, const float* shared_row,
                                               const float* resid_row, float* y_row) {
+  // Every load of the 8 columns first (expert rows, shared output, residual),
+  // then the arithmetic.
   uint4 pk[kMaxTopK];
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j)
     if (j < r.n && r.src[j] != nullptr) pk[j] = __ldcg(reinterpret_cast<const uint4*>(r.src[j] + c));
+  float4 sa = make_float4(0, 0, 0, 0), sb = sa, ra = sa, rb = sa;
+  if (shared_row != nullptr) {
+    sa = __ldcg(reinterpret_cast<const float4*>(shared_row + c));
+    sb = __ldcg(reinterpret_cast<const float4*>(shared_row + c) + 1);
+  }
+  if (resid_row != nullptr) {
+    ra = __ldcg(reinterpret_cast<const float4*>(resid_row + c));
+    rb = __ldcg(reinterpret_cast<const float4*>(resid_row + c) + 1);
+  }
   float routed[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) {
@@ -59,17 +70,8 @@ __device__ __forceinline__ void combine_cols8(const CombineRow& r, int64_t c, co
       routed[2 * q + 1] = __fadd_rn(routed[2 * q + 1], __fmul_rn(r.w[j], f.y));
     }
   }
-  float sh[8] = {0, 0, 0, 0, 0, 0, 0, 0}, rs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (shared_row != nullptr) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(shared_row + c));
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(shared_row + c) + 1);
-    sh[0] = a.x; sh[1] = a.y; sh[2] = a.z; sh[3] = a.w; sh[4] = b.x; sh[5] = b.y; sh[6] = b.z; sh[7] = b.w;
-  }
-  if (resid_row != nullptr) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(resid_row + c));
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(resid_row + c) + 1);
-    rs[0] = a.x; rs[1] = a.y; rs[2] = a.z; rs[3] = a.w; rs[4] = b.x; rs[5] = b.y; rs[6] = b.z; rs[7] = b.w;
-  }
+  const float sh[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+  const float rs[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
   float out[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) {

@@ -35,16 +35,9 @@ namespace {
 constexpr int kWorkers = 15;                   // streaming warps per block
 constexpr int kThreads = (kWorkers + 1) * 32;  // + the routing warp
 
-// 16-byte loads a lane issues per pass over a row: more when few batch rows
-// leave registers free.
+// 16-byte chunks per lane (and per matrix) in one pipelined step.
 template <int MaxT>
-constexpr int chunk_count() { return MaxT <= 4 ? 8 : 4; }
-
-// L2 prefetch: how many of its own units ahead a warp keeps on their way, and
-// how many bytes of down rows the gate/up kernel brings in for the down
-// kernel (more would push the gate/up rows still in use out of L2).
-constexpr int kPrefetchUnits = 4;
-constexpr int64_t kDownPrefetchBytes = 48ll << 20;
+constexpr int step_chunks() { return MaxT <= 4 ? 4 : 2; }
 
 // Routing source: the router's logits (plan path) or a prepared table (the
 // op-level mirrors of expert_ffn_one).
@@ -82,10 +75,9 @@ __device__ __forceinline__ bool wait_ready(uint64_t* ready, ErrorWord* err, int 
 template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     gate_up_decode_kernel(const float* __restrict__ x, int T, int H, int F, int S, Rows gate, Rows up, Rows sgate,
-                          Rows sup, Rows down, Rows sdown, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
+                          Rows sup, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
                           __nv_bfloat16* __restrict__ act_s, ErrorWord* err) {
   using Fm = Fmt<Rows>;
-  constexpr int kChunkMax = chunk_count<MaxT>();
   extern __shared__ __align__(16) float xs[];  // [T][H] bf16-rounded inputs
   __shared__ SmemRoute sroute;
   __shared__ uint64_t route_ready;
@@ -106,101 +98,105 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int gw = blockIdx.x * kWorkers + warp, GW = gridDim.x * kWorkers;
   const int nchunks = H * Fm::kElemBytes / 16;
 
-  // One (gate row, up row) pair against `ntok` batch rows.
-  auto unit = [&](const uint4* gr, const uint4* ur, float gsc, float usc, int ntok, const int* toks,
-                  __nv_bfloat16* out, int64_t out_stride) {
-    float gacc[MaxT], uacc[MaxT];
+  // The warp's work is a stream of jobs — one (gate row, up row) pair against
+  // `ntok` batch rows — cut into steps of kStep 16-byte chunks per lane and
+  // matrix. Software-pipelined two deep: the next step's loads are issued
+  // before this step's products, so the warp always has rows in flight.
+  constexpr int kStep = step_chunks<MaxT>();
+  const int spj = (nchunks + 32 * kStep - 1) / (32 * kStep);  // steps per job
+  struct Job {
+    const uint4* g;
+    const uint4* u;
+    float gs, us;
+    int ntok;
+    const int* toks;
+    __nv_bfloat16* out;
+    int64_t stride;
+  };
+  float gacc[MaxT], uacc[MaxT];
 #pragma unroll
-    for (int j = 0; j < MaxT; ++j) gacc[j] = uacc[j] = 0.0f;
-    for (int pass = 0; pass < nchunks; pass += 32 * kChunkMax) {
-      uint4 wg[kChunkMax], wu[kChunkMax];
+  for (int j = 0; j < MaxT; ++j) gacc[j] = uacc[j] = 0.0f;
+  auto run = [&](int njobs, auto&& job) {
+    const int nsteps = njobs * spj;
+    uint4 ga[kStep], ua[kStep], gb[kStep], ub[kStep];
+    auto issue = [&](int s, uint4 (&g)[kStep], uint4 (&u)[kStep]) {
+      const Job J = job(s / spj);
+      const int base = (s % spj) * 32 * kStep + lane;
 #pragma unroll
-      for (int c = 0; c < kChunkMax; ++c) {
-        const int idx = pass + lane + 32 * c;
+      for (int c = 0; c < kStep; ++c) {
+        const int idx = base + 32 * c;
         if (idx < nchunks) {
-          wg[c] = ld_stream(gr + idx);
-          wu[c] = ld_stream(ur + idx);
+          g[c] = ld_stream(J.g + idx);
+          u[c] = ld_stream(J.u + idx);
         }
       }
+    };
+    auto consume = [&](int s, const uint4 (&g)[kStep], const uint4 (&u)[kStep]) {
+      const Job J = job(s / spj);
+      const int base = (s % spj) * 32 * kStep + lane;
 #pragma unroll
       for (int j = 0; j < MaxT; ++j) {
-        if (j >= ntok) break;
-        const float* xr = xs + static_cast<size_t>(toks == nullptr ? j : toks[j]) * H;
+        if (j >= J.ntok) break;
+        const float* xr = xs + static_cast<size_t>(J.toks == nullptr ? j : J.toks[j]) * H;
 #pragma unroll
-        for (int c = 0; c < kChunkMax; ++c) {
-          const int idx = pass + lane + 32 * c;
+        for (int c = 0; c < kStep; ++c) {
+          const int idx = base + 32 * c;
           if (idx < nchunks) {
-            gacc[j] += Fm::dot_x(wg[c], xr + idx * Fm::kPerChunk);
-            uacc[j] += Fm::dot_x(wu[c], xr + idx * Fm::kPerChunk);
+            gacc[j] += Fm::dot_x(g[c], xr + idx * Fm::kPerChunk);
+            uacc[j] += Fm::dot_x(u[c], xr + idx * Fm::kPerChunk);
           }
         }
       }
-    }
+      if (s % spj == spj - 1) {
 #pragma unroll
-    for (int j = 0; j < MaxT; ++j) {
-      if (j >= ntok) break;
-      const float gv = warp_sum(gacc[j]) * gsc;
-      const float uv = warp_sum(uacc[j]) * usc;
-      if (lane == 0) out[j * out_stride] = __float2bfloat16_rn(swiglu(gv, uv));
+        for (int j = 0; j < MaxT; ++j) {
+          if (j < J.ntok) {
+            const float gv = warp_sum(gacc[j]) * J.gs;
+            const float uv = warp_sum(uacc[j]) * J.us;
+            if (lane == 0) J.out[j * J.stride] = __float2bfloat16_rn(swiglu(gv, uv));
+          }
+          gacc[j] = uacc[j] = 0.0f;
+        }
+      }
+    };
+    if (nsteps > 0) issue(0, ga, ua);
+    for (int s = 0; s < nsteps; s += 2) {
+      if (s + 1 < nsteps) issue(s + 1, gb, ub);
+      consume(s, ga, ua);
+      if (s + 2 < nsteps) issue(s + 2, ga, ua);
+      if (s + 1 < nsteps) consume(s + 1, gb, ub);
     }
   };
 
-  const uint32_t xrow_bytes = static_cast<uint32_t>(H) * Fm::kElemBytes;
-  for (int f = gw; f < S; f += GW)
-    unit(Fm::row(sgate, f), Fm::row(sup, f), Fm::scale(sgate, f), Fm::scale(sup, f), T, nullptr, act_s + f, S);
+  // Shared expert rows f = gw, gw + GW, ... (no routing needed).
+  run(S > gw ? (S - gw + GW - 1) / GW : 0, [&](int k) {
+    const int f = gw + k * GW;
+    return Job{Fm::row(sgate, f), Fm::row(sup, f), Fm::scale(sgate, f), Fm::scale(sup, f), T, nullptr, act_s + f, S};
+  });
   if (!wait_ready(&route_ready, err, 12)) return;
   pdl_launch_dependents();
   const int U = sroute.count;
-  auto routed_row = [&](int q) { return static_cast<int64_t>(sroute.expert[q / F]) * F + q % F; };
-  if (lane == 0)
-    for (int k = 0; k < kPrefetchUnits; ++k) {
-      const int q = gw + k * GW;
-      if (q >= U * F) break;
-      prefetch_l2(Fm::row(gate, routed_row(q)), xrow_bytes);
-      prefetch_l2(Fm::row(up, routed_row(q)), xrow_bytes);
-    }
-  for (int q = gw; q < U * F; q += GW) {
-    const int qn = q + kPrefetchUnits * GW;
-    if (lane == 0 && qn < U * F) {
-      prefetch_l2(Fm::row(gate, routed_row(qn)), xrow_bytes);
-      prefetch_l2(Fm::row(up, routed_row(qn)), xrow_bytes);
-    }
+  run(U * F > gw ? (U * F - gw + GW - 1) / GW : 0, [&](int k) {
+    const int q = gw + k * GW;
     const int u = q / F, f = q % F;
     const int64_t row = static_cast<int64_t>(sroute.expert[u]) * F + f;
     const int base = sroute.base[u];
-    unit(Fm::row(gate, row), Fm::row(up, row), Fm::scale(gate, row), Fm::scale(up, row), sroute.ntok[u],
-         sroute.slot_tok + base, act + static_cast<int64_t>(base) * F + f, F);
-  }
-  // The down kernel's warp gw takes output channels gw, gw + GW, ...: bring
-  // their shared and expert rows into L2 now, while the other warps finish.
-  if (lane == 0) {
-    const int64_t per_expert = static_cast<int64_t>(H) * F * Fm::kElemBytes;
-    const int64_t shared_bytes = static_cast<int64_t>(H) * S * Fm::kElemBytes;
-    int ucap = static_cast<int>((kDownPrefetchBytes - shared_bytes) / (per_expert > 0 ? per_expert : 1));
-    ucap = ucap < 0 ? 0 : (ucap > U ? U : ucap);
-    for (int ch = gw; ch < H; ch += GW) {
-      if (S > 0) prefetch_l2(Fm::row(sdown, ch), static_cast<uint32_t>(S) * Fm::kElemBytes);
-      for (int u = 0; u < ucap; ++u)
-        prefetch_l2(Fm::row(down, static_cast<int64_t>(sroute.expert[u]) * H + ch),
-                    static_cast<uint32_t>(F) * Fm::kElemBytes);
-    }
-  }
+    return Job{Fm::row(gate, row), Fm::row(up, row), Fm::scale(gate, row), Fm::scale(up, row), sroute.ntok[u],
+               sroute.slot_tok + base, act + static_cast<int64_t>(base) * F + f, F};
+  });
 }
 
 // ---------------------------------------------------------------------------
 // down + combine: one streaming warp per output channel c (grid-stride): the
 // shared down row against every batch row's shared activation, then the
-// selected experts' down rows two at a time (the second's loads in flight
-// while the first's dot products run), each finished in registers and added
-// to its rows' sums in ascending expert order.
+// selected experts' down rows, each finished in registers and added to its
+// rows' sums in ascending expert order.
 template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     down_decode_kernel(int T, int H, int F, int S, Rows down, Rows sdown, RouteSrc rsrc,
                        const __nv_bfloat16* __restrict__ act, const __nv_bfloat16* __restrict__ act_s,
-                       const float* resid, float* y, ErrorWord* err, DecodeNext next) {
+                       const float* resid, float* y, ErrorWord* err) {
   using Fm = Fmt<Rows>;
-  constexpr int kChunkMax = chunk_count<MaxT>();
-  constexpr int kHalf = kChunkMax / 2;
   __shared__ SmemRoute sroute;
   __shared__ uint64_t route_ready;
   __shared__ float row_sum[kWorkers][kDecodeMaxRows];
@@ -219,134 +215,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   const int gw = blockIdx.x * kWorkers + warp, GW = gridDim.x * kWorkers;
+  // A channel's rows — the shared row, then each selected expert's in
+  // ascending id — cut into steps of kStep chunks per lane and pipelined two
+  // deep (the next step's loads before this step's products). The first two
+  // steps are issued before waiting for the gate/up grid's activations.
+  constexpr int kStep = step_chunks<MaxT>();
   const int nch_s = S * Fm::kElemBytes / 16, nch_f = F * Fm::kElemBytes / 16;
+  const int spr_s = S > 0 ? (nch_s + 32 * kStep - 1) / (32 * kStep) : 0;
+  const int spr_f = (nch_f + 32 * kStep - 1) / (32 * kStep);
   float* sum = row_sum[warp];
   bool waited = false, have_route = false;
   for (int c = gw; c < H; c += GW) {
     if (lane < kDecodeMaxRows) sum[lane] = 0.0f;
     __syncwarp();
-    if (S > 0) {
-      const uint4* wr = Fm::row(sdown, c);
-      float acc[MaxT];
+    float acc[MaxT];
 #pragma unroll
-      for (int t = 0; t < MaxT; ++t) acc[t] = 0.0f;
-      for (int pass = 0; pass < nch_s; pass += 32 * kChunkMax) {
-        uint4 w[kChunkMax];
+    for (int j = 0; j < MaxT; ++j) acc[j] = 0.0f;
+    int nsteps = spr_s;  // + U * spr_f once the routing table is known
+    bool known = false;
+    auto learn = [&]() {
+      if (known) return true;
+      if (!have_route) {
+        if (!wait_ready(&route_ready, err, 24)) return false;
+        have_route = true;
+      }
+      nsteps = spr_s + sroute.count * spr_f;
+      known = true;
+      return true;
+    };
+    auto issue = [&](int st, uint4 (&w)[kStep]) {
+      const uint4* p;
+      int n, base;
+      if (st < spr_s) {
+        p = Fm::row(sdown, c);
+        n = nch_s;
+        base = st * 32 * kStep + lane;
+      } else {
+        const int r = (st - spr_s) / spr_f;
+        p = Fm::row(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
+        n = nch_f;
+        base = ((st - spr_s) % spr_f) * 32 * kStep + lane;
+      }
 #pragma unroll
-        for (int q = 0; q < kChunkMax; ++q) {
-          const int idx = pass + lane + 32 * q;
-          if (idx < nch_s) w[q] = ld_stream(wr + idx);
-        }
-        if (!waited) {
-          pdl_wait();  // the activations come from the gate/up grid
-          waited = true;
-        }
+      for (int q = 0; q < kStep; ++q)
+        if (base + 32 * q < n) w[q] = ld_stream(p + base + 32 * q);
+    };
+    auto consume = [&](int st, const uint4 (&w)[kStep]) {
+      if (!waited) {
+        pdl_wait();  // the activations come from the gate/up grid
+        waited = true;
+      }
+      if (st < spr_s) {
+        const int base = st * 32 * kStep + lane;
 #pragma unroll
         for (int t = 0; t < MaxT; ++t) {
           if (t >= T) break;
           const __nv_bfloat16* ar = act_s + static_cast<int64_t>(t) * S;
 #pragma unroll
-          for (int q = 0; q < kChunkMax; ++q) {
-            const int idx = pass + lane + 32 * q;
-            if (idx < nch_s) acc[t] += Fm::dot_act(w[q], ar + idx * Fm::kPerChunk);
+          for (int q = 0; q < kStep; ++q)
+            if (base + 32 * q < nch_s) acc[t] += Fm::dot_act(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+        }
+        if (st == spr_s - 1) {
+          const float sc = Fm::scale(sdown, c);
+#pragma unroll
+          for (int t = 0; t < MaxT; ++t) {
+            if (t < T) {
+              const float v = warp_sum(acc[t]) * sc;
+              if (lane == 0) sum[t] = v;
+            }
+            acc[t] = 0.0f;
           }
         }
+        return;
       }
-      const float sc = Fm::scale(sdown, c);
-#pragma unroll
-      for (int t = 0; t < MaxT; ++t) {
-        if (t >= T) break;
-        const float v = warp_sum(acc[t]) * sc;
-        if (lane == 0) sum[t] = v;
-      }
-    }
-    if (!waited) {
-      pdl_wait();
-      waited = true;
-    }
-    if (!have_route) {
-      if (!wait_ready(&route_ready, err, 24)) return;
-      have_route = true;
-    }
-    const int U = sroute.count;
-    for (int u0 = 0; u0 < U; u0 += 2) {
-      const bool two = u0 + 1 < U;
-      const int64_t r0 = static_cast<int64_t>(sroute.expert[u0]) * H + c;
-      const int64_t r1 = two ? static_cast<int64_t>(sroute.expert[u0 + 1]) * H + c : r0;
-      const int b0 = sroute.base[u0], n0 = sroute.ntok[u0];
-      const int b1 = two ? sroute.base[u0 + 1] : 0, n1 = two ? sroute.ntok[u0 + 1] : 0;
-      const uint4* p0 = Fm::row(down, r0);
-      const uint4* p1 = Fm::row(down, r1);
-      float a0[MaxT], a1[MaxT];
-#pragma unroll
-      for (int j = 0; j < MaxT; ++j) a0[j] = a1[j] = 0.0f;
-      for (int pass = 0; pass < nch_f; pass += 32 * kHalf) {
-        uint4 w0[kHalf], w1[kHalf];
-#pragma unroll
-        for (int q = 0; q < kHalf; ++q) {
-          const int idx = pass + lane + 32 * q;
-          if (idx < nch_f) {
-            w0[q] = ld_stream(p0 + idx);
-            if (two) w1[q] = ld_stream(p1 + idx);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < MaxT; ++j) {
-          if (j >= n0) break;
-          const __nv_bfloat16* ar = act + static_cast<int64_t>(b0 + j) * F;
-#pragma unroll
-          for (int q = 0; q < kHalf; ++q) {
-            const int idx = pass + lane + 32 * q;
-            if (idx < nch_f) a0[j] += Fm::dot_act(w0[q], ar + idx * Fm::kPerChunk);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < MaxT; ++j) {
-          if (j >= n1) break;
-          const __nv_bfloat16* ar = act + static_cast<int64_t>(b1 + j) * F;
-#pragma unroll
-          for (int q = 0; q < kHalf; ++q) {
-            const int idx = pass + lane + 32 * q;
-            if (idx < nch_f) a1[j] += Fm::dot_act(w1[q], ar + idx * Fm::kPerChunk);
-          }
-        }
-      }
-      const float s0 = Fm::scale(down, r0), s1 = Fm::scale(down, r1);
+      const int r = (st - spr_s) / spr_f, sr = (st - spr_s) % spr_f;
+      const int b0 = sroute.base[r], n0 = sroute.ntok[r];
+      const int base = sr * 32 * kStep + lane;
 #pragma unroll
       for (int j = 0; j < MaxT; ++j) {
         if (j >= n0) break;
-        const float v = warp_sum(a0[j]) * s0;
-        if (lane == 0) {
-          const int t = sroute.slot_tok[b0 + j];
-          sum[t] = __fadd_rn(sum[t], __fmul_rn(sroute.slot_w[b0 + j], v));
-        }
-      }
+        const __nv_bfloat16* ar = act + static_cast<int64_t>(b0 + j) * F;
 #pragma unroll
-      for (int j = 0; j < MaxT; ++j) {
-        if (j >= n1) break;
-        const float v = warp_sum(a1[j]) * s1;
-        if (lane == 0) {
-          const int t = sroute.slot_tok[b1 + j];
-          sum[t] = __fadd_rn(sum[t], __fmul_rn(sroute.slot_w[b1 + j], v));
+        for (int q = 0; q < kStep; ++q)
+          if (base + 32 * q < nch_f) acc[j] += Fm::dot_act(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+      }
+      if (sr == spr_f - 1) {
+        const float sc = Fm::scale(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
+#pragma unroll
+        for (int j = 0; j < MaxT; ++j) {
+          if (j < n0) {
+            const float v = warp_sum(acc[j]) * sc;
+            if (lane == 0) {
+              const int t = sroute.slot_tok[b0 + j];
+              sum[t] = __fadd_rn(sum[t], __fmul_rn(sroute.slot_w[b0 + j], v));
+            }
+          }
+          acc[j] = 0.0f;
         }
       }
+    };
+    uint4 wa[kStep], wb[kStep];
+    if (spr_s == 0 && !learn()) return;
+    if (nsteps > 0) issue(0, wa);
+    for (int st = 0; st < nsteps; st += 2) {
+      if (st + 1 >= spr_s && !learn()) return;
+      if (st + 1 < nsteps) issue(st + 1, wb);
+      consume(st, wa);
+      if (st + 2 >= spr_s && !learn()) return;
+      if (st + 2 < nsteps) issue(st + 2, wa);
+      if (st + 1 < nsteps) consume(st + 1, wb);
     }
+    if (!learn()) return;  // a channel with no rows to stream still needs its routing
     __syncwarp();
     for (int t = lane; t < T; t += 32) {
       const int64_t o = static_cast<int64_t>(t) * H + c;
       y[o] = resid != nullptr ? __fadd_rn(resid[o], sum[t]) : sum[t];
     }
     __syncwarp();
-  }
-  // The next layer of a stack: its router rows and shared gate/up rows start
-  // towards L2 now, ahead of its router and gate/up kernels.
-  if (lane == 0 && next.router != nullptr) {
-    for (int e = gw; e < rsrc.E; e += GW)
-      prefetch_l2(next.router + static_cast<int64_t>(e) * H, static_cast<uint32_t>(H) * 4);
-    for (int f = gw; f < S; f += GW) {
-      prefetch_l2(static_cast<const char*>(next.sgate) + f * next.srow_bytes, static_cast<uint32_t>(next.srow_bytes));
-      prefetch_l2(static_cast<const char*>(next.sup) + f * next.srow_bytes, static_cast<uint32_t>(next.srow_bytes));
-    }
   }
 }
 
@@ -391,7 +376,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
                                     Rows sgate, Rows sup, Rows sdown, const DecodeRouting& routing,
                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                     ErrorWord* err, int sm_count, cudaStream_t stream, cudaEvent_t between,
-                                    bool pdl, const DecodeNext* next) {
+                                    bool pdl) {
   cudaError_t st = prepare_kernels<Rows>();
   if (st != cudaSuccess) return st;
   RouteSrc rs{routing.logits, routing.table, routing.experts, routing.top_k, routing.renormalize, routing.ids_out,
@@ -401,7 +386,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   const void* dn = nullptr;
   pick_kernels<Rows>(T, &gu, &dn);
   {
-    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &down, &sdown, &rs, &act, &act_s, &err};
+    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &rs, &act, &act_s, &err};
     st = launch_maybe_pdl(gu, dim3(sm_count),
                           dim3(kThreads), smem, stream, args, pdl);
     if (st != cudaSuccess) return st;
@@ -412,8 +397,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   }
   rs.ids_out = nullptr;
   rs.w_out = nullptr;
-  DecodeNext nx = next != nullptr ? *next : DecodeNext{nullptr, nullptr, nullptr, 0};
-  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err, &nx};
+  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err};
   return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), 0,
                           stream, args, pdl && between == nullptr);
 }
@@ -440,20 +424,19 @@ cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int 
                                        const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
                                        const __nv_bfloat16* sdown, const DecodeRouting& routing, __nv_bfloat16* act,
                                        __nv_bfloat16* act_s, const float* resid, float* y, ErrorWord* err,
-                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl,
-                                       const DecodeNext* next) {
+                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl) {
   return launch_decode_experts_t<Bf16Rows>(x, T, H, F, S, Bf16Rows{gate, H}, Bf16Rows{up, H}, Bf16Rows{down, F},
                                            Bf16Rows{sgate, H}, Bf16Rows{sup, H}, Bf16Rows{sdown, S}, routing, act,
-                                           act_s, resid, y, err, sm_count, stream, between, pdl, next);
+                                           act_s, resid, y, err, sm_count, stream, between, pdl);
 }
 
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
                                      Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
                                      const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
                                      const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between, bool pdl, const DecodeNext* next) {
+                                     cudaEvent_t between, bool pdl) {
   return launch_decode_experts_t<Q8Rows>(x, T, H, F, S, gate, up, down, sgate, sup, sdown, routing, act, act_s,
-                                         resid, y, err, sm_count, stream, between, pdl, next);
+                                         resid, y, err, sm_count, stream, between, pdl);
 }
 
 cudaError_t prepare_decode_experts(int max_rows, int H) {

@@ -46,15 +46,6 @@ struct DecodeRouting {
   float* weights_out;
 };
 
-// Weights of the next layer of a stack, for the down kernel to start bringing
-// into L2 while the next router runs (all null: none).
-struct DecodeNext {
-  const float* router;  // [E, H] fp32
-  const void* sgate;    // [S, H] rows of srow_bytes
-  const void* sup;
-  int64_t srow_bytes;
-};
-
 // Launches gate/up then down+combine; `between` (optional) is recorded
 // between the two, for per-kernel timing.
 cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int S, const __nv_bfloat16* gate,
@@ -63,13 +54,12 @@ cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int 
                                        const __nv_bfloat16* sdown, const DecodeRouting& routing,
                                        __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                        ErrorWord* err, int sm_count, cudaStream_t stream,
-                                       cudaEvent_t between = nullptr, bool pdl = false,
-                                       const DecodeNext* next = nullptr);
+                                       cudaEvent_t between = nullptr, bool pdl = false);
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
                                      Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
                                      const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
                                      const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between = nullptr, bool pdl = false, const DecodeNext* next = nullptr);
+                                     cudaEvent_t between = nullptr, bool pdl = false);
 
 // ---- weights and synthetic inputs (weights.cu) ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
