@@ -109,7 +109,7 @@ struct uocr_moe_plan {
   DecodeRoute* route = nullptr;
   __nv_bfloat16* act = nullptr;
   __nv_bfloat16* act_s = nullptr;
-  unsigned* counter = nullptr;
+  unsigned* counter = nullptr;  // the decode router's last-block ticket
   ErrorWord* err = nullptr;
   // Prefill (rows above decode_rows): tcgen05 grouped GEMM path, bf16 weights.
   bool prefill = false;
@@ -619,10 +619,13 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   // Programmatic dependent launch chains router -> gate/up -> down (and the
   // next layer's router); the profiling path records events between them instead.
   const bool pdl = ev == nullptr;
-  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl), "forward: router");
+  // The router's last block builds the routing table once; the expert
+  // kernels copy it.
+  const RouteOut ro{p->route, K, d.renormalize, p->ids, p->weights, p->counter};
+  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl, &ro), "forward: router");
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
-  const DecodeRouting routing{p->logits, nullptr, E, K, d.renormalize, p->ids, p->weights};
+  const DecodeRouting routing{nullptr, p->route, E, K, d.renormalize, nullptr, nullptr};
   if (p->decode_tc) {
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     DecodeTcCall c{};

@@ -195,8 +195,12 @@ template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     down_decode_kernel(int T, int H, int F, int S, Rows down, Rows sdown, RouteSrc rsrc,
                        const __nv_bfloat16* __restrict__ act, const __nv_bfloat16* __restrict__ act_s,
-                       const float* resid, float* y, ErrorWord* err) {
+                       const float* resid, float* y, ErrorWord* err, int stage_act) {
   using Fm = Fmt<Rows>;
+  // stage_act: the block copies the activations (shared rows [T, S], then the
+  // routed slots [slots, F]) into shared memory once, so the products read
+  // them at shared-memory latency instead of one L2 round trip per step.
+  extern __shared__ __align__(16) __nv_bfloat16 act_sm[];
   __shared__ SmemRoute sroute;
   __shared__ uint64_t route_ready;
   __shared__ float row_sum[kWorkers][kDecodeMaxRows];
@@ -216,15 +220,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int gw = blockIdx.x * kWorkers + warp, GW = gridDim.x * kWorkers;
   // A channel's rows — the shared row, then each selected expert's in
-  // ascending id — cut into steps of kStep chunks per lane and pipelined two
-  // deep (the next step's loads before this step's products). The first two
+  // ascending id — cut into steps of kStep chunks per lane and pipelined four
+  // deep (three steps' loads in flight while one is multiplied). The first
   // steps are issued before waiting for the gate/up grid's activations.
   constexpr int kStep = step_chunks<MaxT>();
   const int nch_s = S * Fm::kElemBytes / 16, nch_f = F * Fm::kElemBytes / 16;
   const int spr_s = S > 0 ? (nch_s + 32 * kStep - 1) / (32 * kStep) : 0;
   const int spr_f = (nch_f + 32 * kStep - 1) / (32 * kStep);
   float* sum = row_sum[warp];
-  bool waited = false, have_route = false;
+  bool waited = false, have_route = false, staged = !stage_act;
+  const __nv_bfloat16* acts = stage_act ? act_sm : act_s;                      // [T, S]
+  const __nv_bfloat16* actr = stage_act ? act_sm + static_cast<int64_t>(T) * S : act;  // [slots, F]
+  // Every streaming warp calls this exactly once (also on its error paths,
+  // so that none waits at the barrier for a warp that left): wait for the
+  // activations and the routing table, copy, and meet the other streaming warps.
+  auto stage = [&]() -> bool {
+    if (staged) return true;
+    staged = true;
+    if (!waited) {
+      pdl_wait();
+      waited = true;
+    }
+    bool good = have_route;
+    if (!good) good = have_route = wait_ready(&route_ready, err, 25);
+    if (good) {
+      const int U = sroute.count;
+      const int slots = U > 0 ? sroute.base[U - 1] + sroute.ntok[U - 1] : 0;
+      const int n_s = T * S / 8, n_r = slots * F / 8;  // 16-byte chunks
+      const uint4* src_s = reinterpret_cast<const uint4*>(act_s);
+      const uint4* src_r = reinterpret_cast<const uint4*>(act);
+      uint4* dst = reinterpret_cast<uint4*>(act_sm);
+      for (int i = threadIdx.x; i < n_s + n_r; i += kWorkers * 32)
+        dst[i] = i < n_s ? __ldcg(src_s + i) : __ldcg(src_r + (i - n_s));
+    }
+    named_bar_sync(1, kWorkers * 32);
+    return good;
+  };
+  bool ok = true;
   for (int c = gw; c < H; c += GW) {
     if (lane < kDecodeMaxRows) sum[lane] = 0.0f;
     __syncwarp();
@@ -265,15 +297,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();  // the activations come from the gate/up grid
         waited = true;
       }
+      if (!staged && !stage()) ok = false;
+      if (!ok) return;
       if (st < spr_s) {
         const int base = st * 32 * kStep + lane;
 #pragma unroll
         for (int t = 0; t < MaxT; ++t) {
           if (t >= T) break;
-          const __nv_bfloat16* ar = act_s + static_cast<int64_t>(t) * S;
+          const __nv_bfloat16* ar = acts + static_cast<int64_t>(t) * S;
 #pragma unroll
           for (int q = 0; q < kStep; ++q)
-            if (base + 32 * q < nch_s) acc[t] += Fm::dot_act(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+            if (base + 32 * q < nch_s) acc[t] += Fm::template dot_act<2>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
         }
         if (st == spr_s - 1) {
           const float sc = Fm::scale(sdown, c);
@@ -294,10 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < MaxT; ++j) {
         if (j >= n0) break;
-        const __nv_bfloat16* ar = act + static_cast<int64_t>(b0 + j) * F;
+        const __nv_bfloat16* ar = actr + static_cast<int64_t>(b0 + j) * F;
 #pragma unroll
         for (int q = 0; q < kStep; ++q)
-          if (base + 32 * q < nch_f) acc[j] += Fm::dot_act(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+          if (base + 32 * q < nch_f) acc[j] += Fm::template dot_act<2>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
       }
       if (sr == spr_f - 1) {
         const float sc = Fm::scale(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
@@ -314,18 +348,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    uint4 wa[kStep], wb[kStep];
-    if (spr_s == 0 && !learn()) return;
-    if (nsteps > 0) issue(0, wa);
-    for (int st = 0; st < nsteps; st += 2) {
-      if (st + 1 >= spr_s && !learn()) return;
-      if (st + 1 < nsteps) issue(st + 1, wb);
-      consume(st, wa);
-      if (st + 2 >= spr_s && !learn()) return;
-      if (st + 2 < nsteps) issue(st + 2, wa);
-      if (st + 1 < nsteps) consume(st + 1, wb);
+    // Four steps in flight: a ring of four register buffers, unrolled.
+    uint4 w0[kStep], w1[kStep], w2[kStep], w3[kStep];
+    auto issue_at = [&](int st, uint4 (&w)[kStep]) {
+      if (st >= spr_s && !learn()) ok = false;
+      if (ok && st < nsteps) issue(st, w);
+    };
+    issue_at(0, w0);
+    issue_at(1, w1);
+    issue_at(2, w2);
+    for (int st = 0; ok && st < nsteps; st += 4) {
+      issue_at(st + 3, w3);
+      if (!ok) break;
+      consume(st, w0);
+      issue_at(st + 4, w0);
+      if (!ok) break;
+      if (st + 1 < nsteps) consume(st + 1, w1);
+      issue_at(st + 5, w1);
+      if (!ok) break;
+      if (st + 2 < nsteps) consume(st + 2, w2);
+      issue_at(st + 6, w2);
+      if (!ok) break;
+      if (st + 3 < nsteps) consume(st + 3, w3);
     }
-    if (!learn()) return;  // a channel with no rows to stream still needs its routing
+    if (!ok || !learn()) {  // (a channel with no rows to stream still needs its routing)
+      ok = false;
+      break;
+    }
     __syncwarp();
     for (int t = lane; t < T; t += 32) {
       const int64_t o = static_cast<int64_t>(t) * H + c;
@@ -333,9 +382,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   }
+  stage();  // warps without a channel (or that stopped early) still meet the others
 }
 
 std::mutex g_prep_mu;
+size_t g_down_dyn_limit[kMaxDevices] = {};  // dynamic shared memory the down kernel may take
 
 template <typename Rows>
 cudaError_t prepare_kernels() {
@@ -349,7 +400,20 @@ cudaError_t prepare_kernels() {
   if (st == cudaSuccess) st = allow_max_dynamic_smem(gate_up_decode_kernel<Rows, 4>);
   if (st == cudaSuccess) st = allow_max_dynamic_smem(gate_up_decode_kernel<Rows, 8>);
   if (st == cudaSuccess) st = allow_max_dynamic_smem(gate_up_decode_kernel<Rows, kDecodeMaxRows>);
-  if (st == cudaSuccess && dev < kMaxDevices) done[dev] = true;
+  if (st == cudaSuccess) st = allow_max_dynamic_smem(down_decode_kernel<Rows, 1>);
+  if (st == cudaSuccess) st = allow_max_dynamic_smem(down_decode_kernel<Rows, 4>);
+  if (st == cudaSuccess) st = allow_max_dynamic_smem(down_decode_kernel<Rows, 8>);
+  if (st == cudaSuccess) st = allow_max_dynamic_smem(down_decode_kernel<Rows, kDecodeMaxRows>);
+  if (st == cudaSuccess && dev < kMaxDevices) {
+    cudaFuncAttributes a{};
+    int optin = 0;
+    st = cudaFuncGetAttributes(&a, down_decode_kernel<Rows, kDecodeMaxRows>);
+    if (st == cudaSuccess) st = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (st == cudaSuccess) {
+      g_down_dyn_limit[dev] = static_cast<size_t>(optin) - a.sharedSizeBytes;
+      done[dev] = true;
+    }
+  }
   return st;
 }
 
@@ -397,9 +461,14 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   }
   rs.ids_out = nullptr;
   rs.w_out = nullptr;
-  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err};
-  return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), 0,
-                          stream, args, pdl && between == nullptr);
+  // Activations staged in shared memory when they fit (T*S + T*k*F bf16).
+  int dev = 0;
+  if ((st = cudaGetDevice(&dev)) != cudaSuccess) return st;
+  const size_t need = (static_cast<size_t>(T) * S + static_cast<size_t>(T) * routing.top_k * F) * 2;
+  int stage = dev < kMaxDevices && need <= g_down_dyn_limit[dev] ? 1 : 0;
+  void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err, &stage};
+  return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), stage ? need : 0, stream, args,
+                          pdl && between == nullptr);
 }
 
 }  // namespace

@@ -23,10 +23,14 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <bool Cg>
+// Activation loads: 0 read-only global path, 1 through L2 only (written
+// earlier in the same kernel), 2 generic (shared or global memory).
+template <int Mode>
 __device__ __forceinline__ uint4 ld_act(const uint4* p) {
-  if constexpr (Cg)
+  if constexpr (Mode == 1)
     return __ldcg(p);
+  else if constexpr (Mode == 2)
+    return *p;
   else
     return __ldg(p);
 }
@@ -50,9 +54,8 @@ struct Fmt<Bf16Rows> {
     const float4 x1 = reinterpret_cast<const float4*>(x)[1];
     return dot8_bf16(w, x0, x1);
   }
-  // 16 bytes of weights against bf16 activations in global memory; Cg reads
-  // them through L2 only (activations written earlier in the same kernel).
-  template <bool Cg = false>
+  // 16 bytes of weights against bf16 activations (load mode as ld_act).
+  template <int Cg = 0>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
     return dot8_bf16_bf16(w, ld_act<Cg>(reinterpret_cast<const uint4*>(act)));
   }
@@ -81,7 +84,7 @@ struct Fmt<Q8Rows> {
     }
     return s;
   }
-  template <bool Cg = false>
+  template <int Cg = 0>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
     const uint4 a0 = ld_act<Cg>(reinterpret_cast<const uint4*>(act));

@@ -210,7 +210,7 @@ __device__ __forceinline__ bool down_pair(const DownUnit& A, const DownUnit& B, 
 #pragma unroll
       for (int q = 0; q < kC; ++q) {
         const int idx = pass + lane + 32 * q;
-        if (idx < A.nchunks) a0[j] += Fm::template dot_act<true>(w0[q], ar + idx * Fm::kPerChunk);
+        if (idx < A.nchunks) a0[j] += Fm::template dot_act<1>(w0[q], ar + idx * Fm::kPerChunk);
       }
     }
 #pragma unroll
@@ -220,7 +220,7 @@ __device__ __forceinline__ bool down_pair(const DownUnit& A, const DownUnit& B, 
 #pragma unroll
       for (int q = 0; q < kC; ++q) {
         const int idx = pass + lane + 32 * q;
-        if (idx < B.nchunks) a1[j] += Fm::template dot_act<true>(w1[q], ar + idx * Fm::kPerChunk);
+        if (idx < B.nchunks) a1[j] += Fm::template dot_act<1>(w1[q], ar + idx * Fm::kPerChunk);
       }
     }
   }

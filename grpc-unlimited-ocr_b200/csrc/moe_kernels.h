@@ -24,8 +24,18 @@ cudaError_t launch_maybe_pdl(const void* func, dim3 grid, dim3 block, size_t sme
 
 // ---- router (router.cu) ----
 // logits [T, E] = x [T, H] . router [E, H]^T (+ bias), the reference's fp32 dot order.
+// Optional routing output of the decode router: the last block builds the
+// batch's routing table (and the rank-order ids / weights) once.
+struct RouteOut {
+  DecodeRoute* table;
+  int top_k, renorm;
+  int* ids_out;
+  float* w_out;
+  unsigned* ticket;  // zero between launches; the last block resets it
+};
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
-                                 float* logits, cudaStream_t stream, bool pdl = false);
+                                 float* logits, cudaStream_t stream, bool pdl = false,
+                                 const RouteOut* route = nullptr);
 cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,
                              float* weights, cudaStream_t stream);
 cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int K, int E, DecodeRoute* route,

@@ -203,6 +203,25 @@ __device__ inline void route_from_logits(const float* logits, int T, int E, int 
   route_sync(bar, nthreads);
 }
 
+// Writes a table built in shared memory to its global form (route_from_table's input).
+__device__ inline void route_to_table(const SmemRoute* r, DecodeRoute* g, int tid, int nthreads) {
+  const int U = r->count;
+  if (tid == 0) {
+    g->active_count = U;
+    g->slot_total = U > 0 ? r->base[U - 1] + r->ntok[U - 1] : 0;
+  }
+  for (int u = tid; u < U; u += nthreads) {
+    const int base = r->base[u], cnt = r->ntok[u];
+    g->active_expert[u] = r->expert[u];
+    g->tok_count[u] = cnt;
+    g->slot_base[u] = base;
+    for (int j = 0; j < cnt; ++j) {
+      g->tok_index[u][j] = r->slot_tok[base + j];
+      g->tok_weight[u][j] = r->slot_w[base + j];
+    }
+  }
+}
+
 // Copies a precomputed routing table (the expert_ffn_one mirrors) into shared memory.
 __device__ inline void route_from_table(const DecodeRoute* g, int T, SmemRoute* r, int tid, int nthreads, int bar) {
   const int U = __ldcg(&g->active_count);

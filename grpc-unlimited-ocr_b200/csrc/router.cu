@@ -24,7 +24,7 @@ constexpr int kStageUnroll = 4;  // float4 loads in flight per thread while stag
 __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restrict__ x, int T, int H,
                                                             const float* __restrict__ router,
                                                             const float* __restrict__ bias, int E,
-                                                            float* __restrict__ logits) {
+                                                            float* __restrict__ logits, RouteOut ro) {
   extern __shared__ float smem[];
   const int e = blockIdx.x;
   const int tid = threadIdx.x;
@@ -71,8 +71,20 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
     float acc = 0.0f, tail = 0.0f;
     if (t < T) {
       const float* xr = xs + t * xstride;
-#pragma unroll 8
-      for (int i = lane8; i < full; i += 8) acc = __fadd_rn(acc, __fmul_rn(xr[i], ws[i]));
+      // Sixteen elements of the chain loaded before they are added: the
+      // shared-memory latency is paid once per sixteen dependent adds.
+      int i = lane8;
+      for (; i + 120 < full; i += 128) {
+        float xv[16], wv[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          xv[u] = xr[i + 8 * u];
+          wv[u] = ws[i + 8 * u];
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(xv[u], wv[u]));
+      }
+      for (; i < full; i += 8) acc = __fadd_rn(acc, __fmul_rn(xr[i], ws[i]));
       if (lane8 == 0)
         for (int i = full; i < H; ++i) tail = __fadd_rn(tail, __fmul_rn(xr[i], ws[i]));
     }
@@ -88,6 +100,22 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
       logits[static_cast<int64_t>(t) * E + e] = s;
     }
   }
+  if (ro.table == nullptr) return;
+  // The last block to finish builds the batch's routing table once, with all
+  // of its threads, for the expert kernels to copy.
+  __shared__ int s_last;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(ro.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ SmemRoute r;
+  route_from_logits(logits, T, E, ro.top_k, ro.renorm, &r, tid, blockDim.x, 1, ro.ids_out, ro.w_out);
+  route_to_table(&r, ro.table, tid, blockDim.x);
+  if (tid == 0) *ro.ticket = 0;
 }
 
 // Standalone softmax/top-k over logits rows: one warp per row (the op-level
@@ -138,13 +166,14 @@ cudaError_t prepare_router_decode() {
 }
 
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
-                                 float* logits, cudaStream_t stream, bool pdl) {
+                                 float* logits, cudaStream_t stream, bool pdl, const RouteOut* route) {
   const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
   if (smem > 48 * 1024) {
     const cudaError_t st = prepare_router_decode();
     if (st != cudaSuccess) return st;
   }
-  void* args[] = {&x, &T, &H, &router, &bias, &E, &logits};
+  RouteOut ro = route != nullptr ? *route : RouteOut{nullptr, 0, 0, nullptr, nullptr, nullptr};
+  void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro};
   return launch_maybe_pdl(reinterpret_cast<const void*>(router_logits_kernel), dim3(E), dim3(256), smem, stream, args,
                           pdl);
 }
