@@ -621,7 +621,7 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   const bool pdl = ev == nullptr;
   // The router's last block builds the routing table once; the expert
   // kernels copy it.
-  const RouteOut ro{p->route, K, d.renormalize, p->ids, p->weights, p->counter};
+  const RouteOut ro{p->route, K, d.renormalize, p->ids, p->weights, p->counter, p->err};
   UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl, &ro), "forward: router");
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;

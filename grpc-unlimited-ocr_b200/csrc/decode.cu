@@ -78,7 +78,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                           Rows sup, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
                           __nv_bfloat16* __restrict__ act_s, ErrorWord* err) {
   using Fm = Fmt<Rows>;
-  extern __shared__ __align__(16) float xs[];  // [T][H] bf16-rounded inputs
+  // bf16-rounded inputs, [T][kQuads][chunks] float4s: the lanes reading
+  // consecutive chunks read consecutive 16-byte words (no bank conflicts).
+  extern __shared__ __align__(16) float xs[];
   __shared__ SmemRoute sroute;
   __shared__ uint64_t route_ready;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -87,7 +89,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   // x was written by the grid two launches back, complete before this one started.
-  for (int i = threadIdx.x; i < T * H; i += blockDim.x) xs[i] = bf16_round(__ldcg(x + i));
+  {
+    constexpr int kPer = Fm::kPerChunk, kQ = Fm::kQuads;
+    const int nch = H / kPer;
+    for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
+      const int t = i / H, k = i % H, c = k / kPer, q = (k % kPer) >> 2;
+      xs[((static_cast<size_t>(t) * kQ + q) * nch + c) * 4 + (k & 3)] = bf16_round(__ldcg(x + i));
+    }
+  }
   __syncthreads();
   if (warp == kWorkers) {
     pdl_wait();  // the router's logits
@@ -137,13 +146,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < MaxT; ++j) {
         if (j >= J.ntok) break;
-        const float* xr = xs + static_cast<size_t>(J.toks == nullptr ? j : J.toks[j]) * H;
+        const float4* xr = reinterpret_cast<const float4*>(xs) +
+                           static_cast<size_t>(J.toks == nullptr ? j : J.toks[j]) * Fm::kQuads * nchunks;
 #pragma unroll
         for (int c = 0; c < kStep; ++c) {
           const int idx = base + 32 * c;
           if (idx < nchunks) {
-            gacc[j] += Fm::dot_x(g[c], xr + idx * Fm::kPerChunk);
-            uacc[j] += Fm::dot_x(u[c], xr + idx * Fm::kPerChunk);
+            gacc[j] += Fm::dot_xq(g[c], xr + idx, nchunks);
+            uacc[j] += Fm::dot_xq(u[c], xr + idx, nchunks);
           }
         }
       }

@@ -54,6 +54,10 @@ struct Fmt<Bf16Rows> {
     const float4 x1 = reinterpret_cast<const float4*>(x)[1];
     return dot8_bf16(w, x0, x1);
   }
+  // The same product with the chunk's inputs stored as kQuads float4s
+  // `qs` float4s apart (the conflict-free shared layout of the gate/up kernel).
+  static constexpr int kQuads = 2;
+  __device__ static float dot_xq(const uint4& w, const float4* x, int qs) { return dot8_bf16(w, x[0], x[qs]); }
   // 16 bytes of weights against bf16 activations (load mode as ld_act).
   template <int Cg = 0>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
@@ -70,13 +74,17 @@ struct Fmt<Q8Rows> {
   }
   __device__ static float scale(const Q8Rows& r, int64_t i) { return __ldg(r.scale + i); }
   __device__ static float dot_x(const uint4& w, const float* x) {
+    return dot_xq(w, reinterpret_cast<const float4*>(x), 1);
+  }
+  static constexpr int kQuads = 4;
+  __device__ static float dot_xq(const uint4& w, const float4* x, int qs) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
     float s = 0.0f;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float a, b, c, d;
       i8x4_to_f32(words[q], a, b, c, d);
-      const float4 xv = reinterpret_cast<const float4*>(x)[q];
+      const float4 xv = x[q * qs];
       s = fmaf(a, xv.x, s);
       s = fmaf(b, xv.y, s);
       s = fmaf(c, xv.z, s);

@@ -32,6 +32,7 @@ struct RouteOut {
   int* ids_out;
   float* w_out;
   unsigned* ticket;  // zero between launches; the last block resets it
+  ErrorWord* err;    // bounded waits that gave up (null: not reported)
 };
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
                                  float* logits, cudaStream_t stream, bool pdl = false,

@@ -199,28 +199,31 @@ __global__ void scan_kernel(const int* __restrict__ block_counts, int nblk, int 
 }
 
 // Positions of every selection (stable: token order inside each expert's
-// segment), then the bf16 rows: x^ [T, H] for the shared expert and the
-// permuted copies xperm [T*K, H] for the routed experts.
-__global__ void __launch_bounds__(kPermBlock) scatter_kernel(const float* __restrict__ x, int T, int H, int K, int E,
-                                                             const int* __restrict__ ids,
-                                                             const int* __restrict__ block_offset,
-                                                             int* __restrict__ pos_of, __nv_bfloat16* __restrict__ xhat,
-                                                             __nv_bfloat16* __restrict__ xperm) {
-  __shared__ int sid[kPermBlock][kMaxTopK];
+// segment). A row's rank among the earlier rows of its warp that chose the
+// same expert is a population count over a per-warp, per-expert lane mask
+// (a row's k ids are distinct, so each lane sets its bit once per expert).
+__global__ void __launch_bounds__(kPermBlock) positions_kernel(int T, int K, int E, const int* __restrict__ ids,
+                                                               const int* __restrict__ block_offset,
+                                                               int* __restrict__ pos_of) {
   __shared__ int wcount[8][kMaxExperts];
-  __shared__ int spos[kPermBlock][kMaxTopK];
+  __shared__ unsigned lanes[8][kMaxExperts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kPermBlock + threadIdx.x;
-  for (int i = threadIdx.x; i < 8 * kMaxExperts; i += blockDim.x) (&wcount[0][0])[i] = 0;
-  for (int j = 0; j < K; ++j) {
-    int e = t < T ? ids[static_cast<int64_t>(t) * K + j] : -1;
-    if (e < 0 || e >= E) e = -1;
-    sid[threadIdx.x][j] = e;
+  for (int i = threadIdx.x; i < 8 * kMaxExperts; i += blockDim.x) {
+    (&wcount[0][0])[i] = 0;
+    (&lanes[0][0])[i] = 0u;
   }
   __syncthreads();
-  for (int j = 0; j < K; ++j) {
-    const int e = sid[threadIdx.x][j];
-    if (e >= 0) atomicAdd(&wcount[warp][e], 1);
+  int sid[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    int e = (j < K && t < T) ? ids[static_cast<int64_t>(t) * K + j] : -1;
+    if (e < 0 || e >= E) e = -1;
+    sid[j] = e;
+    if (e >= 0) {
+      atomicAdd(&wcount[warp][e], 1);
+      atomicOr(&lanes[warp][e], 1u << lane);
+    }
   }
   __syncthreads();
   // Exclusive prefix over warps, per expert.
@@ -233,41 +236,55 @@ __global__ void __launch_bounds__(kPermBlock) scatter_kernel(const float* __rest
     }
   }
   __syncthreads();
-  if (t < T) {
-    for (int j = 0; j < K; ++j) {
-      const int e = sid[threadIdx.x][j];
-      if (e < 0) {
-        spos[threadIdx.x][j] = -1;
-        continue;
-      }
-      int rank = 0;  // earlier rows of this warp that chose e
-      for (int r = warp * 32; r < static_cast<int>(threadIdx.x); ++r)
-        for (int q = 0; q < K; ++q) rank += sid[r][q] == e;
-      const int p = block_offset[static_cast<int64_t>(blockIdx.x) * E + e] + wcount[warp][e] + rank;
-      spos[threadIdx.x][j] = p;
-      pos_of[static_cast<int64_t>(t) * K + j] = p;
-    }
+  if (t >= T) return;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j >= K) break;
+    const int e = sid[j];
+    int p = -1;
+    if (e >= 0)
+      p = block_offset[static_cast<int64_t>(blockIdx.x) * E + e] + wcount[warp][e] +
+          __popc(lanes[warp][e] & ((1u << lane) - 1u));
+    pos_of[static_cast<int64_t>(t) * K + j] = p;
   }
-  __syncthreads();
-  // Row copies: the warp streams its 32 rows one by one, 8 floats per lane step.
-  for (int r = 0; r < 32; ++r) {
-    const int lr = warp * 32 + r;
-    const int tr = blockIdx.x * kPermBlock + lr;
-    if (tr >= T) break;
-    const float* src = x + static_cast<int64_t>(tr) * H;
-    for (int c = lane * 8; c < H; c += 32 * 8) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(src + c));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(src + c + 4));
+}
+
+// The bf16 rows: x^ [T, H] for the shared expert and the permuted copies
+// xperm [T*K, H] for the routed experts. Grid-stride over (row, 8-column)
+// items, two per thread per step with both loads issued first.
+__global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restrict__ x, int T, int H, int K,
+                                                           const int* __restrict__ pos_of,
+                                                           __nv_bfloat16* __restrict__ xhat,
+                                                           __nv_bfloat16* __restrict__ xperm) {
+  const int cpr = H / 8;  // 8-column items per row
+  const int64_t n = static_cast<int64_t>(T) * cpr;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n; i0 += 2 * stride) {
+    float4 v[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n) {
+        const float4* src = reinterpret_cast<const float4*>(x + (i / cpr) * H + (i % cpr) * 8);
+        v[u][0] = __ldg(src);
+        v[u][1] = __ldg(src + 1);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n) continue;
+      const int64_t t = i / cpr, c = (i % cpr) * 8;
       uint4 pk;
-      __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(b.x, b.y), h3 = __floats2bfloat162_rn(b.z, b.w);
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[u][0].x, v[u][0].y), h1 = __floats2bfloat162_rn(v[u][0].z, v[u][0].w);
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[u][1].x, v[u][1].y), h3 = __floats2bfloat162_rn(v[u][1].z, v[u][1].w);
       pk.x = *reinterpret_cast<uint32_t*>(&h0);
       pk.y = *reinterpret_cast<uint32_t*>(&h1);
       pk.z = *reinterpret_cast<uint32_t*>(&h2);
       pk.w = *reinterpret_cast<uint32_t*>(&h3);
-      *reinterpret_cast<uint4*>(xhat + static_cast<int64_t>(tr) * H + c) = pk;
+      *reinterpret_cast<uint4*>(xhat + t * H + c) = pk;
       for (int j = 0; j < K; ++j) {
-        const int p = spos[lr][j];
+        const int p = __ldg(pos_of + t * K + j);
         if (p >= 0) *reinterpret_cast<uint4*>(xperm + static_cast<int64_t>(p) * H + c) = pk;
       }
     }
@@ -374,8 +391,9 @@ cudaError_t launch_prefill_route(const PrefillCall& c, cudaStream_t stream) {
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
   scan_kernel<<<1, kMaxExperts, 0, stream>>>(s.block_counts, nblk, E, s.seg_count, s.seg_start, s.block_offset);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
-  scatter_kernel<<<nblk, kPermBlock, 0, stream>>>(c.x, T, H, K, E, c.ids, s.block_offset, s.pos_of, s.xhat,
-                                                  s.xperm);
+  positions_kernel<<<nblk, kPermBlock, 0, stream>>>(T, K, E, c.ids, s.block_offset, s.pos_of);
+  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  permute_copy_kernel<<<c.sm_count * 8, 256, 0, stream>>>(c.x, T, H, K, s.pos_of, s.xhat, s.xperm);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
   return mark(2);
 }

@@ -118,6 +118,107 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
   if (tid == 0) *ro.ticket = 0;
 }
 
+constexpr int kRouterCluster = 8;  // CTAs of the decode router's cluster (portable size)
+
+// The decode router as one 8-CTA thread-block cluster: CTA c stages the router
+// rows of experts c, c+8, ... into shared memory (before waiting for the grid
+// that writes x), computes their logits for every batch row in the exact dot
+// order, and after a cluster barrier (release/acquire: the other CTAs' logits
+// are visible) CTA 0 builds the routing table. No global ticket, no last-block
+// handshake.
+__global__ void __launch_bounds__(256) router_cluster_kernel(const float* __restrict__ x, int T, int H,
+                                                             const float* __restrict__ router,
+                                                             const float* __restrict__ bias, int E,
+                                                             float* __restrict__ logits, RouteOut ro) {
+  extern __shared__ __align__(16) float smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cta = blockIdx.x;
+  const int per = (E + kRouterCluster - 1) / kRouterCluster;  // expert rows per CTA (layout stride)
+  const int ne = cta < E ? (E - cta + kRouterCluster - 1) / kRouterCluster : 0;
+  const int xstride = H + 8;
+  float* ws = smem;                                 // [per][H]
+  float* xs = smem + static_cast<size_t>(per) * H;  // [T][H + 8]
+  // Bulk copies (TMA engine, one thread issues them all): the CTA's router
+  // rows before the wait for x — one round trip for all of them — then the x rows.
+  __shared__ __align__(8) uint64_t bars[2];
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    if (ne > 0) {
+      mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(ne) * H * 4);
+      for (int i = 0; i < ne; ++i)
+        bulk_g2s(ws + static_cast<size_t>(i) * H, router + static_cast<int64_t>(cta + kRouterCluster * i) * H,
+                 static_cast<uint32_t>(H) * 4, &bars[0]);
+    } else {
+      mbar_arrive(&bars[0]);
+    }
+  }
+  pdl_wait();  // x is written by the previous grid
+  pdl_launch_dependents();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[1], static_cast<uint32_t>(T) * H * 4);
+    for (int t = 0; t < T; ++t)
+      bulk_g2s(xs + static_cast<size_t>(t) * xstride, x + static_cast<int64_t>(t) * H, static_cast<uint32_t>(H) * 4,
+               &bars[1]);
+  }
+  __syncthreads();  // the barriers are initialised before anyone waits on them
+  const bool ok = mbar_wait(&bars[0], 0) & mbar_wait(&bars[1], 0);
+  if (!ok && tid == 0 && ro.err != nullptr) raise_error(ro.err, kDevWaitTimeout, 40, cta, 0);
+  __syncthreads();
+  // Chains (expert i, row t, lane l8): the eight lanes of a chain group are
+  // eight consecutive threads of one warp.
+  const int n_items = ne * T * 8;
+  const int full = H & ~7;
+  for (int b = warp * 32; b < n_items; b += blockDim.x) {
+    const int item = b + lane;
+    const bool valid = item < n_items;
+    const int i = valid ? item / (T * 8) : 0, t = valid ? (item / 8) % T : 0, l8 = item & 7;
+    const float* xr = xs + t * xstride;
+    const float* wr = ws + static_cast<size_t>(i) * H;
+    float acc = 0.0f, tail = 0.0f;
+    if (valid) {
+      int k = l8;
+      for (; k + 120 < full; k += 128) {
+        float xv[16], wv[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          xv[u] = xr[k + 8 * u];
+          wv[u] = wr[k + 8 * u];
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(xv[u], wv[u]));
+      }
+      for (; k < full; k += 8) acc = __fadd_rn(acc, __fmul_rn(xr[k], wr[k]));
+      if (l8 == 0)
+        for (int q = full; q < H; ++q) tail = __fadd_rn(tail, __fmul_rn(xr[q], wr[q]));
+    }
+    float a[8];
+    const int gbase = lane & ~7;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) a[q] = __shfl_sync(0xffffffffu, acc, gbase + q);
+    if (valid && l8 == 0) {
+      const int e = cta + kRouterCluster * i;
+      const float lo = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+      const float hi = __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7]));
+      float sum = __fadd_rn(__fadd_rn(lo, hi), tail);
+      if (bias != nullptr) sum = __fadd_rn(sum, bias[e]);
+      logits[static_cast<int64_t>(t) * E + e] = sum;
+    }
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (cta != 0 || ro.table == nullptr) return;
+  __shared__ SmemRoute r;
+  route_from_logits(logits, T, E, ro.top_k, ro.renorm, &r, tid, blockDim.x, 1, ro.ids_out, ro.w_out);
+  route_to_table(&r, ro.table, tid, blockDim.x);
+}
+
+size_t router_cluster_smem(int T, int H, int E) {
+  const size_t per = static_cast<size_t>((E + kRouterCluster - 1) / kRouterCluster);
+  return (per * H + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
+}
+
 // Standalone softmax/top-k over logits rows: one warp per row (the op-level
 // mirror of expert_topk, int64 ids like the reference).
 __global__ void __launch_bounds__(256) topk_rows_kernel(const float* __restrict__ logits, int64_t rows, int E,
@@ -152,6 +253,8 @@ __global__ void route_from_ids_kernel(const int64_t* ids, const float* weights, 
 
 }  // namespace
 
+size_t g_cluster_dyn_limit[kMaxDevices] = {};
+
 cudaError_t prepare_router_decode() {
   static bool raised[kMaxDevices] = {};
   int dev = 0;
@@ -159,7 +262,13 @@ cudaError_t prepare_router_decode() {
   if (st != cudaSuccess) return st;
   if (dev < kMaxDevices && !raised[dev]) {
     st = allow_max_dynamic_smem(router_logits_kernel);
+    if (st == cudaSuccess) st = allow_max_dynamic_smem(router_cluster_kernel);
     if (st != cudaSuccess) return st;
+    cudaFuncAttributes a{};
+    int optin = 0;
+    if ((st = cudaFuncGetAttributes(&a, router_cluster_kernel)) != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return st;
+    g_cluster_dyn_limit[dev] = static_cast<size_t>(optin) - a.sharedSizeBytes;
     raised[dev] = true;
   }
   return cudaSuccess;
@@ -167,12 +276,31 @@ cudaError_t prepare_router_decode() {
 
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
                                  float* logits, cudaStream_t stream, bool pdl, const RouteOut* route) {
-  const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
-  if (smem > 48 * 1024) {
-    const cudaError_t st = prepare_router_decode();
-    if (st != cudaSuccess) return st;
+  RouteOut ro = route != nullptr ? *route : RouteOut{nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr};
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if ((st = prepare_router_decode()) != cudaSuccess) return st;
+  const size_t csmem = router_cluster_smem(T, H, E);
+  if (route != nullptr && dev < kMaxDevices && csmem <= g_cluster_dyn_limit[dev]) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kRouterCluster);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = csmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kRouterCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro};
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(router_cluster_kernel), args);
   }
-  RouteOut ro = route != nullptr ? *route : RouteOut{nullptr, 0, 0, nullptr, nullptr, nullptr};
+  const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
   void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro};
   return launch_maybe_pdl(reinterpret_cast<const void*>(router_logits_kernel), dim3(E), dim3(256), smem, stream, args,
                           pdl);
