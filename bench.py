@@ -338,7 +338,6 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill section")
     ap.add_argument("--prefill-rows", type=int, default=None, help="shrink the prefill batch (profiling captures)")
-    ap.add_argument("--persistent", action="store_true", help="one persistent launch per decode stack")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -372,7 +371,7 @@ def main():
     T = args.batch
     fmt_int8 = args.format == "int8"
     plan = M.Plan(cfg.dims(), max_rows=max(T, 1), weight_format=M.WEIGHT_INT8 if fmt_int8 else M.WEIGHT_BF16,
-                  renormalize=True, device=local, flags=M.PLAN_PERSISTENT_DECODE if args.persistent else 0)
+                  renormalize=True, device=local)
     host_layer0 = None
     for layer in range(cfg.layers):
         t = C.device_layer(cfg, layer, device=dev)
@@ -452,13 +451,8 @@ def main():
     step_bytes, gu_bytes = decode_bytes(cfg, active, fmt_int8)
     hbm_peak, peak_kind = measured_peaks()
     gu_achieved = (sum(gu_bytes) / len(gu_bytes)) / (prof["gate_up"] * 1e-3) / 1e9
-    # The dominant kernel: with the default plan the whole stack is one
-    # persistent launch, so its achieved bandwidth is the step's.
     step_gbs = step_bytes / (ms_max * 1e-3) / 1e9
-    if (not args.persistent):
-        traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
-    else:
-        traffic = traffic_from_profile(f"decode_persistent_{args.format}_t{T}.txt")
+    traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
 
     prefill = None
     if not args.no_prefill:
@@ -483,7 +477,7 @@ def main():
                          f"scaled to the {cfg.layers}-layer stack"}
 
     if rank == 0:
-        launches_per_step = 3 * cfg.layers if (not args.persistent) else 1
+        launches_per_step = 3 * cfg.layers
         line = {
             "metric": "MoE layer tokens/s (decode)",
             "value": world * T / (ms_max * 1e-3),
@@ -496,17 +490,12 @@ def main():
                        "weights": args.format, "renormalize": True,
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "no flush: 20 GB of weights per step pass exceed the 126 MB L2"},
-            "roofline": ({"bound": "hbm", "kernel": "gate_up_decode", "achieved": gu_achieved, "peak": hbm_peak,
-                          "peak_source": peak_kind, "unit": "GB/s", "frac": gu_achieved / hbm_peak}
-                         if (not args.persistent) else
-                         {"bound": "hbm", "kernel": "persistent_decode_kernel (whole 24-layer stack, one launch)",
-                          "achieved": step_gbs, "peak": hbm_peak, "peak_source": peak_kind, "unit": "GB/s",
-                          "frac": step_gbs / hbm_peak}) | {
+            "roofline": {"bound": "hbm", "kernel": "gate_up_decode", "achieved": gu_achieved, "peak": hbm_peak,
+                         "peak_source": peak_kind, "unit": "GB/s", "frac": gu_achieved / hbm_peak,
                          "traffic": traffic,
                          "step_achieved": step_gbs, "step_frac": step_gbs / hbm_peak,
                          "algorithmic_bytes_per_step": step_bytes,
-                         "layered_kernel_ms": {k: round(v, 5) for k, v in prof.items()},
-                         "layered_gate_up_achieved": gu_achieved,
+                         "kernel_ms": {k: round(v, 5) for k, v in prof.items()},
                          "distinct_experts_per_layer": active},
             "cpu_baseline": cpu,
             "e2e": {"value": world * T / (e2e_max * 1e-3), "unit": "tokens/s",

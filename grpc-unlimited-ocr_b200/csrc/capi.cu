@@ -15,7 +15,6 @@
 #include <vector>
 
 #include "../../include/uocr_moe.h"
-#include "decode_persistent.h"
 #include "decode_tc.h"
 #include "ep.h"
 #include "moe_kernels.h"
@@ -115,11 +114,6 @@ struct uocr_moe_plan {
   bool prefill = false;
   PrefillDims pdims{};
   PrefillScratch pscratch{};
-  // Decode batches as one persistent launch: per-layer weight pointers on the
-  // device and the grid barrier's state.
-  bool persistent = false;
-  DecodeLayerW* dlayers = nullptr;
-  GridBarrier* gbar = nullptr;
   // bf16 decode batches on the tensor cores.
   bool decode_tc = false;
   DecodeTcScratch dtc{};
@@ -184,8 +178,6 @@ struct uocr_moe_plan {
     act_s = c.take<__nv_bfloat16>(dr * (S > 0 ? S : 1));
     counter = c.take<unsigned>(1);
     err = c.take<ErrorWord>(1);
-    gbar = c.take<GridBarrier>(1);
-    dlayers = c.take<DecodeLayerW>(layers.size());
     if (prefill) {
       char* base = c.take<char>(prefill_scratch_bytes(pdims, !ep));
       carve_prefill_scratch(pdims, base, &pscratch, !ep);
@@ -319,17 +311,6 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
                     (d.flags & UOCR_PLAN_EP_STRIDED) != 0 ? 1 : 0};
     p->elay = ep_layout(p->pdims, p->emap);
   }
-  p->persistent = dr > 0 && (d.flags & UOCR_PLAN_PERSISTENT_DECODE) != 0 && (d.flags & UOCR_PLAN_TENSOR_DECODE) == 0 &&
-                  persistent_decode_fits(dr, static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
-                                         static_cast<int>(d.experts_per_token), static_cast<int>(d.shared_ffn),
-                                         p->sm_count, static_cast<size_t>(smem_optin));
-  if (p->persistent) {
-    const cudaError_t pst = prepare_persistent_decode();
-    if (pst != cudaSuccess) {
-      delete p;
-      return cuda_fail(pst, "plan_create: persistent decode set-up");
-    }
-  }
   p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
                  decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
                                      static_cast<int>(d.shared_ffn));
@@ -364,20 +345,6 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   if (st != cudaSuccess) {
     uocr_moe_plan_destroy(p);
     return cuda_fail(st, "plan_create: arena clear");
-  }
-  {
-    // Per-layer weight pointers for the persistent decode kernel.
-    std::vector<DecodeLayerW> dl(p->layers.size());
-    for (size_t i = 0; i < dl.size(); ++i) {
-      const LayerDev& L = p->layers[i];
-      dl[i] = DecodeLayerW{L.router, L.bias, L.gate, L.up, L.down, L.sgate, L.sup, L.sdown,
-                           L.gate_s, L.up_s, L.down_s, L.sgate_s, L.sup_s, L.sdown_s};
-    }
-    st = cudaMemcpy(p->dlayers, dl.data(), dl.size() * sizeof(DecodeLayerW), cudaMemcpyHostToDevice);
-    if (st != cudaSuccess) {
-      uocr_moe_plan_destroy(p);
-      return cuda_fail(st, "plan_create: layer table");
-    }
   }
   if (p->ep) {
     // A block of its own: CUDA IPC exports whole cudaMalloc allocations.
@@ -542,34 +509,6 @@ PrefillCall prefill_call(const uocr_moe_plan* p, const LayerDev& L, const float*
   return c;
 }
 
-PersistentDecodeCall persistent_call(const uocr_moe_plan* p, int64_t first_layer, int64_t n_layers, const float* x,
-                                     bool residual, float* y, int64_t rows) {
-  const uocr_moe_desc& d = p->d;
-  PersistentDecodeCall c{};
-  c.layers = p->dlayers + first_layer;
-  c.n_layers = static_cast<int>(n_layers);
-  c.x = x;
-  c.y = y;
-  c.residual = residual ? 1 : 0;
-  c.T = static_cast<int>(rows);
-  c.H = static_cast<int>(d.hidden);
-  c.E = static_cast<int>(d.routed_experts);
-  c.K = static_cast<int>(d.experts_per_token);
-  c.F = static_cast<int>(d.expert_ffn);
-  c.S = static_cast<int>(d.shared_ffn);
-  c.renorm = d.renormalize;
-  c.int8 = d.weight_format == UOCR_WEIGHT_INT8 ? 1 : 0;
-  c.logits = p->logits;
-  c.ids_out = p->ids;
-  c.w_out = p->weights;
-  c.act = p->act;
-  c.act_s = p->act_s;
-  c.barrier = p->gbar;
-  c.err = p->err;
-  c.sm_count = p->sm_count;
-  return c;
-}
-
 EpCall ep_call(const uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows, const float* resid, float* y) {
   EpCall c{};
   c.pc = prefill_call(p, L, x, rows, resid, y);
@@ -608,12 +547,6 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
     c.events = ev;
     UOCR_TRY(launch_prefill(c, stream), "forward: prefill");
     if (nev != nullptr) *nev = 6;
-    return UOCR_OK;
-  }
-  const int64_t li = &L - p->layers.data();
-  if (p->persistent && ev == nullptr) {
-    UOCR_TRY(launch_persistent_decode(persistent_call(p, li, 1, x, resid != nullptr, y, rows), stream),
-             "forward: persistent decode");
     return UOCR_OK;
   }
   // Programmatic dependent launch chains router -> gate/up -> down (and the
@@ -720,13 +653,6 @@ int uocr_moe_forward_stack(uocr_moe_plan* p, float* h, int64_t rows, void* strea
     if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: a layer's weights are not set");
   DeviceGuard guard(p->d.device);
   auto stream = static_cast<cudaStream_t>(stream_v);
-  if (p->persistent && rows <= p->decode_rows) {
-    // One launch for the whole stack: nothing to gain from a graph.
-    UOCR_TRY(launch_persistent_decode(persistent_call(p, 0, static_cast<int64_t>(p->layers.size()), h, true, h, rows),
-                                      stream),
-             "forward_stack: persistent decode");
-    return UOCR_OK;
-  }
   auto run_all = [&]() {
     for (const auto& L : p->layers) {
       int rc = run_layer(p, L, h, rows, h, h, stream);

@@ -1,5 +1,5 @@
-// Weight-row access shared by the decode kernels (decode.cu,
-// decode_persistent.cu): streaming 16-byte loads and the dot products of one
+// Weight-row access of the decode kernels (decode.cu): streaming 16-byte
+// loads and the dot products of one
 // chunk of bf16 or per-channel int8 weights against fp32 or bf16 inputs.
 #pragma once
 

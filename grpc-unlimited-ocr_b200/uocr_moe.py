@@ -23,7 +23,6 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
 PLAN_TENSOR_DECODE = 2
 PLAN_EP_STRIDED = 4
-PLAN_PERSISTENT_DECODE = 8
 EP_HANDLE_BYTES = 256
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).

@@ -85,12 +85,6 @@ typedef struct uocr_moe_desc {
 /* Expert parallelism: expert e lives on rank e % ep_world instead of the
  * default contiguous ranges (rank e / (routed_experts / ep_world)). */
 #define UOCR_PLAN_EP_STRIDED 4
-/* Decode batches run per layer as three kernels (router, gate/up,
- * down+combine) chained by programmatic dependent launch, the stack captured
- * as one CUDA graph. This flag runs them instead as ONE persistent cooperative
- * launch per forward / forward_stack call (all layers, grid-wide barriers
- * between the phases) when the rows fit in shared memory; same bits. */
-#define UOCR_PLAN_PERSISTENT_DECODE 8
 
 int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** plan);
 int uocr_moe_plan_destroy(uocr_moe_plan* plan);

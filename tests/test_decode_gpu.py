@@ -112,7 +112,7 @@ TC_SHAPES = [(1, 256, 8, 3, 128, 128, True, 0), (5, 128, 128, 8, 128, 0, True, 0
 
 @pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt,flags",
                          [s + (0,) for s in SMALL_SHAPES + TC_SHAPES] + [s + (M.PLAN_TENSOR_DECODE,) for s in TC_SHAPES]
-                         + [s + (M.PLAN_PERSISTENT_DECODE,) for s in SMALL_SHAPES])
+)
 def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt, flags):
     import torch
     rng = np.random.default_rng(T * 7919 + E)
@@ -167,9 +167,9 @@ def c1_layer(cuda):
     return cfg, t, host_weights(t)
 
 
-# The decode kernel sets: per-layer launches (default), one persistent launch,
-# and the tensor-core GEMV variant.
-DECODE_PATHS = {"layered": 0, "persistent": M.PLAN_PERSISTENT_DECODE, "tensor_cores": M.PLAN_TENSOR_DECODE}
+# The decode kernel sets: CUDA-core weight streaming (default) and the
+# tensor-core GEMV variant.
+DECODE_PATHS = {"layered": 0, "tensor_cores": M.PLAN_TENSOR_DECODE}
 
 
 @pytest.mark.parametrize("path", list(DECODE_PATHS))
@@ -188,7 +188,7 @@ def test_config1_layer_bf16(cuda, c1_layer, T, path):
     assert err <= BF16_TOL
 
 
-@pytest.mark.parametrize("path", ["persistent", "layered"])
+@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
 @pytest.mark.parametrize("T", [1, 8])
 def test_config2_layer_int8(cuda, c1_layer, T, path):
     import torch
@@ -210,7 +210,7 @@ def test_config2_layer_int8(cuda, c1_layer, T, path):
     assert err <= INT8_TOL
 
 
-@pytest.mark.parametrize("path", ["persistent", "layered"])
+@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
 def test_stack_residual_two_layers(cuda, path):
     import torch
     cfg = C.CONFIGS[1]
@@ -226,37 +226,6 @@ def test_stack_residual_two_layers(cuda, path):
     for t in layers:
         want = want + O.moe_forward(host_weights(t), want, cfg.top_k, renormalize=True).y
     assert max_rel(to_np(h), want) <= BF16_TOL
-
-
-@pytest.mark.parametrize("fmt", [M.WEIGHT_BF16, M.WEIGHT_INT8])
-@pytest.mark.parametrize("T", [1, 3, 8, 16])
-def test_persistent_stack_equals_layered_launches(cuda, T, fmt):
-    """The one-launch stack and the per-layer kernels do the same arithmetic in
-    the same order: bitwise equal outputs, and the same last-layer ids."""
-    import torch
-    cfg = C.CONFIGS[1 if fmt == M.WEIGHT_BF16 else 2]
-    layers = [C.device_layer(cfg, l) for l in range(3)]
-    plans = [M.Plan(cfg.dims(layers=3), max_rows=16, weight_format=fmt, flags=f)
-             for f in (M.PLAN_PERSISTENT_DECODE, M.PLAN_NO_GRAPHS)]
-    for p in plans:
-        for l, t in enumerate(layers):
-            C.load_layer(p, cfg, l, t)
-    x = C.device_input(cfg, T)
-    outs = []
-    for p in plans:
-        h = x.clone()
-        for _ in range(2):
-            h.copy_(x)
-            p.forward_stack(h)
-        p.check()
-        y = torch.empty_like(x)
-        ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=cuda)
-        p.forward(2, h, y, ids)
-        p.check()
-        outs.append((h, y, ids))
-    assert torch.equal(outs[0][0], outs[1][0])
-    assert torch.equal(outs[0][1], outs[1][1])
-    assert torch.equal(outs[0][2], outs[1][2])
 
 
 @pytest.mark.parametrize("path", ["layered", "tensor_cores"])
