@@ -457,15 +457,17 @@ def main():
     prefill = None
     if not args.no_prefill:
         plan.close()  # free the decode stack's 20 GB first
+        # Expert parallelism (world > 1) assigns expert e to rank e % G: with
+        # the Zipf-skewed router that spreads the hot experts over the ranks.
+        # Contiguous ranges (rank e // (E / G)) are measured beside it.
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
                               want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
-                              rows=args.prefill_rows, world=world, rank=rank)
+                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1)
         if world > 1:
-            # Ablation: the Zipf-hot experts spread over the ranks (e % G).
             alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
-                              rows=args.prefill_rows, world=world, rank=rank, strided=True)
-            prefill["ablation_strided_experts"] = {k: alt[k] for k in ("value", "ms_per_layer", "kernel_ms",
-                                                                     "rows_received_per_rank", "parallelism")}
+                              rows=args.prefill_rows, world=world, rank=rank, strided=False)
+            prefill["contiguous_experts"] = {k: alt[k] for k in ("value", "ms_per_layer", "kernel_ms",
+                                                               "rows_received_per_rank", "parallelism")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

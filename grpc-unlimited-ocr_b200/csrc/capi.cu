@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -128,6 +129,7 @@ struct uocr_moe_plan {
   std::vector<char*> opened;
   bool ep_connected = false;
   bool ep_local_group = false;
+  uint64_t ep_wait_ns = 20ull * 1000 * 1000 * 1000;  // UOCR_EP_WAIT_MS at creation, default 20 s
 
   // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
   struct GraphEntry {
@@ -310,6 +312,10 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     p->emap = EpMap{W, d.ep_rank, static_cast<int>(d.routed_experts), static_cast<int>(d.routed_experts) / W,
                     (d.flags & UOCR_PLAN_EP_STRIDED) != 0 ? 1 : 0};
     p->elay = ep_layout(p->pdims, p->emap);
+    if (const char* v = std::getenv("UOCR_EP_WAIT_MS")) {
+      const long long ms = std::atoll(v);
+      if (ms > 0) p->ep_wait_ns = static_cast<uint64_t>(ms) * 1000000ull;
+    }
   }
   p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
                  decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
@@ -519,6 +525,7 @@ EpCall ep_call(const uocr_moe_plan* p, const LayerDev& L, const float* x, int64_
   c.gate_local = as_bf16(L.gate);
   c.up_local = as_bf16(L.up);
   c.down_local = as_bf16(L.down);
+  c.wait_ns = p->ep_wait_ns;
   return c;
 }
 

@@ -12,7 +12,6 @@
 namespace uocr_b200 {
 namespace {
 
-constexpr uint64_t kEpWaitNs = 20ull * 1000 * 1000 * 1000;
 constexpr uint32_t kEpWaitPolls = 1u << 27;
 
 __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
@@ -177,14 +176,15 @@ __global__ void ep_arrive_kernel(EpPeers peers, EpLayout lay, int rank, int worl
     st_release_sys(reinterpret_cast<unsigned*>(peers.base[threadIdx.x] + lay.flags) + rank, e);
 }
 
-__global__ void ep_wait_kernel(const unsigned* flags, int world, const unsigned* epoch, ErrorWord* err, int site) {
+__global__ void ep_wait_kernel(const unsigned* flags, int world, const unsigned* epoch, ErrorWord* err, int site,
+                               uint64_t wait_ns) {
   if (static_cast<int>(threadIdx.x) >= world) return;
   const unsigned target = *epoch;
   const unsigned* f = flags + threadIdx.x;
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 0;; ++i) {
     if (static_cast<int>(ld_acquire_sys(f) - target) >= 0) break;
-    if (i >= kEpWaitPolls || ((i & 63u) == 63u && global_timer_ns() - start > kEpWaitNs)) {
+    if (i >= kEpWaitPolls || ((i & 63u) == 63u && global_timer_ns() - start > wait_ns)) {
       raise_error(err, kDevWaitTimeout, site, static_cast<int>(threadIdx.x), static_cast<int>(target));
       break;
     }
@@ -300,7 +300,7 @@ cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream) {
 
 cudaError_t ep_wait(const EpCall& c, int site, cudaStream_t stream) {
   const auto* flags = reinterpret_cast<const unsigned*>(c.peers.base[c.map.rank] + c.lay.flags);
-  ep_wait_kernel<<<1, 32, 0, stream>>>(flags, c.map.world, c.es.epoch, c.pc.err, site);
+  ep_wait_kernel<<<1, 32, 0, stream>>>(flags, c.map.world, c.es.epoch, c.pc.err, site, c.wait_ns);
   return cudaGetLastError();
 }
 

@@ -80,6 +80,7 @@ struct EpCall {
   const __nv_bfloat16* gate_local;
   const __nv_bfloat16* up_local;
   const __nv_bfloat16* down_local;
+  uint64_t wait_ns;  // how long a barrier waits for the other ranks
 };
 
 // The phases of one layer; ep_forward runs them with the barriers between.
@@ -88,7 +89,7 @@ cudaError_t ep_experts(const EpCall& c, cudaStream_t stream);
 cudaError_t ep_shared(const EpCall& c, cudaStream_t stream);
 cudaError_t ep_combine(const EpCall& c, cudaStream_t stream);
 // Barrier over the ranks' exchange regions: arrive publishes this rank's
-// next epoch to every rank; wait spins (bounded: ~20 s, then an error word)
+// next epoch to every rank; wait spins (bounded: wait_ns, then an error word)
 // until every rank published it. Data written before arrive on any rank is
 // visible to every rank's kernels after its wait.
 cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream);

@@ -152,8 +152,9 @@ int uocr_moe_profile_stack(uocr_moe_plan* plan, float* h, int64_t rows, int32_t 
  * hidden % 256 == 0, expert_ffn and shared_ffn % 128 == 0) whatever the row
  * count. Between the phases the ranks pull rows and expert outputs from each
  * other's memory over NVLink (CUDA IPC mappings) and meet at device-side
- * barriers; a rank that does not arrive within ~20 s makes uocr_moe_check
- * report UOCR_ERR_TIMEOUT, after which the ranks' plans must be recreated.
+ * barriers; a rank that does not arrive within 20 s (UOCR_EP_WAIT_MS in the
+ * environment at plan creation overrides it) makes uocr_moe_check report
+ * UOCR_ERR_TIMEOUT, after which the ranks' plans must be recreated.
  * The result equals, bit for bit, a single-GPU plan's on the same rows.
  *
  * Setup: each rank gets its handle, the ranks exchange them (any transport:

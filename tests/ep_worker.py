@@ -1,7 +1,12 @@
 """One rank of the multi-GPU expert-parallel check (run by torchrun from
 test_ep_multi_gpu.py, one process per GPU): config-3 shapes, this rank's
 slice of the rows through an expert-parallel plan, compared bitwise with a
-single-GPU plan over the same rows on the same GPU."""
+single-GPU plan over the same rows on the same GPU.
+
+EP_MODE=timeout checks failure detection instead: rank 1 connects and then
+never takes part in a forward (it waits, alive, at a host barrier), so rank
+0's device barrier must give up after UOCR_EP_WAIT_MS and uocr_moe_check
+must report UOCR_ERR_TIMEOUT — no fault, no hang."""
 import datetime
 import os
 import sys
@@ -34,6 +39,23 @@ def main():
     ep.connect(plan)
     x = C.device_input(cfg, total, device=dev)[start:start + count].contiguous()
     y = torch.empty_like(x)
+    if os.environ.get("EP_MODE") == "timeout":
+        result = 0
+        if rank == 0:
+            plan.forward(0, x, y)
+            try:
+                plan.check()
+                result = 1  # should not complete without the peer
+            except M.UocrError as e:
+                result = 0 if e.code == 6 else 2
+        flag = torch.tensor([result], device=dev)
+        dist.all_reduce(flag)  # rank 1 waits here, alive, until rank 0 is done
+        dist.barrier()
+        plan.close()
+        dist.destroy_process_group()
+        if rank == 0:
+            print(f"EP timeout world {world}: {'EP_TIMEOUT_OK' if flag.item() == 0 else 'EP_TIMEOUT_BAD'}")
+        sys.exit(0 if flag.item() == 0 else 1)
     for _ in range(3):  # repeated calls reuse the exchange buffers
         plan.forward(0, x, y)
     plan.check()

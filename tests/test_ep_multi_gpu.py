@@ -34,3 +34,19 @@ def test_ep_ranks_equal_single_gpu(world, strided, rows):
     print(r.stdout[-2000:], r.stderr[-4000:])
     assert r.returncode == 0
     assert "EP_OK" in r.stdout
+
+
+def test_ep_missing_peer_times_out():
+    """A rank that never joins a forward: the others' bounded device barrier
+    gives up after UOCR_EP_WAIT_MS (1 s here) and check() reports a timeout."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, EP_MODE="timeout", EP_ROWS="1024", UOCR_EP_WAIT_MS="1000", NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.join(HERE, "ep_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    print(r.stdout[-2000:], r.stderr[-4000:])
+    assert r.returncode == 0
+    assert "EP_TIMEOUT_OK" in r.stdout
