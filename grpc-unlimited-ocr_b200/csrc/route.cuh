@@ -30,10 +30,11 @@ struct SmemRoute {
   int ids[kDecodeMaxRows * kMaxTopK];
   float w[kDecodeMaxRows * kMaxTopK];
   int slot_of[kMaxExperts];
-  float ebuf[8][kMaxExperts];
+  alignas(16) float ebuf[8][kMaxExperts];  // 16-byte rows: read as float4 by softmax_topk_warp
 };
 
-// Softmax + top-k of one row by one warp; lane 0 writes ids/weights.
+// Softmax + top-k of one row by one warp; lanes 0..K-1 write ids/weights
+// (rank order). Every intermediate stays in registers.
 template <typename IdT>
 __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm, float* ebuf, IdT* ids,
                                   float* weights) {
@@ -64,8 +65,18 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
     __syncwarp();
     float inv = 0.0f;
     if (lane == 0) {
+      // The reference's double total in index order (ops.cpp:179-183); the
+      // 16-byte reads are issued ahead of the dependent adds.
       double total = 0.0;
-      for (int e = 0; e < E; ++e) total += static_cast<double>(ebuf[e]);
+      int e = 0;
+      for (; e + 3 < E; e += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(ebuf + e);
+        total += static_cast<double>(q.x);
+        total += static_cast<double>(q.y);
+        total += static_cast<double>(q.z);
+        total += static_cast<double>(q.w);
+      }
+      for (; e < E; ++e) total += static_cast<double>(ebuf[e]);
       inv = static_cast<float>(1.0 / total);
     }
     inv = __shfl_sync(0xffffffffu, inv, 0);
@@ -74,9 +85,9 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
       if (lane + 32 * i < E) v[i] = v[i] * inv;
     __syncwarp();
   }
-  float sum = 0.0f;
-  float chosen[kMaxTopK];
-  int chosen_id[kMaxTopK];
+  // K rounds of warp argmax (lower id on a tie); lane j keeps round j's winner.
+  float sum = 0.0f, my_w = 0.0f;
+  int my_id = 0;
   for (int j = 0; j < K; ++j) {
     float best = -INFINITY;
     int best_e = 0x7fffffff;
@@ -103,15 +114,15 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
       for (int i = 0; i < 4; ++i)
         if (i == (best_e >> 5)) v[i] = -INFINITY;
     }
-    chosen[j] = best;
-    chosen_id[j] = best_e;
+    if (lane == j) {
+      my_w = best;
+      my_id = best_e;
+    }
     sum += best;
   }
-  if (lane == 0) {
-    for (int j = 0; j < K; ++j) {
-      ids[j] = static_cast<IdT>(chosen_id[j]);
-      weights[j] = renorm ? chosen[j] / sum : chosen[j];
-    }
+  if (lane < K) {
+    ids[lane] = static_cast<IdT>(my_id);
+    weights[lane] = renorm ? my_w / sum : my_w;
   }
 }
 
@@ -181,11 +192,28 @@ __device__ inline void route_from_logits(const float* logits, int T, int E, int 
     if (e >= 0 && e < E) atomicAdd(&r->ntok[r->slot_of[e]], 1);
   }
   route_sync(bar, nthreads);
-  if (tid == 0) {
-    int acc = 0;
-    for (int u = 0; u < r->count; ++u) {
-      r->base[u] = acc;
-      acc += r->ntok[u];
+  if (warp == 0) {
+    // base = exclusive scan of ntok over the experts in ascending id.
+    const int U = r->count;
+    int cnt[4], local = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int u = lane * 4 + q;
+      cnt[q] = u < U ? r->ntok[u] : 0;
+      local += cnt[q];
+    }
+    int incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int acc = incl - local;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int u = lane * 4 + q;
+      if (u < U) r->base[u] = acc;
+      acc += cnt[q];
     }
   }
   route_sync(bar, nthreads);

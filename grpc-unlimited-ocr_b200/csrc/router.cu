@@ -135,9 +135,11 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   const int cta = blockIdx.x;
   const int per = (E + kRouterCluster - 1) / kRouterCluster;  // expert rows per CTA (layout stride)
   const int ne = cta < E ? (E - cta + kRouterCluster - 1) / kRouterCluster : 0;
+  // Rows 8 floats longer than H: the router rows (and the x rows) that the
+  // lanes of a warp read at the same offset fall in different banks.
   const int xstride = H + 8;
-  float* ws = smem;                                 // [per][H]
-  float* xs = smem + static_cast<size_t>(per) * H;  // [T][H + 8]
+  float* ws = smem;                                       // [per][H + 8]
+  float* xs = smem + static_cast<size_t>(per) * xstride;  // [T][H + 8]
   // Bulk copies (TMA engine, one thread issues them all): the CTA's router
   // rows before the wait for x — one round trip for all of them — then the x rows.
   __shared__ __align__(8) uint64_t bars[2];
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
     if (ne > 0) {
       mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(ne) * H * 4);
       for (int i = 0; i < ne; ++i)
-        bulk_g2s(ws + static_cast<size_t>(i) * H, router + static_cast<int64_t>(cta + kRouterCluster * i) * H,
+        bulk_g2s(ws + static_cast<size_t>(i) * xstride, router + static_cast<int64_t>(cta + kRouterCluster * i) * H,
                  static_cast<uint32_t>(H) * 4, &bars[0]);
     } else {
       mbar_arrive(&bars[0]);
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
     const bool valid = item < n_items;
     const int i = valid ? item / (T * 8) : 0, t = valid ? (item / 8) % T : 0, l8 = item & 7;
     const float* xr = xs + t * xstride;
-    const float* wr = ws + static_cast<size_t>(i) * H;
+    const float* wr = ws + static_cast<size_t>(i) * xstride;
     float acc = 0.0f, tail = 0.0f;
     if (valid) {
       int k = l8;
@@ -216,14 +218,14 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
 
 size_t router_cluster_smem(int T, int H, int E) {
   const size_t per = static_cast<size_t>((E + kRouterCluster - 1) / kRouterCluster);
-  return (per * H + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
+  return ((per + static_cast<size_t>(T)) * (H + 8)) * sizeof(float);
 }
 
 // Standalone softmax/top-k over logits rows: one warp per row (the op-level
 // mirror of expert_topk, int64 ids like the reference).
 __global__ void __launch_bounds__(256) topk_rows_kernel(const float* __restrict__ logits, int64_t rows, int E,
                                                         int K, int renorm, int64_t* ids, float* weights) {
-  __shared__ float ebuf[8][kMaxExperts];
+  __shared__ __align__(16) float ebuf[8][kMaxExperts];
   const int warp = threadIdx.x >> 5;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
   if (r >= rows) return;
