@@ -40,19 +40,25 @@ __device__ inline void raise_error(ErrorWord* e, int code, int where, int a, int
 }
 
 // Routing of one decode batch (rows <= kDecodeMaxRows), written by the
-// router's last block. Experts appear once each, in ascending id order (for
-// the op-level mirror of expert_ffn_one: in rank order), with the batch rows
-// routed to them in row order. Slot = slot_base[u] + s indexes the [slots, F]
-// activation scratch.
+// router. Experts appear once each, in ascending id order (for the op-level
+// mirror of expert_ffn_one: in rank order). Expert u owns the slots
+// slot_base[u] .. slot_base[u] + tok_count[u] - 1, its batch rows in row
+// order; slot s names batch row slot_tok[s] with combine weight slot_w[s] and
+// indexes the [slots, F] activation scratch.
 struct DecodeRoute {
   int active_count;
   int slot_total;
+  int reserved[2];
   int active_expert[kMaxActive];
   int tok_count[kMaxActive];
   int slot_base[kMaxActive];
-  int tok_index[kMaxActive][kDecodeMaxRows];
-  float tok_weight[kMaxActive][kDecodeMaxRows];
+  int slot_tok[kMaxActive];
+  float slot_w[kMaxActive];
 };
+
+// Shared-memory floats one warp's softmax/top-k needs: the row's keys, then
+// the selected weights and ids in rank order.
+constexpr int kTopkScratch = kMaxExperts + 2 * kMaxTopK;
 
 // A stack of weight rows: bf16, or int8 with one fp32 scale per row.
 struct Bf16Rows {

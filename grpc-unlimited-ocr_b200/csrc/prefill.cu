@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) router_logits_rows_kernel(const float* __
 
 __global__ void __launch_bounds__(256) topk_rows_i32_kernel(const float* __restrict__ logits, int T, int E, int K,
                                                             int renorm, int* ids, float* weights) {
-  __shared__ __align__(16) float ebuf[8][kMaxExperts];
+  __shared__ __align__(16) float ebuf[8][kTopkScratch];
   const int warp = threadIdx.x >> 5;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
   if (r >= T) return;

@@ -11,16 +11,21 @@
 // logits and so holds the same table; nothing is exchanged between blocks.
 #pragma once
 
+#include <cstddef>
+
 #include "moe_common.cuh"
 
 namespace uocr_b200 {
 
-// Routing table in shared memory: experts in ascending id order, each with
-// the batch rows routed to it in row order. Expert u's rows occupy slots
+// Routing table in shared memory. Its leading members have DecodeRoute's
+// layout (the global form written by the router), so the table moves between
+// the two as a flat copy of 16-byte words. Expert u (ascending id) owns slots
 // base[u] .. base[u] + ntok[u] - 1; a slot indexes the [slots, F] activation
 // rows and names its batch row and combine weight.
 struct SmemRoute {
   int count;
+  int slot_total;
+  int reserved[2];
   int expert[kMaxActive];
   int ntok[kMaxActive];
   int base[kMaxActive];
@@ -29,22 +34,78 @@ struct SmemRoute {
   // scratch of route_from_logits
   int ids[kDecodeMaxRows * kMaxTopK];
   float w[kDecodeMaxRows * kMaxTopK];
-  int slot_of[kMaxExperts];
-  alignas(16) float ebuf[8][kMaxExperts];  // 16-byte rows: read as float4 by softmax_topk_warp
+  alignas(16) unsigned rowmask[kDecodeMaxRows][4];  // experts of each row, 128-bit mask
+  alignas(16) float ebuf[8][kTopkScratch];
 };
+static_assert(offsetof(SmemRoute, count) == offsetof(DecodeRoute, active_count), "table layout");
+static_assert(offsetof(SmemRoute, expert) == offsetof(DecodeRoute, active_expert), "table layout");
+static_assert(offsetof(SmemRoute, ntok) == offsetof(DecodeRoute, tok_count), "table layout");
+static_assert(offsetof(SmemRoute, base) == offsetof(DecodeRoute, slot_base), "table layout");
+static_assert(offsetof(SmemRoute, slot_tok) == offsetof(DecodeRoute, slot_tok), "table layout");
+static_assert(offsetof(SmemRoute, slot_w) == offsetof(DecodeRoute, slot_w), "table layout");
+static_assert(sizeof(DecodeRoute) % 16 == 0, "table copied in 16-byte words");
 
-// Softmax + top-k of one row by one warp; lanes 0..K-1 write ids/weights
-// (rank order). Every intermediate stays in registers.
-template <typename IdT>
-__device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm, float* ebuf, IdT* ids,
+// Logits of a row: from global memory through L2 (written by another block or
+// an earlier grid), or from shared memory.
+template <bool kShared>
+__device__ __forceinline__ float load_logit(const float* p) {
+  if constexpr (kShared)
+    return *p;
+  else
+    return __ldcg(p);
+}
+
+// Nonzero softmax numerators at or above this make every partial sum of a
+// row exact in double: each is then a multiple of 2^-45 (a float >= 2^-22 has
+// an ulp >= 2^-45), and each of at most 128 terms is below 2 (the max-shifted
+// exp), so every partial sum is an integer multiple of 2^-45 below 2^8,
+// i.e. below 2^53 units. Exact sums do not depend on the order of the adds.
+constexpr float kExactSumFloor = 2.384185791015625e-07f;  // 2^-22
+
+// Rank of each of the lane's N elements e = lane + 32 i among the row's E
+// keys in shared memory (padded to a multiple of 4 with -inf): the number of
+// keys that come first (higher value, or the same value and a lower id).
+template <int N>
+__device__ __forceinline__ void rank_keys(const float* keys, int Epad, int lane, const float (&key)[4],
+                                          int (&rank)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) rank[i] = 0;
+  for (int c = 0; c < Epad; c += 4) {
+    const float4 q = *reinterpret_cast<const float4*>(keys + c);
+    const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        rank[i] += (qv[j] > key[i]) | ((qv[j] == key[i]) & (c + j < lane + 32 * i));
+  }
+}
+
+// Softmax + top-k of one row by one warp; lanes 0..K-1 write ids/weights in
+// rank order. `scratch` is kTopkScratch floats of shared memory (16-byte
+// aligned) owned by the warp.
+//   softmax: max shift, float exp, the reference's double total in index
+//     order (ops.cpp:179-183) — as a warp tree when every numerator is 0 or
+//     at least kExactSumFloor (then the total is exact and equals the
+//     sequential one bit for bit), else sequentially by lane 0 — and a
+//     multiply by float(1 / total);
+//   top-k: each element's rank is counted directly (higher probability first,
+//     lower id on a tie, feed_forward.cpp:46-48); ranks below K are the
+//     selection. A NaN probability (NaN logits) ranks after every number.
+//   renormalisation divides by the rank-order float sum of the k weights.
+template <typename IdT, bool kSharedLogits = false>
+__device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm, float* scratch, IdT* ids,
                                   float* weights) {
   const int lane = threadIdx.x & 31;
+  float* keys = scratch;                                           // [kMaxExperts]
+  float* sel_w = scratch + kMaxExperts;                            // [kMaxTopK]
+  int* sel_id = reinterpret_cast<int*>(scratch + kMaxExperts + kMaxTopK);  // [kMaxTopK]
   float v[4];
   float peak = -INFINITY;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < E ? __ldcg(logits + e) : -INFINITY;
+    v[i] = e < E ? load_logit<kSharedLogits>(logits + e) : -INFINITY;
     peak = fmaxf(peak, v[i]);
   }
 #pragma unroll
@@ -52,78 +113,69 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
   if (peak == -INFINITY) {
     // A fully masked row softmaxes to zeros (ops.cpp:175-177).
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = lane + 32 * i < E ? 0.0f : -INFINITY;
+    for (int i = 0; i < 4; ++i) v[i] = 0.0f;
   } else {
+    bool exact = true;
+    double part = 0.0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) {
+      if (lane + 32 * i < E) {
         v[i] = expf(v[i] - peak);
-        ebuf[e] = v[i];
+        exact &= v[i] == 0.0f || v[i] >= kExactSumFloor;
+        part += static_cast<double>(v[i]);
       }
     }
-    __syncwarp();
-    float inv = 0.0f;
-    if (lane == 0) {
-      // The reference's double total in index order (ops.cpp:179-183); the
-      // 16-byte reads are issued ahead of the dependent adds.
-      double total = 0.0;
-      int e = 0;
-      for (; e + 3 < E; e += 4) {
-        const float4 q = *reinterpret_cast<const float4*>(ebuf + e);
-        total += static_cast<double>(q.x);
-        total += static_cast<double>(q.y);
-        total += static_cast<double>(q.z);
-        total += static_cast<double>(q.w);
-      }
-      for (; e < E; ++e) total += static_cast<double>(ebuf[e]);
-      inv = static_cast<float>(1.0 / total);
-    }
-    inv = __shfl_sync(0xffffffffu, inv, 0);
+    double total;
+    if (__all_sync(0xffffffffu, exact)) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (lane + 32 * i < E) v[i] = v[i] * inv;
-    __syncwarp();
-  }
-  // K rounds of warp argmax (lower id on a tie); lane j keeps round j's winner.
-  float sum = 0.0f, my_w = 0.0f;
-  int my_id = 0;
-  for (int j = 0; j < K; ++j) {
-    float best = -INFINITY;
-    int best_e = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (v[i] > best || (v[i] == best && e < best_e))) {
-        best = v[i];
-        best_e = e;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
-      if (ob > best || (ob == best && oe < best_e)) {
-        best = ob;
-        best_e = oe;
-      }
-    }
-    // Remove the winner from its owner lane (a removed slot can never win again).
-    if ((best_e & 31) == lane) {
+      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+      total = part;
+    } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        if (i == (best_e >> 5)) v[i] = -INFINITY;
+        if (lane + 32 * i < E) keys[lane + 32 * i] = v[i];
+      __syncwarp();
+      total = 0.0;
+      if (lane == 0)
+        for (int e = 0; e < E; ++e) total += static_cast<double>(keys[e]);
+      total = __shfl_sync(0xffffffffu, total, 0);
+      __syncwarp();
     }
-    if (lane == j) {
-      my_w = best;
-      my_id = best_e;
-    }
-    sum += best;
+    const float inv = static_cast<float>(1.0 / total);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = v[i] * inv;
   }
+  const int Epad = (E + 3) & ~3;
+  float key[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = e < E && !isnan(v[i]) ? v[i] : -INFINITY;
+    if (e < Epad) keys[e] = key[i];
+  }
+  __syncwarp();
+  int rank[4];
+  if (E <= 64)
+    rank_keys<2>(keys, Epad, lane, key, rank);
+  else
+    rank_keys<4>(keys, Epad, lane, key, rank);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E && rank[i] < K) {
+      sel_w[rank[i]] = v[i];
+      sel_id[rank[i]] = e;
+    }
+  }
+  __syncwarp();
   if (lane < K) {
-    ids[lane] = static_cast<IdT>(my_id);
-    weights[lane] = renorm ? my_w / sum : my_w;
+    float sum = 0.0f;
+    for (int j = 0; j < K; ++j) sum += sel_w[j];
+    const float w = sel_w[lane];
+    ids[lane] = static_cast<IdT>(sel_id[lane]);
+    weights[lane] = renorm ? w / sum : w;
   }
+  __syncwarp();
 }
 
 // Synchronises the threads building a routing table: one warp (nthreads 32)
@@ -135,134 +187,116 @@ __device__ __forceinline__ void route_sync(int bar, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthreads) : "memory");
 }
 
-// Builds the routing table of T rows from logits [T, E] with `nthreads`
-// threads (one warp, or a multiple of 32 synchronising on named barrier
-// `bar`; tid < nthreads) that all call this function. When ids_out is not
-// null the rank-order ids/weights are also written there.
+// Number of set bits of a 128-bit mask below bit e.
+__device__ __forceinline__ int popc_below(const uint4& m, int e) {
+  const unsigned w[4] = {m.x, m.y, m.z, m.w};
+  const int q = e >> 5;
+  int n = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i < q) n += __popc(w[i]);
+    if (i == q) n += __popc(w[i] & ((1u << (e & 31)) - 1u));
+  }
+  return n;
+}
+
+// Builds the routing table of T rows from logits [T, E] (global memory, or
+// shared memory when kSharedLogits) with `nthreads` threads (one warp, or a
+// multiple of 32 synchronising on named barrier `bar`; tid < nthreads) that
+// all call this function. When ids_out is not null the rank-order
+// ids/weights are also written there.
+//
+// Each selection i (row t, expert e) finds its slot directly: slot = the
+// number of selections of experts below e (= the expert's base) plus the
+// number of earlier rows that chose e, so an expert's rows stay in row order;
+// the expert's place among the active experts is the number of active experts
+// below it (the union of the rows' masks).
+template <bool kSharedLogits = false>
 __device__ inline void route_from_logits(const float* logits, int T, int E, int K, int renorm, SmemRoute* r, int tid,
                                          int nthreads, int bar, int* ids_out, float* w_out) {
   const int warp = tid >> 5, lane = tid & 31;
   const int row_warps = (nthreads >> 5) < 8 ? (nthreads >> 5) : 8;
   if (warp < row_warps)
-    for (int t = warp; t < T; t += row_warps)
-      softmax_topk_warp<int>(logits + static_cast<int64_t>(t) * E, E, K, renorm, r->ebuf[warp], r->ids + t * K,
-                             r->w + t * K);
-  for (int i = tid; i < kMaxExperts; i += nthreads) r->slot_of[i] = 0;
-  for (int i = tid; i < kMaxActive; i += nthreads) r->ntok[i] = 0;
+    for (int t = warp; t < T; t += row_warps) {
+      softmax_topk_warp<int, kSharedLogits>(logits + static_cast<int64_t>(t) * E, E, K, renorm, r->ebuf[warp],
+                                            r->ids + t * K, r->w + t * K);
+      const int e = lane < K ? r->ids[t * K + lane] : -1;
+      const bool valid = e >= 0 && e < E;
+      unsigned m[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) m[q] = __reduce_or_sync(0xffffffffu, valid && (e >> 5) == q ? 1u << (e & 31) : 0u);
+      if (lane == 0) *reinterpret_cast<uint4*>(r->rowmask[t]) = make_uint4(m[0], m[1], m[2], m[3]);
+    }
   route_sync(bar, nthreads);
+  uint4 used = make_uint4(0u, 0u, 0u, 0u);
+  int slots = 0;
+  for (int t = 0; t < T; ++t) {
+    const uint4 m = *reinterpret_cast<const uint4*>(r->rowmask[t]);
+    used.x |= m.x;
+    used.y |= m.y;
+    used.z |= m.z;
+    used.w |= m.w;
+    slots += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+  }
+  if (tid == 0) {
+    r->count = __popc(used.x) + __popc(used.y) + __popc(used.z) + __popc(used.w);
+    r->slot_total = slots;
+  }
   const int n = T * K;
   for (int i = tid; i < n; i += nthreads) {
     const int e = r->ids[i];
-    if (e >= 0 && e < E) r->slot_of[e] = 1;  // the same value from every writer
+    const float wi = r->w[i];
     if (ids_out != nullptr) {
       ids_out[i] = e;
-      w_out[i] = r->w[i];
+      w_out[i] = wi;
     }
-  }
-  route_sync(bar, nthreads);
-  if (warp == 0) {
-    // Experts in ascending id order: exclusive scan of the used flags.
-    int flags[4], local = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int e = lane * 4 + q;
-      flags[q] = e < E ? r->slot_of[e] : 0;
-      local += flags[q];
-    }
-    int incl = local;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += v;
-    }
-    int pos = incl - local;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int e = lane * 4 + q;
-      if (flags[q]) {
-        r->expert[pos] = e;
-        r->slot_of[e] = pos++;
-      }
-    }
-    if (lane == 31) r->count = incl;
-  }
-  route_sync(bar, nthreads);
-  for (int i = tid; i < n; i += nthreads) {
-    const int e = r->ids[i];
-    if (e >= 0 && e < E) atomicAdd(&r->ntok[r->slot_of[e]], 1);
-  }
-  route_sync(bar, nthreads);
-  if (warp == 0) {
-    // base = exclusive scan of ntok over the experts in ascending id.
-    const int U = r->count;
-    int cnt[4], local = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int u = lane * 4 + q;
-      cnt[q] = u < U ? r->ntok[u] : 0;
-      local += cnt[q];
-    }
-    int incl = local;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
-    }
-    int acc = incl - local;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int u = lane * 4 + q;
-      if (u < U) r->base[u] = acc;
-      acc += cnt[q];
-    }
-  }
-  route_sync(bar, nthreads);
-  // A selection's place among its expert's rows = how many earlier rows chose
-  // that expert (ids within a row are distinct), so rows stay in row order.
-  for (int i = tid; i < n; i += nthreads) {
-    const int t = i / K, e = r->ids[i];
     if (e < 0 || e >= E) continue;
-    int place = 0;
-    for (int q = 0; q < t * K; ++q) place += r->ids[q] == e;
-    const int slot = r->base[r->slot_of[e]] + place;
-    r->slot_tok[slot] = t;
-    r->slot_w[slot] = r->w[i];
+    int less = 0, same = 0, cnt = 0;
+    for (int j = 0; j < n; ++j) {
+      const int ej = r->ids[j];
+      less += (ej >= 0) & (ej < e);
+      cnt += ej == e;
+      same += (ej == e) & (j < i);
+    }
+    const int slot = less + same;
+    r->slot_tok[slot] = i / K;
+    r->slot_w[slot] = wi;
+    if (same == 0) {
+      const int u = popc_below(used, e);
+      r->expert[u] = e;
+      r->ntok[u] = cnt;
+      r->base[u] = less;
+    }
   }
   route_sync(bar, nthreads);
 }
 
 // Writes a table built in shared memory to its global form (route_from_table's input).
 __device__ inline void route_to_table(const SmemRoute* r, DecodeRoute* g, int tid, int nthreads) {
-  const int U = r->count;
-  if (tid == 0) {
-    g->active_count = U;
-    g->slot_total = U > 0 ? r->base[U - 1] + r->ntok[U - 1] : 0;
-  }
-  for (int u = tid; u < U; u += nthreads) {
-    const int base = r->base[u], cnt = r->ntok[u];
-    g->active_expert[u] = r->expert[u];
-    g->tok_count[u] = cnt;
-    g->slot_base[u] = base;
-    for (int j = 0; j < cnt; ++j) {
-      g->tok_index[u][j] = r->slot_tok[base + j];
-      g->tok_weight[u][j] = r->slot_w[base + j];
-    }
-  }
+  constexpr int kWords = static_cast<int>(sizeof(DecodeRoute) / 16);
+  const uint4* src = reinterpret_cast<const uint4*>(r);
+  uint4* dst = reinterpret_cast<uint4*>(g);
+  for (int i = tid; i < kWords; i += nthreads) dst[i] = src[i];
 }
 
-// Copies a precomputed routing table (the expert_ffn_one mirrors) into shared memory.
+// Copies a table from its global form into shared memory: every load is
+// issued before the first store, so the copy costs one trip to L2.
 __device__ inline void route_from_table(const DecodeRoute* g, int T, SmemRoute* r, int tid, int nthreads, int bar) {
-  const int U = __ldcg(&g->active_count);
-  if (tid == 0) r->count = U;
-  for (int u = tid; u < U; u += nthreads) {
-    const int base = __ldcg(&g->slot_base[u]);
-    const int cnt = __ldcg(&g->tok_count[u]);
-    r->expert[u] = __ldcg(&g->active_expert[u]);
-    r->ntok[u] = cnt;
-    r->base[u] = base;
-    for (int j = 0; j < cnt; ++j) {
-      r->slot_tok[base + j] = __ldcg(&g->tok_index[u][j]);
-      r->slot_w[base + j] = __ldcg(&g->tok_weight[u][j]);
+  constexpr int kWords = static_cast<int>(sizeof(DecodeRoute) / 16);
+  constexpr int kPer = (kWords + 31) / 32;
+  const uint4* src = reinterpret_cast<const uint4*>(g);
+  uint4* dst = reinterpret_cast<uint4*>(r);
+  for (int base = 0; base < kWords; base += kPer * nthreads) {
+    uint4 v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = base + k * nthreads + tid;
+      if (i < kWords) v[k] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = base + k * nthreads + tid;
+      if (i < kWords) dst[i] = v[k];
     }
   }
   (void)T;

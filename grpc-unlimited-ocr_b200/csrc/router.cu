@@ -123,9 +123,10 @@ constexpr int kRouterCluster = 8;  // CTAs of the decode router's cluster (porta
 // The decode router as one 8-CTA thread-block cluster: CTA c stages the router
 // rows of experts c, c+8, ... into shared memory (before waiting for the grid
 // that writes x), computes their logits for every batch row in the exact dot
-// order, and after a cluster barrier (release/acquire: the other CTAs' logits
-// are visible) CTA 0 builds the routing table. No global ticket, no last-block
-// handshake.
+// order — into global memory and into CTA 0's shared memory (distributed
+// shared memory) — and after a cluster barrier (release/acquire: the other
+// CTAs' logits are visible) CTA 0 builds the routing table from its own shared
+// memory. No global ticket, no last-block handshake.
 __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __restrict__ x, int T, int H,
                                                              const float* __restrict__ router,
                                                              const float* __restrict__ bias, int E,
@@ -140,6 +141,8 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   const int xstride = H + 8;
   float* ws = smem;                                       // [per][H + 8]
   float* xs = smem + static_cast<size_t>(per) * xstride;  // [T][H + 8]
+  // The batch's logits [T, E], gathered in CTA 0's copy of this array.
+  __shared__ __align__(16) float cl_logits[kDecodeMaxRows * kMaxExperts];
   // Bulk copies (TMA engine, one thread issues them all): the CTA's router
   // rows before the wait for x — one round trip for all of them — then the x rows.
   __shared__ __align__(8) uint64_t bars[2];
@@ -156,6 +159,9 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
       mbar_arrive(&bars[0]);
     }
   }
+  // Every CTA of the cluster has started before any writes another's shared
+  // memory: this arrive pairs with the wait before the chains.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   pdl_wait();  // x is written by the previous grid
   pdl_launch_dependents();
   if (tid == 0) {
@@ -167,7 +173,10 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   __syncthreads();  // the barriers are initialised before anyone waits on them
   const bool ok = mbar_wait(&bars[0], 0) & mbar_wait(&bars[1], 0);
   if (!ok && tid == 0 && ro.err != nullptr) raise_error(ro.err, kDevWaitTimeout, 40, cta, 0);
-  __syncthreads();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  // This thread's address of CTA 0's cl_logits.
+  uint32_t cl0;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(cl0) : "r"(smem_addr(cl_logits)));
   // Chains (expert i, row t, lane l8): the eight lanes of a chain group are
   // eight consecutive threads of one warp.
   const int n_items = ne * T * 8;
@@ -206,13 +215,16 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
       float sum = __fadd_rn(__fadd_rn(lo, hi), tail);
       if (bias != nullptr) sum = __fadd_rn(sum, bias[e]);
       logits[static_cast<int64_t>(t) * E + e] = sum;
+      if (ro.table != nullptr)
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cl0 + static_cast<uint32_t>(t * E + e) * 4u), "f"(sum)
+                     : "memory");
     }
   }
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   if (cta != 0 || ro.table == nullptr) return;
   __shared__ SmemRoute r;
-  route_from_logits(logits, T, E, ro.top_k, ro.renorm, &r, tid, blockDim.x, 1, ro.ids_out, ro.w_out);
+  route_from_logits<true>(cl_logits, T, E, ro.top_k, ro.renorm, &r, tid, blockDim.x, 1, ro.ids_out, ro.w_out);
   route_to_table(&r, ro.table, tid, blockDim.x);
 }
 
@@ -225,7 +237,7 @@ size_t router_cluster_smem(int T, int H, int E) {
 // mirror of expert_topk, int64 ids like the reference).
 __global__ void __launch_bounds__(256) topk_rows_kernel(const float* __restrict__ logits, int64_t rows, int E,
                                                         int K, int renorm, int64_t* ids, float* weights) {
-  __shared__ __align__(16) float ebuf[8][kMaxExperts];
+  __shared__ __align__(16) float ebuf[8][kTopkScratch];
   const int warp = threadIdx.x >> 5;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
   if (r >= rows) return;
@@ -248,8 +260,8 @@ __global__ void route_from_ids_kernel(const int64_t* ids, const float* weights, 
     route->active_expert[j] = static_cast<int>(id);
     route->tok_count[j] = 1;
     route->slot_base[j] = j;
-    route->tok_index[j][0] = 0;
-    route->tok_weight[j][0] = weights[j];
+    route->slot_tok[j] = 0;
+    route->slot_w[j] = weights[j];
   }
 }
 
@@ -284,7 +296,8 @@ cudaError_t launch_router_logits(const float* x, int T, int H, const float* rout
   if (st != cudaSuccess) return st;
   if ((st = prepare_router_decode()) != cudaSuccess) return st;
   const size_t csmem = router_cluster_smem(T, H, E);
-  if (route != nullptr && dev < kMaxDevices && csmem <= g_cluster_dyn_limit[dev]) {
+  if (route != nullptr && T <= kDecodeMaxRows && E <= kMaxExperts && dev < kMaxDevices &&
+      csmem <= g_cluster_dyn_limit[dev]) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(kRouterCluster);
     cfg.blockDim = dim3(256);

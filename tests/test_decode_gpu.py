@@ -146,6 +146,56 @@ def test_tied_router_rows_pick_lower_id(cuda):
     assert np.array_equal(ids, want.ids)  # exact ties are not near-ties: no exemption
 
 
+def _topk_want(logits, K):
+    """float64 softmax of each row and its order: higher first, lower id on a tie."""
+    l64 = logits.astype(np.float64)
+    p = np.exp(l64 - l64.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    order = np.stack([np.lexsort((np.arange(row.size), -row)) for row in p])
+    return p, order
+
+
+@pytest.mark.parametrize("E,K", [(8, 3), (37, 6), (64, 6), (64, 8), (100, 1), (128, 8)])
+@pytest.mark.parametrize("renorm", [False, True])
+def test_expert_topk_edge_rows(cuda, E, K, renorm):
+    """uocr_expert_topk on rows that take both totals of the softmax (numerators
+    all >= 2^-22, or some smaller: logits scaled by 40), rows with exact ties,
+    and a fully masked row (softmax of zeros, ops.cpp:175-177)."""
+    import torch
+    rng = np.random.default_rng(E * 31 + K)
+    rows = 64
+    logits = rng.standard_normal((rows, E)).astype(np.float32)
+    logits[rows // 2:] *= 40
+    for r in range(0, rows, 5):  # exact ties, one of them at the top
+        a, b = rng.choice(E, 2, replace=False)
+        logits[r, b] = logits[r, a]
+        if r % 10 == 0:
+            logits[r, a] = logits[r, b] = logits[r].max()
+    logits[3] = -np.inf
+    dl = torch.from_numpy(logits).to(cuda)
+    ids = torch.empty(rows, K, dtype=torch.int64, device=cuda)
+    wts = torch.empty(rows, K, dtype=torch.float32, device=cuda)
+    M.expert_topk(dl, K, renorm, ids, wts)
+    got_ids, got_w = ids.cpu().numpy(), wts.cpu().numpy()
+    p, order = _topk_want(np.where(np.isinf(logits), 0, logits), K)
+    assert np.array_equal(got_ids[3], np.arange(K))
+    if not renorm:
+        assert np.all(got_w[3] == 0)
+    for r in range(rows):
+        if r == 3:
+            continue
+        want = order[r, :K]
+        if not np.array_equal(got_ids[r], want):
+            srt = p[r, order[r, :K + 1]]
+            gaps = np.abs(np.diff(srt)) / np.maximum(srt[:-1], 1e-300)
+            assert gaps.min() < 1e-5, f"row {r}: {got_ids[r]} != {want}"
+            continue
+        w = p[r, want]
+        if renorm:
+            w = w / w.sum()
+        np.testing.assert_allclose(got_w[r], w, rtol=2e-6, atol=1e-30)
+
+
 def test_router_bias(cuda):
     import torch
     rng = np.random.default_rng(3)
