@@ -559,8 +559,7 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   // Programmatic dependent launch chains router -> gate/up -> down (and the
   // next layer's router); the profiling path records events between them instead.
   const bool pdl = ev == nullptr;
-  // The router's last block builds the routing table once; the expert
-  // kernels copy it.
+  // The router builds the routing table once; the expert kernels copy it.
   const RouteOut ro{p->route, K, d.renormalize, p->ids, p->weights, p->counter, p->err};
   UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl, &ro), "forward: router");
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
@@ -635,6 +634,8 @@ int uocr_moe_forward(uocr_moe_plan* p, int64_t layer, const float* x, int64_t ro
   if (rows == 0 && !p->ep) return UOCR_OK;  // an expert-parallel rank takes part with no rows
   if (rows > 0 && (x == nullptr || y == nullptr)) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: null x or y");
   if (rows > 0 && x == y) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: x and y must not overlap");
+  if (rows > 0 && (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: x must be 16-byte aligned");
   const LayerDev& L = p->layers[static_cast<size_t>(layer)];
   if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "forward: layer weights not set");
   DeviceGuard guard(p->d.device);
@@ -654,6 +655,8 @@ int uocr_moe_forward_stack(uocr_moe_plan* p, float* h, int64_t rows, void* strea
     return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: null argument");
   if (rows < 0 || rows > p->d.max_rows)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: rows outside [0, max_rows]");
+  if (rows > 0 && (reinterpret_cast<uintptr_t>(h) & 15) != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: h must be 16-byte aligned");
   if (int rc = ep_ready(p, "forward_stack"); rc != UOCR_OK) return rc;
   if (rows == 0 && !p->ep) return UOCR_OK;
   for (const auto& L : p->layers)

@@ -56,9 +56,9 @@ struct DecodeRoute {
   float slot_w[kMaxActive];
 };
 
-// Shared-memory floats one warp's softmax/top-k needs: the row's keys, then
-// the selected weights and ids in rank order.
-constexpr int kTopkScratch = kMaxExperts + 2 * kMaxTopK;
+// Shared-memory floats one warp's softmax/top-k needs: the row's 64-bit keys,
+// then the selected weights and ids in rank order.
+constexpr int kTopkScratch = 2 * kMaxExperts + 2 * kMaxTopK;
 
 // A stack of weight rows: bf16, or int8 with one fp32 scale per row.
 struct Bf16Rows {

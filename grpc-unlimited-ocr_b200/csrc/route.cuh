@@ -62,22 +62,27 @@ __device__ __forceinline__ float load_logit(const float* p) {
 // i.e. below 2^53 units. Exact sums do not depend on the order of the adds.
 constexpr float kExactSumFloor = 2.384185791015625e-07f;  // 2^-22
 
-// Rank of each of the lane's N elements e = lane + 32 i among the row's E
-// keys in shared memory (padded to a multiple of 4 with -inf): the number of
-// keys that come first (higher value, or the same value and a lower id).
+// Selection key of expert e with probability p: the bits of p (a
+// non-negative float orders like its bits) above ~e, so that a higher
+// probability, then a lower id, gives a larger key and no two keys tie. A NaN
+// probability keys as 0, below every number; padding entries are 0 as a whole.
+__device__ __forceinline__ unsigned long long topk_key(float p, int e) {
+  const unsigned hi = p > 0.0f ? __float_as_uint(p) : 0u;
+  return (static_cast<unsigned long long>(hi) << 32) | (0xffffffffu - static_cast<unsigned>(e));
+}
+
+// Rank of each of the lane's N keys among the row's keys in shared memory
+// (padded to an even count with 0): the number of larger keys.
 template <int N>
-__device__ __forceinline__ void rank_keys(const float* keys, int Epad, int lane, const float (&key)[4],
+__device__ __forceinline__ void rank_keys(const unsigned long long* keys, int Epad, const unsigned long long (&key)[4],
                                           int (&rank)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) rank[i] = 0;
-  for (int c = 0; c < Epad; c += 4) {
-    const float4 q = *reinterpret_cast<const float4*>(keys + c);
-    const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll 4
+  for (int c = 0; c < Epad; c += 2) {
+    const ulonglong2 q = *reinterpret_cast<const ulonglong2*>(keys + c);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int i = 0; i < N; ++i)
-        rank[i] += (qv[j] > key[i]) | ((qv[j] == key[i]) & (c + j < lane + 32 * i));
+    for (int i = 0; i < N; ++i) rank[i] += static_cast<int>(q.x > key[i]) + static_cast<int>(q.y > key[i]);
   }
 }
 
@@ -90,16 +95,18 @@ __device__ __forceinline__ void rank_keys(const float* keys, int Epad, int lane,
 //     sequential one bit for bit), else sequentially by lane 0 — and a
 //     multiply by float(1 / total);
 //   top-k: each element's rank is counted directly (higher probability first,
-//     lower id on a tie, feed_forward.cpp:46-48); ranks below K are the
-//     selection. A NaN probability (NaN logits) ranks after every number.
+//     lower id on a tie, feed_forward.cpp:46-48) as the number of larger
+//     64-bit keys (topk_key); ranks below K are the selection. A NaN
+//     probability (NaN logits) ranks after every number.
 //   renormalisation divides by the rank-order float sum of the k weights.
 template <typename IdT, bool kSharedLogits = false>
 __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm, float* scratch, IdT* ids,
                                   float* weights) {
   const int lane = threadIdx.x & 31;
-  float* keys = scratch;                                           // [kMaxExperts]
-  float* sel_w = scratch + kMaxExperts;                            // [kMaxTopK]
-  int* sel_id = reinterpret_cast<int*>(scratch + kMaxExperts + kMaxTopK);  // [kMaxTopK]
+  float* sums = scratch;                                                       // [kMaxExperts]
+  auto* keys = reinterpret_cast<unsigned long long*>(scratch);                 // [kMaxExperts]
+  float* sel_w = scratch + 2 * kMaxExperts;                                    // [kMaxTopK]
+  int* sel_id = reinterpret_cast<int*>(scratch + 2 * kMaxExperts + kMaxTopK);  // [kMaxTopK]
   float v[4];
   float peak = -INFINITY;
 #pragma unroll
@@ -133,11 +140,11 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        if (lane + 32 * i < E) keys[lane + 32 * i] = v[i];
+        if (lane + 32 * i < E) sums[lane + 32 * i] = v[i];
       __syncwarp();
       total = 0.0;
       if (lane == 0)
-        for (int e = 0; e < E; ++e) total += static_cast<double>(keys[e]);
+        for (int e = 0; e < E; ++e) total += static_cast<double>(sums[e]);
       total = __shfl_sync(0xffffffffu, total, 0);
       __syncwarp();
     }
@@ -145,20 +152,20 @@ __device__ void softmax_topk_warp(const float* logits, int E, int K, int renorm,
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = v[i] * inv;
   }
-  const int Epad = (E + 3) & ~3;
-  float key[4];
+  const int Epad = (E + 1) & ~1;
+  unsigned long long key[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int e = lane + 32 * i;
-    key[i] = e < E && !isnan(v[i]) ? v[i] : -INFINITY;
+    key[i] = e < E ? topk_key(v[i], e) : 0ull;
     if (e < Epad) keys[e] = key[i];
   }
   __syncwarp();
   int rank[4];
   if (E <= 64)
-    rank_keys<2>(keys, Epad, lane, key, rank);
+    rank_keys<2>(keys, Epad, key, rank);
   else
-    rank_keys<4>(keys, Epad, lane, key, rank);
+    rank_keys<4>(keys, Epad, key, rank);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int e = lane + 32 * i;

@@ -119,13 +119,15 @@ int uocr_moe_set_layer(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_
  * a tie), optional renormalisation, routed SwiGLU experts on bf16-rounded
  * inputs, shared expert, and the combine in expert-id order. ids [rows, k]
  * (int32, rank order) and weights [rows, k] are optional outputs (NULL to
- * skip). x, y, ids and weights are device pointers; x and y must not overlap. */
+ * skip). x, y, ids and weights are device pointers; x and y must not overlap;
+ * x is 16-byte aligned (as every cudaMalloc block is). */
 int uocr_moe_forward(uocr_moe_plan* plan, int64_t layer, const float* x, int64_t rows, float* y, int32_t* ids,
                      float* weights, void* stream);
 
 /* h <- h + MoE_l(h) for l = 0 .. layers-1, in place on device memory h
  * [rows, H]: the decoder's residual around its feed-forward block
- * (src/model/decoder.cpp:181,201) with nothing between the layers. */
+ * (src/model/decoder.cpp:181,201) with nothing between the layers. h is
+ * 16-byte aligned. */
 int uocr_moe_forward_stack(uocr_moe_plan* plan, float* h, int64_t rows, void* stream);
 
 /* Synchronises `stream`, then reports and clears any error word a kernel of

@@ -365,3 +365,9 @@ def test_forward_errors(cuda):
     with pytest.raises(M.UocrError) as e:
         plan.forward(0, x, x)
     assert e.value.code == 1
+    xm = torch.zeros(4 * 64 + 1, device=cuda)[1:].view(4, 64)  # 4 bytes past a 16-byte boundary
+    with pytest.raises(M.UocrError, match="aligned") as e:
+        plan.forward(0, xm, y)
+    assert e.value.code == 1
+    with pytest.raises(M.UocrError, match="aligned"):
+        plan.forward_stack(xm)
