@@ -52,6 +52,7 @@ struct LayerDev {
   bool loaded = false;
   float* router = nullptr;
   float* bias = nullptr;
+  float* norm = nullptr;  // [H] RMSNorm gain (pre-norm plans)
   void* gate = nullptr;
   void* up = nullptr;
   void* down = nullptr;
@@ -111,6 +112,8 @@ struct uocr_moe_plan {
   __nv_bfloat16* act_s = nullptr;
   unsigned* counter = nullptr;  // the decode router's last-block ticket
   ErrorWord* err = nullptr;
+  bool pre_norm = false;
+  float* xnorm = nullptr;  // [max_rows, H] normalised rows for the prefill path (pre-norm plans)
   // Prefill (rows above decode_rows): tcgen05 grouped GEMM path, bf16 weights.
   bool prefill = false;
   PrefillDims pdims{};
@@ -153,6 +156,7 @@ struct uocr_moe_plan {
     const size_t E = static_cast<size_t>(held_experts());
     L.router = c.take<float>(static_cast<size_t>(d.routed_experts) * H);
     L.bias = d.router_bias ? c.take<float>(static_cast<size_t>(d.routed_experts)) : nullptr;
+    L.norm = pre_norm ? c.take<float>(H) : nullptr;
     L.gate = c.take<char>(E * F * H * eb);
     L.up = c.take<char>(E * F * H * eb);
     L.down = c.take<char>(E * H * F * eb);
@@ -180,6 +184,7 @@ struct uocr_moe_plan {
     act_s = c.take<__nv_bfloat16>(dr * (S > 0 ? S : 1));
     counter = c.take<unsigned>(1);
     err = c.take<ErrorWord>(1);
+    if (pre_norm && (prefill || ep)) xnorm = c.take<float>(rows * static_cast<size_t>(d.hidden));
     if (prefill) {
       char* base = c.take<char>(prefill_scratch_bytes(pdims, !ep));
       carve_prefill_scratch(pdims, base, &pscratch, !ep);
@@ -257,6 +262,9 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: layers and max_rows must be positive");
   if (d.weight_format != UOCR_WEIGHT_BF16 && d.weight_format != UOCR_WEIGHT_INT8)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: weight_format must be bf16 (0) or int8 (1)");
+  const bool pre_norm = (d.flags & UOCR_PLAN_PRE_NORM) != 0;
+  if (pre_norm && !(d.rms_norm_eps >= 0.0f && d.rms_norm_eps < 1.0e30f))
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: rms_norm_eps must be a finite value >= 0");
   const bool ep = d.ep_world > 1;
   if (d.ep_world < 0 || d.ep_world > kMaxEpRanks)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: ep_world must be in [0, 8]");
@@ -278,6 +286,7 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
 
   auto* p = new uocr_moe_plan;
   p->d = d;
+  p->pre_norm = pre_norm;
   UOCR_TRY(cudaDeviceGetAttribute(&p->sm_count, cudaDevAttrMultiProcessorCount, d.device), "plan_create: SM count");
   int smem_optin = 0;
   UOCR_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device),
@@ -286,8 +295,8 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   // also holds ~5 KB of static shared memory of its own).
   // (An expert-parallel plan runs every row count through the prefill path.)
   int dr = ep ? 0 : static_cast<int>(d.max_rows < kDecodeMaxRows ? d.max_rows : kDecodeMaxRows);
-  while (dr > 0 && (static_cast<size_t>(d.hidden) + static_cast<size_t>(dr) * (d.hidden + 8)) * 4 + 8192 >
-                       static_cast<size_t>(smem_optin))
+  while (dr > 0 && router_decode_smem(dr, static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
+                                      pre_norm) + 8192 > static_cast<size_t>(smem_optin))
     --dr;
   p->decode_rows = dr;
   if (dr > 0) {
@@ -318,6 +327,7 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     }
   }
   p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
+                 !pre_norm &&
                  decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
                                      static_cast<int>(d.shared_ffn));
 
@@ -449,6 +459,12 @@ int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src
   const int64_t H = p->d.hidden, E = p->d.routed_experts, F = p->d.expert_ffn, S = p->d.shared_ffn;
   int rc = copy_f32(*src, src->router, L.router, static_cast<size_t>(E * H), stream, "router");
   if (rc == UOCR_OK && p->d.router_bias) rc = copy_f32(*src, src->router_bias, L.bias, E, stream, "router_bias");
+  if (rc == UOCR_OK && p->pre_norm) {
+    if (src->norm != nullptr)
+      rc = copy_f32(*src, src->norm, L.norm, static_cast<size_t>(H), stream, "norm");
+    else
+      UOCR_TRY(launch_fill_f32(L.norm, 1.0f, H, stream), "set_layer: unit norm gain");
+  }
   if (!p->ep) {
     if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->gate, E * F, H, L.gate, L.gate_s, stream, "gate");
     if (rc == UOCR_OK) rc = upload_matrix(p, *src, src->up, E * F, H, L.up, L.up_s, stream, "up");
@@ -539,6 +555,12 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts),
             K = static_cast<int>(d.experts_per_token), F = static_cast<int>(d.expert_ffn),
             S = static_cast<int>(d.shared_ffn);
+  const RowNorm norm{L.norm, d.rms_norm_eps, p->pre_norm ? 1 : 0};
+  // The prefill and expert-parallel paths read normalised rows from a copy.
+  if (p->pre_norm && (p->ep || rows > p->decode_rows) && rows > 0) {
+    UOCR_TRY(launch_rms_norm_rows(x, rows, H, norm, p->xnorm, stream), "forward: pre-norm");
+    x = p->xnorm;
+  }
   if (p->ep) {
     EpCall c = ep_call(p, L, x, rows, resid, y);
     UOCR_TRY(ep_forward(c, stream, ev), "forward: expert-parallel prefill");
@@ -561,7 +583,7 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   const bool pdl = ev == nullptr;
   // The router builds the routing table once; the expert kernels copy it.
   const RouteOut ro{p->route, K, d.renormalize, p->ids, p->weights, p->counter, p->err};
-  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl, &ro), "forward: router");
+  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, p->logits, stream, pdl, &ro, norm), "forward: router");
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
   const DecodeRouting routing{nullptr, p->route, E, K, d.renormalize, nullptr, nullptr};
@@ -593,14 +615,14 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
                                         b(L.sdown), routing, p->act, p->act_s, resid, y, p->err, p->sm_count,
-                                        stream, between, pdl),
+                                        stream, between, pdl, norm),
              "forward: experts");
   } else {
     auto q = [](void* v, float* s, int64_t cols) { return Q8Rows{static_cast<const int8_t*>(v), s, cols}; };
     UOCR_TRY(launch_decode_experts_q8(x, T, H, F, S, q(L.gate, L.gate_s, H), q(L.up, L.up_s, H),
                                       q(L.down, L.down_s, F), q(L.sgate, L.sgate_s, H), q(L.sup, L.sup_s, H),
                                       q(L.sdown, L.sdown_s, S), routing, p->act, p->act_s, resid, y, p->err,
-                                      p->sm_count, stream, between, pdl),
+                                      p->sm_count, stream, between, pdl, norm),
              "forward: experts");
   }
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[2], stream), "forward: event");
@@ -899,10 +921,18 @@ int uocr_moe_ep_forward_local(uocr_moe_plan* const* plans, int32_t n, int64_t la
       return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: null or overlapping x, y");
     const LayerDev& L = q->layers[static_cast<size_t>(layer)];
     if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "ep_forward_local: layer weights not set");
-    calls.push_back(ep_call(q, L, x[i], rows[i], nullptr, y[i]));
+    calls.push_back(ep_call(q, L, q->pre_norm && rows[i] > 0 ? q->xnorm : x[i], rows[i], nullptr, y[i]));
   }
   DeviceGuard guard(plans[0]->d.device);
   auto stream = static_cast<cudaStream_t>(stream_v);
+  for (int i = 0; i < n; ++i) {
+    const uocr_moe_plan* q = plans[i];
+    const LayerDev& L = q->layers[static_cast<size_t>(layer)];
+    if (q->pre_norm && rows[i] > 0)
+      UOCR_TRY(launch_rms_norm_rows(x[i], rows[i], static_cast<int>(q->d.hidden),
+                                    RowNorm{L.norm, q->d.rms_norm_eps, 1}, q->xnorm, stream),
+               "ep_forward_local: pre-norm");
+  }
   // Each phase for every rank before the next phase: stream order stands in
   // for the barriers.
   for (auto& c : calls) UOCR_TRY(ep_route(c, stream), "ep_forward_local: route");

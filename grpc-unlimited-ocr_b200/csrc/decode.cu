@@ -26,6 +26,7 @@
 #include "moe_kernels.h"
 #include "ptx.cuh"
 #include "decode_fmt.cuh"
+#include "rms_norm.cuh"
 #include "route.cuh"
 
 namespace uocr_b200 {
@@ -76,7 +77,7 @@ template <typename Rows, int MaxT>
 __global__ void __launch_bounds__(kThreads, 1)
     gate_up_decode_kernel(const float* __restrict__ x, int T, int H, int F, int S, Rows gate, Rows up, Rows sgate,
                           Rows sup, RouteSrc rsrc, __nv_bfloat16* __restrict__ act,
-                          __nv_bfloat16* __restrict__ act_s, ErrorWord* err) {
+                          __nv_bfloat16* __restrict__ act_s, ErrorWord* err, RowNorm norm) {
   using Fm = Fmt<Rows>;
   // bf16-rounded inputs, [T][kQuads][chunks] float4s: the lanes reading
   // consecutive chunks read consecutive 16-byte words (no bank conflicts).
@@ -88,13 +89,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&route_ready, 1);
     fence_mbar_init();
   }
-  // x was written by the grid two launches back, complete before this one started.
+  // The first shared-expert rows of each streaming warp start towards L2
+  // while x is staged (the copy engine fetches them; nothing is held).
+  if (warp < kWorkers && lane == 0) {
+    const int f = blockIdx.x * kWorkers + warp;
+    if (f < S) {
+      prefetch_l2(Fm::row(sgate, f), static_cast<uint32_t>(H) * Fm::kElemBytes);
+      prefetch_l2(Fm::row(sup, f), static_cast<uint32_t>(H) * Fm::kElemBytes);
+    }
+  }
+  // x was written by the grid two launches back, complete before this one
+  // started. Staged once as [T][kQuads][chunks] 16-byte words; with the
+  // pre-norm the raw rows land first, their inverse RMS is taken from shared
+  // memory in the router's summation order (rms_inv_rows, so both see the
+  // same bits), and then they are normalised and rounded in place.
   {
     constexpr int kPer = Fm::kPerChunk, kQ = Fm::kQuads;
     const int nch = H / kPer;
     for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
       const int t = i / H, k = i % H, c = k / kPer, q = (k % kPer) >> 2;
-      xs[((static_cast<size_t>(t) * kQ + q) * nch + c) * 4 + (k & 3)] = bf16_round(__ldcg(x + i));
+      const float v = __ldcg(x + i);
+      xs[((static_cast<size_t>(t) * kQ + q) * nch + c) * 4 + (k & 3)] = norm.on ? v : bf16_round(v);
+    }
+    if (norm.on) {
+      __shared__ double s_part[kDecodeMaxRows * kNormWarps];
+      __shared__ float s_inv[kDecodeMaxRows];
+      __syncthreads();
+      float4* xs4 = reinterpret_cast<float4*>(xs);
+      // word w of row t (elements 4w .. 4w+3) is chunk w / kQ, quad w % kQ
+      rms_inv_rows(
+          T, H, norm.eps,
+          [&](int t, int w) { return xs4[(static_cast<size_t>(t) * kQ + w % kQ) * nch + w / kQ]; }, s_part,
+          s_inv);
+      const float4* g4 = reinterpret_cast<const float4*>(norm.gain);
+      for (int t = 0; t < T; ++t)
+        for (int q = 0; q < kQ; ++q)
+          for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+            float4& v = xs4[(static_cast<size_t>(t) * kQ + q) * nch + c];
+            const float4 g = __ldg(g4 + c * kQ + q);
+            const float inv = s_inv[t];
+            v = make_float4(bf16_round(rms_apply(v.x, inv, g.x)), bf16_round(rms_apply(v.y, inv, g.y)),
+                            bf16_round(rms_apply(v.z, inv, g.z)), bf16_round(rms_apply(v.w, inv, g.w)));
+          }
     }
   }
   __syncthreads();
@@ -450,7 +486,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
                                     Rows sgate, Rows sup, Rows sdown, const DecodeRouting& routing,
                                     __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                     ErrorWord* err, int sm_count, cudaStream_t stream, cudaEvent_t between,
-                                    bool pdl) {
+                                    bool pdl, RowNorm norm) {
   cudaError_t st = prepare_kernels<Rows>();
   if (st != cudaSuccess) return st;
   RouteSrc rs{routing.logits, routing.table, routing.experts, routing.top_k, routing.renormalize, routing.ids_out,
@@ -460,7 +496,7 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   const void* dn = nullptr;
   pick_kernels<Rows>(T, &gu, &dn);
   {
-    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &rs, &act, &act_s, &err};
+    void* args[] = {&x, &T, &H, &F, &S, &gate, &up, &sgate, &sup, &rs, &act, &act_s, &err, &norm};
     st = launch_maybe_pdl(gu, dim3(sm_count),
                           dim3(kThreads), smem, stream, args, pdl);
     if (st != cudaSuccess) return st;
@@ -503,19 +539,20 @@ cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int 
                                        const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
                                        const __nv_bfloat16* sdown, const DecodeRouting& routing, __nv_bfloat16* act,
                                        __nv_bfloat16* act_s, const float* resid, float* y, ErrorWord* err,
-                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl) {
+                                       int sm_count, cudaStream_t stream, cudaEvent_t between, bool pdl,
+                                       RowNorm norm) {
   return launch_decode_experts_t<Bf16Rows>(x, T, H, F, S, Bf16Rows{gate, H}, Bf16Rows{up, H}, Bf16Rows{down, F},
                                            Bf16Rows{sgate, H}, Bf16Rows{sup, H}, Bf16Rows{sdown, S}, routing, act,
-                                           act_s, resid, y, err, sm_count, stream, between, pdl);
+                                           act_s, resid, y, err, sm_count, stream, between, pdl, norm);
 }
 
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
                                      Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
                                      const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
                                      const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between, bool pdl) {
+                                     cudaEvent_t between, bool pdl, RowNorm norm) {
   return launch_decode_experts_t<Q8Rows>(x, T, H, F, S, gate, up, down, sgate, sup, sdown, routing, act, act_s,
-                                         resid, y, err, sm_count, stream, between, pdl);
+                                         resid, y, err, sm_count, stream, between, pdl, norm);
 }
 
 cudaError_t prepare_decode_experts(int max_rows, int H) {

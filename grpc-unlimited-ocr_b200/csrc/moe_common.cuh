@@ -60,6 +60,14 @@ struct DecodeRoute {
 // then the selected weights and ids in rank order.
 constexpr int kTopkScratch = 2 * kMaxExperts + 2 * kMaxTopK;
 
+// The decoder's pre-feed-forward RMSNorm on a layer's input rows (rms_norm.cuh);
+// `on` = 0 leaves the rows as they are.
+struct RowNorm {
+  const float* gain;  // [H]
+  float eps;
+  int on;
+};
+
 // A stack of weight rows: bf16, or int8 with one fp32 scale per row.
 struct Bf16Rows {
   const __nv_bfloat16* w;

@@ -34,9 +34,12 @@ struct RouteOut {
   unsigned* ticket;  // zero between launches; the last block resets it
   ErrorWord* err;    // bounded waits that gave up (null: not reported)
 };
+// With norm.on the router normalises the x rows it stages (rms_norm.cuh).
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
                                  float* logits, cudaStream_t stream, bool pdl = false,
-                                 const RouteOut* route = nullptr);
+                                 const RouteOut* route = nullptr, RowNorm norm = RowNorm{nullptr, 0.0f, 0});
+// Shared memory the decode routers take next to the x rows (plan sizing).
+size_t router_decode_smem(int T, int H, int E, bool norm);
 cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,
                              float* weights, cudaStream_t stream);
 cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int K, int E, DecodeRoute* route,
@@ -58,19 +61,22 @@ struct DecodeRouting {
 };
 
 // Launches gate/up then down+combine; `between` (optional) is recorded
-// between the two, for per-kernel timing.
+// between the two, for per-kernel timing. With norm.on the gate/up kernel
+// normalises the x rows it stages (the residual stays the raw rows).
 cudaError_t launch_decode_experts_bf16(const float* x, int T, int H, int F, int S, const __nv_bfloat16* gate,
                                        const __nv_bfloat16* up, const __nv_bfloat16* down,
                                        const __nv_bfloat16* sgate, const __nv_bfloat16* sup,
                                        const __nv_bfloat16* sdown, const DecodeRouting& routing,
                                        __nv_bfloat16* act, __nv_bfloat16* act_s, const float* resid, float* y,
                                        ErrorWord* err, int sm_count, cudaStream_t stream,
-                                       cudaEvent_t between = nullptr, bool pdl = false);
+                                       cudaEvent_t between = nullptr, bool pdl = false,
+                                       RowNorm norm = RowNorm{nullptr, 0.0f, 0});
 cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S, Q8Rows gate, Q8Rows up,
                                      Q8Rows down, Q8Rows sgate, Q8Rows sup, Q8Rows sdown,
                                      const DecodeRouting& routing, __nv_bfloat16* act, __nv_bfloat16* act_s,
                                      const float* resid, float* y, ErrorWord* err, int sm_count, cudaStream_t stream,
-                                     cudaEvent_t between = nullptr, bool pdl = false);
+                                     cudaEvent_t between = nullptr, bool pdl = false,
+                                     RowNorm norm = RowNorm{nullptr, 0.0f, 0});
 
 // ---- weights and synthetic inputs (weights.cu) ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
@@ -80,5 +86,8 @@ cudaError_t launch_quantize_rows(const void* w, bool bf16, int64_t rows, int64_t
                                  float* scales, cudaStream_t stream);
 cudaError_t launch_synth(uint64_t seed, uint64_t stream_id, float sigma, int64_t offset, int64_t n, bool bf16,
                          void* out, cudaStream_t stream);
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t stream);
+// out [rows, H] = RMSNorm(x) with norm.gain / norm.eps (one warp per row).
+cudaError_t launch_rms_norm_rows(const float* x, int64_t rows, int H, RowNorm norm, float* out, cudaStream_t stream);
 
 }  // namespace uocr_b200

@@ -10,12 +10,36 @@
 // runs them on these logits).
 #include "moe_kernels.h"
 #include "ptx.cuh"
+#include "rms_norm.cuh"
 #include "route.cuh"
 
 namespace uocr_b200 {
 namespace {
 
 constexpr int kStageUnroll = 4;  // float4 loads in flight per thread while staging
+
+// Normalises the T staged x rows (row stride `stride`, 16-byte aligned) in
+// place with the gain staged at gs; every thread of the block (8 warps or
+// more) calls it.
+__device__ void normalize_staged_rows(float* xs, int T, int H, int stride, const float* gs, float eps) {
+  __shared__ double s_part[kDecodeMaxRows * kNormWarps];
+  __shared__ float s_inv[kDecodeMaxRows];
+  rms_inv_rows(
+      T, H, eps, [&](int t, int q) { return reinterpret_cast<const float4*>(xs + static_cast<size_t>(t) * stride)[q]; },
+      s_part, s_inv);
+  const int n4 = H / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(gs);
+  for (int t = 0; t < T; ++t) {
+    float4* r4 = reinterpret_cast<float4*>(xs + static_cast<size_t>(t) * stride);
+    const float inv = s_inv[t];
+    for (int q = threadIdx.x; q < n4; q += blockDim.x) {
+      const float4 v = r4[q], g = g4[q];
+      r4[q] = make_float4(rms_apply(v.x, inv, g.x), rms_apply(v.y, inv, g.y), rms_apply(v.z, inv, g.z),
+                          rms_apply(v.w, inv, g.w));
+    }
+  }
+  __syncthreads();
+}
 
 // One block per expert row of the router: logits[t, e] for every row t of
 // the batch, in the reference's dot order. Launched with programmatic
@@ -24,13 +48,14 @@ constexpr int kStageUnroll = 4;  // float4 loads in flight per thread while stag
 __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restrict__ x, int T, int H,
                                                             const float* __restrict__ router,
                                                             const float* __restrict__ bias, int E,
-                                                            float* __restrict__ logits, RouteOut ro) {
+                                                            float* __restrict__ logits, RouteOut ro, RowNorm norm) {
   extern __shared__ float smem[];
   const int e = blockIdx.x;
   const int tid = threadIdx.x;
   const int xstride = H + 8;  // rows 8 floats apart: the four rows a warp reads sit in different banks
   float* ws = smem;
   float* xs = smem + H;
+  float* gs = xs + static_cast<size_t>(T) * xstride;  // [H] norm gain (norm.on)
   // 16-byte loads, all of a thread's issued before any is stored: one DRAM
   // round trip for the row instead of one per element step.
   const int h4 = H / 4;
@@ -45,6 +70,9 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
       for (int u = 0; u < kStageUnroll; ++u)
         if (i0 + u * static_cast<int>(blockDim.x) < h4) reinterpret_cast<float4*>(ws)[i0 + u * blockDim.x] = v[u];
     }
+    if (norm.on)
+      for (int i = tid; i < h4; i += blockDim.x)
+        reinterpret_cast<float4*>(gs)[i] = __ldg(reinterpret_cast<const float4*>(norm.gain) + i);
   }
   pdl_wait();  // x is written by the previous grid
   pdl_launch_dependents();
@@ -62,6 +90,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const float* __restr
     }
   }
   __syncthreads();
+  if (norm.on) normalize_staged_rows(xs, T, H, xstride, gs, norm.eps);
 
   const int lane8 = tid & 7;
   const int groups = blockDim.x >> 3;
@@ -130,7 +159,8 @@ constexpr int kRouterCluster = 8;  // CTAs of the decode router's cluster (porta
 __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __restrict__ x, int T, int H,
                                                              const float* __restrict__ router,
                                                              const float* __restrict__ bias, int E,
-                                                             float* __restrict__ logits, RouteOut ro) {
+                                                             float* __restrict__ logits, RouteOut ro,
+                                                             RowNorm norm) {
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cta = blockIdx.x;
@@ -141,6 +171,7 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   const int xstride = H + 8;
   float* ws = smem;                                       // [per][H + 8]
   float* xs = smem + static_cast<size_t>(per) * xstride;  // [T][H + 8]
+  float* gs = xs + static_cast<size_t>(T) * xstride;     // [H] norm gain (norm.on)
   // The batch's logits [T, E], gathered in CTA 0's copy of this array.
   __shared__ __align__(16) float cl_logits[kDecodeMaxRows * kMaxExperts];
   // Bulk copies (TMA engine, one thread issues them all): the CTA's router
@@ -150,11 +181,13 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
-    if (ne > 0) {
-      mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(ne) * H * 4);
+    const uint32_t rows_bytes = static_cast<uint32_t>(ne + (norm.on ? 1 : 0)) * H * 4;
+    if (rows_bytes > 0) {
+      mbar_arrive_expect_tx(&bars[0], rows_bytes);
       for (int i = 0; i < ne; ++i)
         bulk_g2s(ws + static_cast<size_t>(i) * xstride, router + static_cast<int64_t>(cta + kRouterCluster * i) * H,
                  static_cast<uint32_t>(H) * 4, &bars[0]);
+      if (norm.on) bulk_g2s(gs, norm.gain, static_cast<uint32_t>(H) * 4, &bars[0]);
     } else {
       mbar_arrive(&bars[0]);
     }
@@ -173,6 +206,7 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   __syncthreads();  // the barriers are initialised before anyone waits on them
   const bool ok = mbar_wait(&bars[0], 0) & mbar_wait(&bars[1], 0);
   if (!ok && tid == 0 && ro.err != nullptr) raise_error(ro.err, kDevWaitTimeout, 40, cta, 0);
+  if (norm.on) normalize_staged_rows(xs, T, H, xstride, gs, norm.eps);
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   // This thread's address of CTA 0's cl_logits.
   uint32_t cl0;
@@ -228,9 +262,13 @@ __global__ void __launch_bounds__(256) router_cluster_kernel(const float* __rest
   route_to_table(&r, ro.table, tid, blockDim.x);
 }
 
-size_t router_cluster_smem(int T, int H, int E) {
+size_t router_cluster_smem(int T, int H, int E, bool norm) {
   const size_t per = static_cast<size_t>((E + kRouterCluster - 1) / kRouterCluster);
-  return ((per + static_cast<size_t>(T)) * (H + 8)) * sizeof(float);
+  return ((per + static_cast<size_t>(T)) * (H + 8) + (norm ? H : 0)) * sizeof(float);
+}
+
+size_t router_fallback_smem(int T, int H, bool norm) {
+  return (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8) + (norm ? H : 0)) * sizeof(float);
 }
 
 // Standalone softmax/top-k over logits rows: one warp per row (the op-level
@@ -289,13 +327,13 @@ cudaError_t prepare_router_decode() {
 }
 
 cudaError_t launch_router_logits(const float* x, int T, int H, const float* router, const float* bias, int E,
-                                 float* logits, cudaStream_t stream, bool pdl, const RouteOut* route) {
+                                 float* logits, cudaStream_t stream, bool pdl, const RouteOut* route, RowNorm norm) {
   RouteOut ro = route != nullptr ? *route : RouteOut{nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr};
   int dev = 0;
   cudaError_t st = cudaGetDevice(&dev);
   if (st != cudaSuccess) return st;
   if ((st = prepare_router_decode()) != cudaSuccess) return st;
-  const size_t csmem = router_cluster_smem(T, H, E);
+  const size_t csmem = router_cluster_smem(T, H, E, norm.on != 0);
   if (route != nullptr && T <= kDecodeMaxRows && E <= kMaxExperts && dev < kMaxDevices &&
       csmem <= g_cluster_dyn_limit[dev]) {
     cudaLaunchConfig_t cfg{};
@@ -312,13 +350,17 @@ cudaError_t launch_router_logits(const float* x, int T, int H, const float* rout
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro};
+    void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro, &norm};
     return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(router_cluster_kernel), args);
   }
-  const size_t smem = (static_cast<size_t>(H) + static_cast<size_t>(T) * (H + 8)) * sizeof(float);
-  void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro};
+  const size_t smem = router_fallback_smem(T, H, norm.on != 0);
+  void* args[] = {&x, &T, &H, &router, &bias, &E, &logits, &ro, &norm};
   return launch_maybe_pdl(reinterpret_cast<const void*>(router_logits_kernel), dim3(E), dim3(256), smem, stream, args,
                           pdl);
+}
+
+size_t router_decode_smem(int T, int H, int E, bool norm) {
+  return router_fallback_smem(T, H, norm);
 }
 
 cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, int renorm, int64_t* ids,

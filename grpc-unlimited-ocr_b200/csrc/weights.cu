@@ -7,6 +7,7 @@
 // group is all zeros), q = clamp(nearbyint(w / scale), -127, 127). One block
 // per row; IEEE division and rintf give the host's bits.
 #include "moe_kernels.h"
+#include "rms_norm.cuh"
 
 namespace uocr_b200 {
 namespace {
@@ -99,6 +100,33 @@ __global__ void add_bias_kernel(float* y, const float* bias, int64_t rows, int64
     y[i] = __fadd_rn(y[i], bias[i % cols]);
 }
 
+__global__ void fill_f32_kernel(float* dst, float value, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = value;
+}
+
+// One block of eight warps per row: its inverse RMS (rms_inv_rows), then the
+// normalised row (H % 4 == 0).
+__global__ void __launch_bounds__(256) rms_norm_rows_kernel(const float* __restrict__ x, int64_t rows, int H,
+                                                            RowNorm norm, float* __restrict__ out) {
+  __shared__ double s_part[kNormWarps];
+  __shared__ float s_inv[1];
+  const int64_t r = blockIdx.x;
+  const float* row = x + r * H;
+  rms_inv_rows(1, H, norm.eps, [&](int, int q) { return __ldcg(reinterpret_cast<const float4*>(row) + q); }, s_part,
+               s_inv);
+  const float inv = s_inv[0];
+  const float4* src = reinterpret_cast<const float4*>(row);
+  const float4* g = reinterpret_cast<const float4*>(norm.gain);
+  float4* dst = reinterpret_cast<float4*>(out + r * H);
+  for (int q = threadIdx.x; q < H / 4; q += blockDim.x) {
+    const float4 v = __ldcg(src + q), w = __ldg(g + q);
+    dst[q] = make_float4(rms_apply(v.x, inv, w.x), rms_apply(v.y, inv, w.y), rms_apply(v.z, inv, w.z),
+                         rms_apply(v.w, inv, w.w));
+  }
+}
+
 unsigned grid_for(int64_t n) {
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
@@ -106,6 +134,18 @@ unsigned grid_for(int64_t n) {
 }
 
 }  // namespace
+
+cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  fill_f32_kernel<<<grid_for(n), 256, 0, stream>>>(dst, value, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm_rows(const float* x, int64_t rows, int H, RowNorm norm, float* out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  rms_norm_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, rows, H, norm, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;

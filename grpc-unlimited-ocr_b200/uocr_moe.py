@@ -23,6 +23,7 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
 PLAN_TENSOR_DECODE = 2
 PLAN_EP_STRIDED = 4
+PLAN_PRE_NORM = 8
 EP_HANDLE_BYTES = 256
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).
@@ -50,7 +51,8 @@ class MoeDesc(ctypes.Structure):
                 ("shared_ffn", ctypes.c_int64), ("layers", ctypes.c_int64), ("max_rows", ctypes.c_int64),
                 ("weight_format", ctypes.c_int32), ("renormalize", ctypes.c_int32),
                 ("router_bias", ctypes.c_int32), ("device", ctypes.c_int32), ("flags", ctypes.c_int32),
-                ("ep_world", ctypes.c_int32), ("ep_rank", ctypes.c_int32)]
+                ("ep_world", ctypes.c_int32), ("ep_rank", ctypes.c_int32), ("rms_norm_eps", ctypes.c_float),
+                ("reserved", ctypes.c_int32)]
 
 
 class EpHandle(ctypes.Structure):
@@ -61,7 +63,7 @@ class LayerSrc(ctypes.Structure):
     _fields_ = [("memory", ctypes.c_int32), ("dtype", ctypes.c_int32), ("router", ctypes.c_void_p),
                 ("router_bias", ctypes.c_void_p), ("gate", ctypes.c_void_p), ("up", ctypes.c_void_p),
                 ("down", ctypes.c_void_p), ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p),
-                ("shared_down", ctypes.c_void_p)]
+                ("shared_down", ctypes.c_void_p), ("norm", ctypes.c_void_p)]
 
 
 _lib = None
@@ -135,15 +137,19 @@ class Plan:
     """One MoE stack on one device (uocr_moe_plan)."""
 
     def __init__(self, dims: Dims, max_rows: int, weight_format: int = WEIGHT_BF16, renormalize: bool = True,
-                 router_bias: bool = False, device: int = 0, flags: int = 0, ep_world: int = 0, ep_rank: int = 0):
+                 router_bias: bool = False, device: int = 0, flags: int = 0, ep_world: int = 0, ep_rank: int = 0,
+                 rms_norm_eps: float = 1e-6):
         """ep_world > 1 makes this plan rank ep_rank of an expert-parallel
-        group (one process per GPU); connect it with ep_connect (see ep.py)."""
+        group (one process per GPU); connect it with ep_connect (see ep.py).
+        flags | PLAN_PRE_NORM puts the decoder's RMSNorm (epsilon
+        rms_norm_eps) in front of every layer."""
         self.dims = dims
         self.max_rows = max_rows
         self.weight_format = weight_format
         self.ep_world, self.ep_rank = ep_world, ep_rank
         desc = MoeDesc(dims.hidden, dims.experts, dims.top_k, dims.ffn, dims.shared_ffn, dims.layers, max_rows,
-                       weight_format, int(renormalize), int(router_bias), device, flags, ep_world, ep_rank)
+                       weight_format, int(renormalize), int(router_bias), device, flags, ep_world, ep_rank,
+                       rms_norm_eps, 0)
         h = ctypes.c_void_p()
         _check(lib().uocr_moe_plan_create(ctypes.byref(desc), ctypes.byref(h)))
         self.h = h
@@ -165,10 +171,11 @@ class Plan:
         return w.value, a.value
 
     def set_layer(self, layer: int, router, gate, up, down, shared_gate=None, shared_up=None, shared_down=None,
-                  router_bias=None, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_F32, stream=None):
-        """Arguments are torch tensors (device memory) or raw addresses."""
+                  router_bias=None, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_F32, stream=None, norm=None):
+        """Arguments are torch tensors (device memory) or raw addresses;
+        norm is the layer's RMSNorm gain (PLAN_PRE_NORM; None = ones)."""
         src = LayerSrc(memory, dtype, _ptr(router), _ptr(router_bias), _ptr(gate), _ptr(up), _ptr(down),
-                       _ptr(shared_gate), _ptr(shared_up), _ptr(shared_down))
+                       _ptr(shared_gate), _ptr(shared_up), _ptr(shared_down), _ptr(norm))
         _check(lib().uocr_moe_set_layer(self.h, layer, ctypes.byref(src), _stream(stream)))
 
     def forward(self, layer: int, x, y, ids=None, weights=None, stream=None, rows: int | None = None):

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define UOCR_MOE_ABI_VERSION 2
+#define UOCR_MOE_ABI_VERSION 3
 
 typedef enum uocr_status {
   UOCR_OK = 0,
@@ -69,6 +69,8 @@ typedef struct uocr_moe_desc {
   int32_t flags;             /* UOCR_PLAN_* bits */
   int32_t ep_world;          /* expert parallelism: ranks (GPUs) sharing the experts; 0 or 1 = none */
   int32_t ep_rank;           /* this plan's rank in [0, ep_world) */
+  float rms_norm_eps;        /* with UOCR_PLAN_PRE_NORM: the norm's epsilon (DecoderDims::rms_norm_eps) */
+  int32_t reserved;          /* 0 */
 } uocr_moe_desc;
 
 /* forward_stack replays a CUDA graph it captured on the first call for the
@@ -85,6 +87,14 @@ typedef struct uocr_moe_desc {
 /* Expert parallelism: expert e lives on rank e % ep_world instead of the
  * default contiguous ranges (rank e / (routed_experts / ep_world)). */
 #define UOCR_PLAN_EP_STRIDED 4
+/* Each layer's input passes the decoder's pre-feed-forward RMSNorm first
+ * (src/model/decoder.cpp:180-181, 200-201; ref::rms_norm,
+ * src/backend/reference/ops.cpp:129-141): forward computes
+ * y = MoE(RMSNorm(x)) and forward_stack h <- h + MoE(RMSNorm(h)) — the
+ * decoder's whole feed-forward block. The gain is each layer's src.norm.
+ * Decode batches normalise inside the router and gate/up kernels; the
+ * tensor-core decode flag is then ignored. */
+#define UOCR_PLAN_PRE_NORM 8
 
 int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** plan);
 int uocr_moe_plan_destroy(uocr_moe_plan* plan);
@@ -109,6 +119,7 @@ typedef struct uocr_moe_layer_src {
   const void* shared_gate;   /* [S, H] (ignored when S == 0) */
   const void* shared_up;     /* [S, H] */
   const void* shared_down;   /* [H, S] */
+  const float* norm;         /* [H] RMSNorm gain with UOCR_PLAN_PRE_NORM (NULL: all ones); ignored otherwise */
 } uocr_moe_layer_src;
 
 int uocr_moe_set_layer(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_src* src, void* stream);

@@ -80,6 +80,8 @@ def ref():
         _ref.ref_last_error.restype = ctypes.c_char_p
         _ref.ref_set_threads.argtypes = [ctypes.c_int]
         _ref.ref_get_threads.restype = ctypes.c_uint
+        _ref.ref_rms_norm.argtypes = [_f32p, _i64, _i64, _f32p, ctypes.c_float]
+        _ref.ref_rms_norm.restype = ctypes.c_int
     return _ref
 
 
@@ -186,6 +188,29 @@ def moe_forward(w: MoeWeights, x: np.ndarray, top_k: int, renormalize: bool, thr
     if rc != 0:
         raise ValueError("oracle_moe_forward: bad argument")
     return MoeResult(y, ids, wts, logits, margin, om)
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray | None, eps: float) -> np.ndarray:
+    """The decoder's pre-feed-forward RMSNorm, restated from
+    src/backend/reference/ops.cpp:129-141: per row, ss = the sum in index order
+    of double(v) * v (np.cumsum adds in order), inv = float(1 / sqrt(ss / H +
+    eps)) in double, then weight * (v * inv) in float. weight None = ones."""
+    x = _c(x)
+    H = x.shape[-1]
+    w = np.ones(H, np.float32) if weight is None else _c(weight)
+    v = x.astype(np.float64)
+    ss = np.cumsum(v * v, axis=-1)[..., -1]
+    inv = (1.0 / np.sqrt(ss / np.float64(H) + np.float64(np.float32(eps)))).astype(np.float32)
+    return (w * (x * inv[..., None]).astype(np.float32)).astype(np.float32)
+
+
+def ref_rms_norm(x: np.ndarray, weight: np.ndarray | None, eps: float) -> np.ndarray:
+    """The reference's own rms_norm (oracle/_ref)."""
+    out = np.array(_c(x), copy=True)
+    w = np.ones(out.shape[-1], np.float32) if weight is None else _c(weight)
+    if ref().ref_rms_norm(_p(out), out.shape[0], out.shape[1], _p(w), eps) != 0:
+        raise RuntimeError(ref().ref_last_error().decode())
+    return out
 
 
 class RefMoe:

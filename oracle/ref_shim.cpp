@@ -3,7 +3,8 @@
 // A C-ABI shim over the reference's own fp32 mixture-of-experts, compiled
 // together with the reference sources where they lie (see oracle/Makefile):
 //   src/model/feed_forward.cpp   MixtureOfExperts::forward (:36-78), GatedMlp (:18-24)
-//   src/backend/reference/ops.cpp linear/dot (:25-38, :91-109), softmax_rows (:169-187), silu (:163-167)
+//   src/backend/reference/ops.cpp linear/dot (:25-38, :91-109), softmax_rows (:169-187), silu (:163-167),
+//                                 rms_norm (:129-141, the decoder's pre-feed-forward norm)
 //   src/model/weight_source.cpp   TableWeights (:77-83)
 //   src/tensor/dtype.cpp
 // The shim only packs caller arrays into a TableWeights under the tensor names
@@ -20,6 +21,7 @@
 #include <string>
 #include <vector>
 
+#include "backend/reference/ops.h"
 #include "backend/reference/parallel.h"
 #include "model/feed_forward.h"
 #include "model/weight_source.h"
@@ -108,5 +110,18 @@ int ref_moe_run(void* handle, const float* x, std::int64_t tokens, float* y) {
 }
 
 void ref_moe_destroy(void* handle) { delete static_cast<RefMoe*>(handle); }
+
+// x [rows, cols] <- rms_norm(x, weight [cols], eps), in place. 0 on success.
+int ref_rms_norm(float* x, std::int64_t rows, std::int64_t cols, const float* weight, float eps) {
+  try {
+    uocr::Tensor t = copy_tensor({rows, cols}, x);
+    uocr::reference::rms_norm(t, copy_tensor({cols}, weight), eps);
+    std::memcpy(x, t.data(), static_cast<std::size_t>(t.numel()) * sizeof(float));
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
 
 }  // extern "C"

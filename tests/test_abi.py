@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = M.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.uocr_abi_version() == 2
+    assert lib.uocr_abi_version() == 3
 
 
 def _desc(**kw):

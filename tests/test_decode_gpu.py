@@ -196,6 +196,33 @@ def test_expert_topk_edge_rows(cuda, E, K, renorm):
         np.testing.assert_allclose(got_w[r], w, rtol=2e-6, atol=1e-30)
 
 
+@pytest.mark.parametrize("T,H,E,K,F,S,fmt", [(1, 64, 8, 3, 32, 32, 0), (5, 128, 16, 4, 48, 0, 1),
+                                              (16, 256, 64, 6, 64, 64, 0), (9, 2048, 16, 4, 256, 128, 1)])
+def test_pre_norm_against_oracle(cuda, T, H, E, K, F, S, fmt):
+    """PLAN_PRE_NORM: y = MoE(RMSNorm(x)) with a per-layer gain, the decoder's
+    feed-forward block (decoder.cpp:180-181) without its residual."""
+    import torch
+    rng = np.random.default_rng(T * 131 + H)
+    w = _tiny_layer(rng, H, E, F, S)
+    g = (1.0 + 0.3 * rng.standard_normal(H)).astype(np.float32)
+    x = (rng.standard_normal((T, H)) * 7.0).astype(np.float32)  # not unit scale: the norm matters
+    eps = 1e-5
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=16, weight_format=fmt, flags=M.PLAN_PRE_NORM, rms_norm_eps=eps)
+    keep = _upload(plan, w, torch, cuda)
+    gd = torch.from_numpy(g).to(cuda)
+    plan.set_layer(0, keep["router"], keep["gate"], keep["up"], keep["down"], keep["shared_gate"], keep["shared_up"],
+                   keep["shared_down"], norm=gd)
+    y, ids, _ = run_plan(plan, 0, torch.from_numpy(x).to(cuda), K, torch)
+    ww = w
+    if fmt == M.WEIGHT_INT8:
+        ww = O.MoeWeights(w.router, *[O.dequantize_q8(*O.quantize_q8(getattr(w, n))) for n in
+                                      ("gate", "up", "down", "shared_gate", "shared_up")],
+                          O.dequantize_q8(*O.quantize_q8(w.shared_down)) if S else w.shared_down)
+    want = O.moe_forward(ww, O.rms_norm(x, g, eps), K, renormalize=True)
+    check_ids(ids, want)
+    assert max_rel(y, want.y) <= (INT8_TOL if fmt else BF16_TOL)
+
+
 def test_router_bias(cuda):
     import torch
     rng = np.random.default_rng(3)
@@ -276,6 +303,42 @@ def test_stack_residual_two_layers(cuda, path):
     for t in layers:
         want = want + O.moe_forward(host_weights(t), want, cfg.top_k, renormalize=True).y
     assert max_rel(to_np(h), want) <= BF16_TOL
+
+
+def test_pre_norm_stack_two_layers_and_24_stay_finite(cuda):
+    """forward_stack with PLAN_PRE_NORM: h <- h + MoE(RMSNorm(h)) per layer
+    (unit gains). Two layers against the oracle; the full 24-layer config-1
+    stack keeps finite values and varied routing (the plain residual stack
+    of N(0, 0.02) SwiGLU layers grows quadratically and overflows)."""
+    import torch
+    cfg = C.CONFIGS[1]
+    layers = [C.device_layer(cfg, l) for l in range(2)]
+    plan = M.Plan(cfg.dims(layers=2), max_rows=8, flags=M.PLAN_PRE_NORM)
+    for l, t in enumerate(layers):
+        C.load_layer(plan, cfg, l, t)
+    x = C.device_input(cfg, 4)
+    h = x.clone()
+    plan.forward_stack(h)
+    plan.check()
+    want = to_np(x)
+    for t in layers:
+        want = want + O.moe_forward(host_weights(t), O.rms_norm(want, None, 1e-6), cfg.top_k, renormalize=True).y
+    assert max_rel(to_np(h), want) <= BF16_TOL
+    del plan, layers
+    plan = M.Plan(cfg.dims(), max_rows=8, flags=M.PLAN_PRE_NORM)
+    for l in range(cfg.layers):
+        C.load_layer(plan, cfg, l, C.device_layer(cfg, l))
+    h = C.device_input(cfg, 8)
+    y = torch.empty_like(h)
+    ids = torch.empty(8, cfg.top_k, dtype=torch.int32, device=cuda)
+    distinct = []
+    for l in range(cfg.layers):
+        plan.forward(l, h, y, ids)
+        h = h + y
+        distinct.append(len(set(ids.cpu().numpy().ravel().tolist())))
+    plan.check()
+    assert torch.isfinite(h).all()
+    assert min(distinct) >= 20  # eight rows with independent routing touch ~35 of 64 experts
 
 
 @pytest.mark.parametrize("path", ["layered", "tensor_cores"])

@@ -167,3 +167,28 @@ def test_synth_statistics_and_determinism():
     assert np.array_equal(tail, a[199000:])
     other = O.synth(9, 2, O.KIND_GATE, 6, 1000, 0.02)
     assert not np.array_equal(other, a[:1000])
+
+
+def test_rms_norm_known_answer():
+    # one row [3, 4]: ss = 25, mean 12.5, inv = 1/sqrt(12.5) in float
+    x = np.array([[3.0, 4.0]], np.float32)
+    inv = np.float32(1.0 / np.sqrt(12.5))
+    got = O.rms_norm(x, np.array([1.0, 2.0], np.float32), 0.0)
+    assert np.array_equal(got, np.array([[np.float32(3.0) * inv, np.float32(2.0) * (np.float32(4.0) * inv)]],
+                                        np.float32))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference sources not present (oracle/_ref not built)")
+@pytest.mark.parametrize("H", [64, 1280, 2048])
+def test_rms_norm_matches_reference(H):
+    """The restatement of ref::rms_norm (ops.cpp:129-141) against the reference's own, bit for bit."""
+    rng = np.random.default_rng(H)
+    x = (rng.standard_normal((40, H)) * rng.choice([1e-3, 1.0, 50.0], (40, 1))).astype(np.float32)
+    x[0] = 0.0  # an all-zero row: inv = 1 / sqrt(eps)
+    g = rng.standard_normal(H).astype(np.float32)
+    for gain in (None, g):
+        for eps in (1e-6, 1e-5):
+            a = O.rms_norm(x, gain, eps)
+            b = O.ref_rms_norm(x, gain, eps)
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+

@@ -160,6 +160,33 @@ def test_prefill_stack_residual(cuda):
     del keep
 
 
+def test_prefill_pre_norm_stack(cuda):
+    """PLAN_PRE_NORM on the prefill path (rows > 16): each layer's rows are
+    normalised into a copy first; h <- h + MoE(RMSNorm(h)) with per-layer gains."""
+    import torch
+    rng = np.random.default_rng(12)
+    H, E, K, F, S, T = 256, 16, 4, 128, 128, 40
+    layers = [_tiny_layer(rng, H, E, F, S) for _ in range(2)]
+    gains = [(1.0 + 0.2 * rng.standard_normal(H)).astype(np.float32) for _ in range(2)]
+    plan = M.Plan(M.Dims(H, E, K, F, S, layers=2), max_rows=T, flags=M.PLAN_PRE_NORM, rms_norm_eps=1e-5)
+    keep = []
+    for i, w in enumerate(layers):
+        k = _upload(plan, w, torch, cuda, layer=i)
+        k["norm"] = torch.from_numpy(gains[i]).to(cuda)
+        plan.set_layer(i, k["router"], k["gate"], k["up"], k["down"], k["shared_gate"], k["shared_up"],
+                       k["shared_down"], norm=k["norm"])
+        keep.append(k)
+    x = (rng.standard_normal((T, H)) * 3.0).astype(np.float32)
+    h = torch.from_numpy(x).to(cuda)
+    plan.forward_stack(h)
+    plan.check()
+    want = x
+    for w, g in zip(layers, gains):
+        want = want + O.moe_forward(w, O.rms_norm(want, g, 1e-5), K, renormalize=True).y
+    assert max_rel(to_np(h), want) <= BF16_TOL
+    del keep
+
+
 def test_prefill_unsupported_shapes_are_reported(cuda):
     import torch
     plan = M.Plan(M.Dims(64, 8, 2, 32, 32), max_rows=64)  # hidden 64: not a 256 multiple
