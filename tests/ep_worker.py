@@ -68,11 +68,38 @@ def main():
         ok = torch.equal(y, y1)
     else:
         ok = True
+    # Two layers with the residual (uocr_moe_forward_stack, captured as a CUDA
+    # graph) against the same stack on one GPU.
+    dims2 = cfg.dims(layers=2)
+    plan2 = M.Plan(dims2, max_rows=max(count, 1), router_bias=True, device=local,
+                   flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank)
+    single2 = M.Plan(dims2, max_rows=max(count, 17), router_bias=True, device=local)
+    t1 = C.device_layer(cfg, 1, device=dev)
+    for pl in (plan2, single2):
+        C.load_layer(pl, cfg, 0, t)
+        C.load_layer(pl, cfg, 1, t1)
+    ep.connect(plan2)
+    s = torch.cuda.Stream(device=dev)
+    h = x.clone()
+    h1 = x.clone()
+    with torch.cuda.stream(s):
+        for _ in range(2):  # capture, then a replay
+            h.copy_(x)
+            plan2.forward_stack(h, stream=s)
+        plan2.check(stream=s)
+        if count > 16:
+            single2.forward_stack(h1, stream=s)
+            single2.check(stream=s)
+            ok = ok and torch.equal(h, h1)
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.barrier()
+    torch.cuda.synchronize()
     plan.close()
     single.close()
+    dist.barrier()
+    plan2.close()
+    single2.close()
     dist.destroy_process_group()
     if rank == 0:
         print(f"EP world {world} strided {strided} rows {total}: {'EP_OK' if flag.item() == 0 else 'EP_MISMATCH'}")
