@@ -114,7 +114,11 @@ struct uocr_moe_plan {
   ErrorWord* err = nullptr;
   bool pre_norm = false;
   float* xnorm = nullptr;  // [max_rows, H] normalised rows for the prefill path (pre-norm plans)
-  // Prefill (rows above decode_rows): tcgen05 grouped GEMM path, bf16 weights.
+  // int8 plans on the prefill path: the layer's experts and shared expert
+  // expanded to bf16 (gate, up, down, shared gate, up, down) before the GEMMs.
+  __nv_bfloat16* wexp = nullptr;
+  // Prefill (rows above decode_rows): tcgen05 grouped GEMM path (bf16; int8
+  // layers are expanded to bf16 first, as the reference does for m > 1).
   bool prefill = false;
   PrefillDims pdims{};
   PrefillScratch pscratch{};
@@ -185,6 +189,9 @@ struct uocr_moe_plan {
     counter = c.take<unsigned>(1);
     err = c.take<ErrorWord>(1);
     if (pre_norm && (prefill || ep)) xnorm = c.take<float>(rows * static_cast<size_t>(d.hidden));
+    if (prefill && d.weight_format == UOCR_WEIGHT_INT8)
+      wexp = c.take<__nv_bfloat16>(3 * static_cast<size_t>(d.routed_experts) * F * d.hidden +
+                                   3 * S * static_cast<size_t>(d.hidden));
     if (prefill) {
       char* base = c.take<char>(prefill_scratch_bytes(pdims, !ep));
       carve_prefill_scratch(pdims, base, &pscratch, !ep);
@@ -307,11 +314,10 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
       return cuda_fail(pst, "plan_create: kernel set-up");
     }
   }
-  // Rows above the decode limit run the prefill path: bf16 weights and the
-  // tile multiples of the tensor-core grouped GEMM.
-  p->prefill = d.max_rows > dr && d.weight_format == UOCR_WEIGHT_BF16 &&
-               prefill_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
-                                 static_cast<int>(d.shared_ffn));
+  // Rows above the decode limit run the prefill path: the tile multiples of
+  // the tensor-core grouped GEMM (int8 weights are expanded to bf16 per layer).
+  p->prefill = d.max_rows > dr && prefill_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
+                                                    static_cast<int>(d.shared_ffn));
   p->pdims = PrefillDims{static_cast<int>(d.max_rows), static_cast<int>(d.hidden), static_cast<int>(d.routed_experts),
                          static_cast<int>(d.experts_per_token), static_cast<int>(d.expert_ffn),
                          static_cast<int>(d.shared_ffn), d.renormalize};
@@ -570,9 +576,34 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   if (rows > p->decode_rows) {
     if (!p->prefill)
       return fail(UOCR_ERR_UNSUPPORTED,
-                  "forward: more than 16 rows needs the prefill path: bf16 weights, hidden % 256 == 0, "
+                  "forward: more than 16 rows needs the prefill path: hidden % 256 == 0, "
                   "expert_ffn and shared_ffn % 128 == 0");
     PrefillCall c = prefill_call(p, L, x, rows, resid, y);
+    if (d.weight_format == UOCR_WEIGHT_INT8) {
+      // The reference's m > 1 int8 path: expand to bf16, then the bf16 GEMMs.
+      const int64_t EF = static_cast<int64_t>(E) * F, EH = static_cast<int64_t>(E) * H;
+      __nv_bfloat16* g = p->wexp;
+      __nv_bfloat16* u = g + EF * H;
+      __nv_bfloat16* dn = u + EF * H;
+      __nv_bfloat16* sg = dn + EH * F;
+      __nv_bfloat16* su = sg + static_cast<int64_t>(S) * H;
+      __nv_bfloat16* sd = su + static_cast<int64_t>(S) * H;
+      auto q8 = [](void* v) { return static_cast<const int8_t*>(v); };
+      UOCR_TRY(launch_dequant_rows(q8(L.gate), L.gate_s, EF, H, g, stream), "forward: int8 expansion");
+      UOCR_TRY(launch_dequant_rows(q8(L.up), L.up_s, EF, H, u, stream), "forward: int8 expansion");
+      UOCR_TRY(launch_dequant_rows(q8(L.down), L.down_s, EH, F, dn, stream), "forward: int8 expansion");
+      if (S > 0) {
+        UOCR_TRY(launch_dequant_rows(q8(L.sgate), L.sgate_s, S, H, sg, stream), "forward: int8 expansion");
+        UOCR_TRY(launch_dequant_rows(q8(L.sup), L.sup_s, S, H, su, stream), "forward: int8 expansion");
+        UOCR_TRY(launch_dequant_rows(q8(L.sdown), L.sdown_s, H, S, sd, stream), "forward: int8 expansion");
+      }
+      c.gate = g;
+      c.up = u;
+      c.down = dn;
+      c.sgate = sg;
+      c.sup = su;
+      c.sdown = sd;
+    }
     c.events = ev;
     UOCR_TRY(launch_prefill(c, stream), "forward: prefill");
     if (nev != nullptr) *nev = 6;

@@ -87,6 +87,11 @@ cudaError_t launch_quantize_rows(const void* w, bool bf16, int64_t rows, int64_t
 cudaError_t launch_synth(uint64_t seed, uint64_t stream_id, float sigma, int64_t offset, int64_t n, bool bf16,
                          void* out, cudaStream_t stream);
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t stream);
+// out [rows, cols] = bf16(float(q) * scale[row]) — the reference's expansion of
+// int8 weights before a bf16 GEMM (src/backend/cuda/gemv_ops.cu:185-190, 214-218),
+// here with one scale per row. cols % 16 == 0.
+cudaError_t launch_dequant_rows(const int8_t* q, const float* scale, int64_t rows, int64_t cols, __nv_bfloat16* out,
+                                cudaStream_t stream);
 // out [rows, H] = RMSNorm(x) with norm.gain / norm.eps (one warp per row).
 cudaError_t launch_rms_norm_rows(const float* x, int64_t rows, int H, RowNorm norm, float* out, cudaStream_t stream);
 

@@ -127,6 +127,32 @@ __global__ void __launch_bounds__(256) rms_norm_rows_kernel(const float* __restr
   }
 }
 
+// out = bf16(float(q) * scale[row]) over [rows, cols] int8 (cols % 16 == 0), 16 weights a thread.
+__global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale, int64_t rows,
+                                    int64_t cols, __nv_bfloat16* __restrict__ out) {
+  const int64_t n16 = rows * cols / 16;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float s = __ldg(scale + (i * 16) / cols);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(q) + i);
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float a = static_cast<float>(static_cast<int8_t>(words[w] & 0xffu)) * s;
+      const float b = static_cast<float>(static_cast<int8_t>((words[w] >> 8) & 0xffu)) * s;
+      const float c = static_cast<float>(static_cast<int8_t>((words[w] >> 16) & 0xffu)) * s;
+      const float d = static_cast<float>(static_cast<int8_t>(words[w] >> 24)) * s;
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+      o[2 * w] = *reinterpret_cast<const uint32_t*>(&lo);
+      o[2 * w + 1] = *reinterpret_cast<const uint32_t*>(&hi);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 unsigned grid_for(int64_t n) {
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
@@ -134,6 +160,14 @@ unsigned grid_for(int64_t n) {
 }
 
 }  // namespace
+
+cudaError_t launch_dequant_rows(const int8_t* q, const float* scale, int64_t rows, int64_t cols, __nv_bfloat16* out,
+                                cudaStream_t stream) {
+  const int64_t n16 = rows * cols / 16;
+  if (n16 <= 0) return cudaSuccess;
+  dequant_rows_kernel<<<grid_for(n16), 256, 0, stream>>>(q, scale, rows, cols, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_fill_f32(float* dst, float value, int64_t n, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;

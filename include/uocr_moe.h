@@ -128,7 +128,11 @@ int uocr_moe_set_layer(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_
  * (src/model/cuda/cuda_decoder.cpp:137-192) and MixtureOfExperts::forward
  * (src/model/feed_forward.cpp:36-78): fp32 router, softmax, top-k (lower id on
  * a tie), optional renormalisation, routed SwiGLU experts on bf16-rounded
- * inputs, shared expert, and the combine in expert-id order. ids [rows, k]
+ * inputs, shared expert, and the combine in expert-id order. Rows <= 16 stream
+ * the selected experts' weights (bf16 or int8); more rows run the tensor-core
+ * grouped GEMMs (hidden % 256, expert_ffn and shared_ffn % 128 == 0), with an
+ * int8 layer first expanded to bf16(q * scale) as the reference's linear_q8
+ * does for m > 1 (src/backend/cuda/gemv_ops.cu:214-218). ids [rows, k]
  * (int32, rank order) and weights [rows, k] are optional outputs (NULL to
  * skip). x, y, ids and weights are device pointers; x and y must not overlap;
  * x is 16-byte aligned (as every cudaMalloc block is). */

@@ -13,7 +13,7 @@ import moe_configs as C
 import oracle as O
 import uocr_moe as M
 from conftest import max_rel
-from test_decode_gpu import BF16_TOL, _tiny_layer, _upload, check_ids, host_weights, run_plan, to_np
+from test_decode_gpu import BF16_TOL, INT8_TOL, _tiny_layer, _upload, check_ids, host_weights, run_plan, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -185,6 +185,32 @@ def test_prefill_pre_norm_stack(cuda):
         want = want + O.moe_forward(w, O.rms_norm(want, g, 1e-5), K, renormalize=True).y
     assert max_rel(to_np(h), want) <= BF16_TOL
     del keep
+
+
+@pytest.mark.parametrize("T,H,E,K,F,S", [(40, 256, 16, 4, 128, 128), (300, 512, 64, 6, 256, 256),
+                                         (129, 256, 8, 2, 128, 0)])
+def test_prefill_int8(cuda, T, H, E, K, F, S):
+    """int8 plans on the prefill path: each layer's weights expanded to
+    bf16(q * scale) before the bf16 GEMMs (the reference's linear_q8 for m > 1,
+    gemv_ops.cu:214-218); per-output-channel scales."""
+    import torch
+    rng = np.random.default_rng(T * 3 + E)
+    w = _tiny_layer(rng, H, E, F, S)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=max(T, 32), weight_format=M.WEIGHT_INT8)
+    _upload(plan, w, torch, cuda)
+    y, ids, _ = run_plan(plan, 0, torch.from_numpy(x).to(cuda), K, torch)
+    deq = {n: O.dequantize_q8(*O.quantize_q8(getattr(w, n))) for n in ("gate", "up", "down")}
+    sh = {n: (O.dequantize_q8(*O.quantize_q8(getattr(w, n))) if S else getattr(w, n))
+          for n in ("shared_gate", "shared_up", "shared_down")}
+    ww = O.MoeWeights(w.router, deq["gate"], deq["up"], deq["down"], sh["shared_gate"], sh["shared_up"],
+                      sh["shared_down"])
+    want = O.moe_forward(ww, x, K, renormalize=True)
+    check_ids(ids, want)
+    assert max_rel(y, want.y) <= INT8_TOL
+    # the same rows through the decode path (rows <= 16, int8 streamed) agree within the int8 bar
+    y16, _, _ = run_plan(plan, 0, torch.from_numpy(x[:16]).to(cuda), K, torch)
+    assert max_rel(y16, y[:16]) <= INT8_TOL
 
 
 def test_prefill_unsupported_shapes_are_reported(cuda):
