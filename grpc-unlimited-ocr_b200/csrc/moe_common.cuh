@@ -139,12 +139,19 @@ __device__ __forceinline__ float dot8_bf16_bf16(const uint4& w, const uint4& a) 
   return s;
 }
 
-// Four int8 weights packed in a word, sign-extended to fp32.
+// Four int8 weights packed in a word, as fp32, exactly. Integer-to-float
+// conversions issue at a fraction of the fp32 rate, which an int8 weight
+// stream at HBM speed would exceed; instead each byte, offset to b + 128 by
+// flipping its sign bit, becomes the low mantissa byte of 2^23 (a byte
+// permute), and subtracting 2^23 + 128 leaves b exactly (both operands lie in
+// [2^23, 2^24), where every integer is a float).
 __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& a, float& b, float& c, float& d) {
-  a = static_cast<float>(static_cast<int8_t>(w & 0xffu));
-  b = static_cast<float>(static_cast<int8_t>((w >> 8) & 0xffu));
-  c = static_cast<float>(static_cast<int8_t>((w >> 16) & 0xffu));
-  d = static_cast<float>(static_cast<int8_t>(w >> 24));
+  const uint32_t u = w ^ 0x80808080u;
+  constexpr float kBias = 8388736.0f;  // 2^23 + 128
+  a = __uint_as_float(__byte_perm(u, 0x4b000000u, 0x7540u)) - kBias;
+  b = __uint_as_float(__byte_perm(u, 0x4b000000u, 0x7541u)) - kBias;
+  c = __uint_as_float(__byte_perm(u, 0x4b000000u, 0x7542u)) - kBias;
+  d = __uint_as_float(__byte_perm(u, 0x4b000000u, 0x7543u)) - kBias;
 }
 
 }  // namespace uocr_b200
