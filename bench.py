@@ -52,11 +52,12 @@ class ClockSampler:
         self.idx = device_index
         self.proc = None
         self.lines = []
+        self.mark_at = 0
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -66,6 +67,17 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first(self, timeout: float = 5.0):
+        """Blocks until the sampler has printed once (its start-up takes longer
+        than a short timed region), so that samples cover the region."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.01)
+
+    def mark(self):
+        """The timed region starts here: only later samples count."""
+        self.mark_at = len(self.lines)
 
     def stop(self):
         if self.proc is None:
@@ -77,7 +89,10 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        during = self.lines[self.mark_at:]
+        # a region shorter than one sampling period: the sample just before it
+        lines = during if during else self.lines[max(0, self.mark_at - 1):self.mark_at]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -90,7 +105,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "samples_in_region": len(during) > 0}
 
 
 def dist_setup():
@@ -394,11 +409,13 @@ def main():
         for _ in range(args.warmup):
             step()
         plan.check(stream=stream)
+        clocks = ClockSampler(local)
+        clocks.start()
+        clocks.wait_first()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        clocks = ClockSampler(local)
-        clocks.start()
+        clocks.mark()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
