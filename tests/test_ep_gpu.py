@@ -58,6 +58,41 @@ def test_local_group_equals_single_plan(cuda, n, strided, rows):
     del keep
 
 
+def test_local_group_pre_norm_equals_single_plan(cuda):
+    """PLAN_PRE_NORM under expert parallelism: each rank normalises its own rows
+    (the same summation order as a single plan), so the group's output is
+    still bitwise the single plan's."""
+    import torch
+    rng = np.random.default_rng(21)
+    H, E, K, F, S, n = 256, 16, 4, 128, 128, 2
+    w = _skewed(rng, H, E, F, S)
+    dims = M.Dims(H, E, K, F, S)
+    g = torch.from_numpy((1.0 + 0.3 * rng.standard_normal(H)).astype(np.float32)).to(cuda)
+    plans = [M.Plan(dims, max_rows=64, router_bias=True, flags=M.PLAN_PRE_NORM, rms_norm_eps=1e-5, ep_world=n,
+                    ep_rank=r) for r in range(n)]
+    single = M.Plan(dims, max_rows=128, router_bias=True, flags=M.PLAN_PRE_NORM, rms_norm_eps=1e-5)
+    keep = []
+    for p in plans + [single]:
+        k = _upload(p, w, torch, cuda)
+        p.set_layer(0, k["router"], k["gate"], k["up"], k["down"], k["shared_gate"], k["shared_up"],
+                    k["shared_down"], router_bias=k["router_bias"], norm=g)
+        keep.append(k)
+    M.ep_connect_local(plans)
+    x = torch.from_numpy((rng.standard_normal((90, H)) * 4.0).astype(np.float32)).to(cuda)
+    rows = [64, 26]
+    xs = [t.contiguous() for t in torch.split(x, rows)]
+    ys = [torch.empty_like(t) for t in xs]
+    M.ep_forward_local(plans, 0, xs, ys)
+    y = torch.empty_like(x)
+    single.forward(0, x, y)
+    for p in plans + [single]:
+        p.check()
+    assert torch.equal(torch.cat(ys), y)
+    want = O.moe_forward(w, O.rms_norm(to_np(x), to_np(g), 1e-5), K, renormalize=True)
+    assert max_rel(to_np(y), want.y) <= BF16_TOL
+    del keep
+
+
 def test_local_group_repeats_and_stacks(cuda):
     """Several layers and repeated calls reuse the exchange buffers safely."""
     import torch
