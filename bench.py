@@ -199,20 +199,25 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0, strided=False):
+def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0, strided=False,
+                int8=False):
     """one MoE layer over 32768 rows (8 pages x 4096),
     Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and the
     gate/up GEMM against the bf16 tensor roofline. With world > 1 the layer
     runs expert-parallel: each rank holds 64 / world experts and 32768 / world
     rows (strong scaling), and the time is the max over ranks. `rows` shrinks
     the batch (profiling captures only); `strided` assigns expert e to rank
-    e % world instead of contiguous ranges."""
+    e % world instead of contiguous ranges. `int8` (one GPU) quantises the
+    layer per output channel; the prefill path then expands it to bf16 per
+    layer before the GEMMs (the expansion is timed inside the router's
+    interval of kernel_ms)."""
     import torch
     cfg = C.CONFIGS[3]
     total = rows or cfg.rows[0]
     import ep
     start, T = ep.rows_of(total, world, rank)
     plan = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0,
+                  weight_format=M.WEIGHT_INT8 if int8 else M.WEIGHT_BF16,
                   ep_world=world if world > 1 else 0, ep_rank=rank, flags=M.PLAN_EP_STRIDED if strided else 0)
     t = C.device_layer(cfg, 0, device=dev)
     C.load_layer(plan, cfg, 0, t)
@@ -259,7 +264,8 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     peak, peak_src = measured_tensor_peak()
     out = {
         "workload": f"{cfg.name}: 1 layer, {total} rows" + (" (8 pages x 4096)" if total == 32768 else "")
-                    + ", Zipf(1.2)-biased router, bf16",
+                    + ", Zipf(1.2)-biased router, "
+                    + ("int8 per-channel weights expanded to bf16 per layer" if int8 else "bf16"),
         "value": total / (ms * 1e-3), "unit": "tokens/s", "ms_per_layer": ms, "n_gpus": world,
         "scaling": "strong" if world > 1 else None,
         "tflops_per_layer": total_flops / (ms * 1e-3) / 1e12,
@@ -484,7 +490,8 @@ def main():
         # Contiguous ranges (rank e // (E / G)) are measured beside it.
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
                               want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
-                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1)
+                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1,
+                              int8=fmt_int8 and world == 1)
         if world > 1:
             alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
                               rows=args.prefill_rows, world=world, rank=rank, strided=False)
