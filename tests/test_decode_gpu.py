@@ -223,6 +223,37 @@ def test_pre_norm_against_oracle(cuda, T, H, E, K, F, S, fmt):
     assert max_rel(y, want.y) <= (INT8_TOL if fmt else BF16_TOL)
 
 
+@pytest.mark.parametrize("T,fmt,flags", [(1, 0, M.PLAN_PRE_NORM), (8, 0, M.PLAN_PRE_NORM), (1, 1, M.PLAN_PRE_NORM),
+                                         (8, 0, M.PLAN_TENSOR_DECODE), (300, 0, M.PLAN_PRE_NORM),
+                                         (300, 1, M.PLAN_PRE_NORM)])
+def test_checkpoint_dims(cuda, T, fmt, flags):
+    """The checkpoint's own MoE shapes (src/weights/architecture.h:21-30:
+    hidden 1280, 64 experts, top-6, expert ffn 896, 2 shared experts = 1792)
+    with its own semantics (raw softmax weights, feed_forward.cpp:40), decode
+    and prefill row counts, bf16 and int8, behind the pre-feed-forward norm."""
+    import torch
+    H, E, K, F, S = 1280, 64, 6, 896, 1792
+    rng = np.random.default_rng(T + 7 * fmt + flags)
+    w = _tiny_layer(rng, H, E, F, S)
+    g = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    x = (rng.standard_normal((T, H)) * 2.0).astype(np.float32)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=max(T, 16), weight_format=fmt, renormalize=False, flags=flags)
+    keep = _upload(plan, w, torch, cuda)
+    pre = (flags & M.PLAN_PRE_NORM) != 0
+    if pre:
+        gd = torch.from_numpy(g).to(cuda)
+        plan.set_layer(0, keep["router"], keep["gate"], keep["up"], keep["down"], keep["shared_gate"],
+                       keep["shared_up"], keep["shared_down"], norm=gd)
+    y, ids, _ = run_plan(plan, 0, torch.from_numpy(x).to(cuda), K, torch)
+    ww = w
+    if fmt == M.WEIGHT_INT8:
+        ww = O.MoeWeights(w.router, *[O.dequantize_q8(*O.quantize_q8(getattr(w, n))) for n in
+                                      ("gate", "up", "down", "shared_gate", "shared_up", "shared_down")])
+    want = O.moe_forward(ww, O.rms_norm(x, g, 1e-6) if pre else x, K, renormalize=False)
+    check_ids(ids, want)
+    assert max_rel(y, want.y) <= (INT8_TOL if fmt else BF16_TOL)
+
+
 def test_router_bias(cuda):
     import torch
     rng = np.random.default_rng(3)
