@@ -1,14 +1,15 @@
 // Decode-path expert kernels (rows <= 16) on the CUDA cores: weight streaming
 // over only the experts the batch selected, plus the shared expert.
 //
-// One block per SM with 16 streaming warps and one routing warp. A streaming
-// warp owns one weight row (or the gate+up pair of one row) at a time and
-// issues every 128-bit load of it before using any, so an SM keeps ~16 rows
-// (about 128 KB) in flight; work is dealt grid-stride so all SMs stream. bf16
-// rows are 8 weights per load, int8 rows 16 weights per load with the
-// per-output-channel scale applied once to a row's sum. The routing warp
-// builds the routing table in shared memory from the router's logits while
-// the streaming warps work through the shared expert, which needs none.
+// One block per SM with 15 streaming warps and one routing warp. A streaming
+// warp works through a stream of weight rows (or gate+up row pairs) in steps
+// of four 16-byte loads per lane and matrix, the next steps' loads issued
+// before the current step's products, so an SM keeps ~90-120 KB in flight;
+// work is dealt grid-stride so all SMs stream. bf16 rows are 8 weights per
+// load, int8 rows 16 weights per load with the per-output-channel scale
+// applied once to a row's sum. The routing warp copies the routing table the
+// router built (or builds it from the logits) into shared memory while the
+// streaming warps work through the shared expert, which needs none.
 // Reference equivalents: expert_gate_up_kernel / expert_down_kernel
 // (src/backend/cuda/gemv_ops.cu:145-169) and the shared expert's gemv_kernel
 // calls (:133-141, src/model/cuda/cuda_decoder.cpp:119-125, 155-156).
