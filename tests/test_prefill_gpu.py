@@ -213,6 +213,26 @@ def test_prefill_int8(cuda, T, H, E, K, F, S):
     assert max_rel(y16, y[:16]) <= INT8_TOL
 
 
+def test_decode_and_prefill_paths_agree(cuda):
+    """The same rows through the streaming decode kernels (16 rows) and inside a
+    prefill batch (the tensor-core GEMMs): same ids, outputs within the bf16
+    bar — the MoE-level analogue of the reference's decode == prefill check
+    (tests/decoder_test.cpp:92-97)."""
+    import torch
+    rng = np.random.default_rng(17)
+    H, E, K, F, S = 512, 32, 4, 256, 256
+    w = _tiny_layer(rng, H, E, F, S)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=64)
+    _upload(plan, w, torch, cuda)
+    x = torch.from_numpy(rng.standard_normal((64, H)).astype(np.float32)).to(cuda)
+    y_pre, ids_pre, _ = run_plan(plan, 0, x, K, torch)
+    y_dec, ids_dec, _ = run_plan(plan, 0, x[:16].contiguous(), K, torch)
+    assert np.array_equal(ids_dec, ids_pre[:16])
+    assert max_rel(y_dec, y_pre[:16]) <= BF16_TOL
+    want = O.moe_forward(w, to_np(x[:16]), K, renormalize=True)
+    assert max_rel(y_dec, want.y) <= BF16_TOL
+
+
 def test_prefill_unsupported_shapes_are_reported(cuda):
     import torch
     plan = M.Plan(M.Dims(64, 8, 2, 32, 32), max_rows=64)  # hidden 64: not a 256 multiple
