@@ -28,6 +28,38 @@ def test_library_exports_every_declared_symbol():
     assert lib.uocr_abi_version() == 3
 
 
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors have the C layouts of the header's structs: a small C
+    program compiled against include/uocr_moe.h prints sizeof and offsetof."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "uocr_moe.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {}
+    for ln in out:
+        parts = ln.split()
+        if len(parts) == 3:
+            got[(parts[0], parts[1])] = int(parts[2])
+    for cname, cls in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for field, _ in cls._fields_:
+            assert got[(cname, field)] == getattr(cls, field).offset, (cname, field)
+    assert ctypes.sizeof(M.EpHandle) == 256
+
+
 def _desc(**kw):
     d = dict(hidden=64, routed_experts=8, experts_per_token=2, expert_ffn=32, shared_ffn=32, layers=1, max_rows=4,
              weight_format=0, renormalize=1, router_bias=0, device=0, flags=0)
