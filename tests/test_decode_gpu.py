@@ -101,7 +101,10 @@ def _upload(plan, w: O.MoeWeights, torch, cuda, layer=0):
     return keep
 
 
+# (16, 2048, 128, ...): the router rows and x rows exceed the cluster router's
+# shared memory, so the block-per-expert router with its last-block table build runs.
 SMALL_SHAPES = [
+    (16, 2048, 128, 8, 128, 128, True, 0),
     (1, 64, 8, 3, 32, 32, True, 0), (5, 128, 16, 1, 48, 0, True, 0), (16, 256, 128, 8, 64, 64, True, 0),
     (3, 96, 12, 4, 32, 48, False, 0), (16, 64, 2, 2, 16, 16, True, 0), (7, 128, 32, 6, 64, 128, True, 1),
     (16, 512, 64, 6, 256, 512, True, 1), (2, 1024, 16, 2, 1536, 2560, True, 0), (9, 2048, 16, 4, 2560, 128, True, 1)]
@@ -196,8 +199,12 @@ def test_expert_topk_edge_rows(cuda, E, K, renorm):
         np.testing.assert_allclose(got_w[r], w, rtol=2e-6, atol=1e-30)
 
 
+# (16, 2048, 128, ...) does not fit the 8-CTA cluster router's shared memory:
+# it runs the 128-block router (its last block builds the table), which then
+# normalises the rows it stages too.
 @pytest.mark.parametrize("T,H,E,K,F,S,fmt", [(1, 64, 8, 3, 32, 32, 0), (5, 128, 16, 4, 48, 0, 1),
-                                              (16, 256, 64, 6, 64, 64, 0), (9, 2048, 16, 4, 256, 128, 1)])
+                                              (16, 256, 64, 6, 64, 64, 0), (9, 2048, 16, 4, 256, 128, 1),
+                                              (16, 2048, 128, 8, 128, 128, 0)])
 def test_pre_norm_against_oracle(cuda, T, H, E, K, F, S, fmt):
     """PLAN_PRE_NORM: y = MoE(RMSNorm(x)) with a per-layer gain, the decoder's
     feed-forward block (decoder.cpp:180-181) without its residual."""
