@@ -373,6 +373,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return;
       }
+      if (Fm::kElemBytes == 2 && spr_f == 1) {
+        // (bf16) The expert's whole row is in this step: each of its batch
+        // rows is finished here (same sums in the same order as below), with
+        // a loop that is not unrolled over the row bound. (The int8 form of
+        // this loop spills registers.)
+        const int r = st - spr_s;
+        const int b0 = sroute.base[r], n0 = sroute.ntok[r];
+        const float sc = Fm::scale(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
+#pragma unroll 1
+        for (int j = 0; j < n0; ++j) {
+          const __nv_bfloat16* ar = actr + static_cast<int64_t>(b0 + j) * F;
+          float a = 0.0f;
+#pragma unroll
+          for (int q = 0; q < kStep; ++q)
+            if (lane + 32 * q < nch_f) a += Fm::template dot_act<2>(w[q], ar + (lane + 32 * q) * Fm::kPerChunk);
+          const float v = warp_sum(a) * sc;
+          if (lane == 0) {
+            const int t = sroute.slot_tok[b0 + j];
+            sum[t] = __fadd_rn(sum[t], __fmul_rn(sroute.slot_w[b0 + j], v));
+          }
+        }
+        return;
+      }
       const int r = (st - spr_s) / spr_f, sr = (st - spr_s) % spr_f;
       const int b0 = sroute.base[r], n0 = sroute.ntok[r];
       const int base = sr * 32 * kStep + lane;
