@@ -507,6 +507,91 @@ int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src
 
 namespace {
 
+// fp32 [n] from an fp32 or bf16 source on the host or the device; bf16 is
+// widened exactly on the device.
+int copy_widen(int32_t memory, int32_t dtype, const void* from, float* dst, size_t n, cudaStream_t stream,
+               const char* name) {
+  if (from == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, std::string("set_layer_parts: missing ") + name);
+  const cudaMemcpyKind kind = memory == UOCR_MEMORY_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+  if (dtype == UOCR_DTYPE_F32) {
+    UOCR_TRY(cudaMemcpyAsync(dst, from, n * 4, kind, stream), "set_layer_parts: fp32 copy");
+    return UOCR_OK;
+  }
+  const void* dev = from;
+  void* staging = nullptr;
+  if (memory == UOCR_MEMORY_HOST) {
+    UOCR_TRY(cudaMallocAsync(&staging, n * 2, stream), "set_layer_parts: staging allocation");
+    const cudaError_t st = cudaMemcpyAsync(staging, from, n * 2, kind, stream);
+    if (st != cudaSuccess) {
+      cudaFreeAsync(staging, stream);
+      return cuda_fail(st, "set_layer_parts: upload");
+    }
+    dev = staging;
+  }
+  const cudaError_t st = launch_bf16_to_f32(static_cast<const __nv_bfloat16*>(dev), dst, static_cast<int64_t>(n), stream);
+  if (staging != nullptr) cudaFreeAsync(staging, stream);
+  if (st != cudaSuccess) return cuda_fail(st, "set_layer_parts: widening");
+  return UOCR_OK;
+}
+
+}  // namespace
+
+int uocr_moe_set_layer_parts(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_parts* src, void* stream_v) {
+  if (p == nullptr || src == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: null argument");
+  if (layer < 0 || layer >= p->d.layers)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: layer out of range");
+  if (src->memory != UOCR_MEMORY_HOST && src->memory != UOCR_MEMORY_DEVICE)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: memory must be host (0) or device (1)");
+  if (src->dtype != UOCR_DTYPE_F32 && src->dtype != UOCR_DTYPE_BF16)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: dtype must be f32 (0) or bf16 (1)");
+  if (p->d.router_bias && src->router_bias == nullptr)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: the plan expects a router bias");
+  const int64_t H = p->d.hidden, E = p->d.routed_experts, F = p->d.expert_ffn, S = p->d.shared_ffn;
+  if (E > 0 && (src->gate == nullptr || src->up == nullptr || src->down == nullptr))
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "set_layer_parts: gate, up and down must each list the experts");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  LayerDev& L = p->layers[static_cast<size_t>(layer)];
+  uocr_moe_layer_src ms{};  // the memory and dtype upload_matrix reads
+  ms.memory = src->memory;
+  ms.dtype = src->dtype;
+  int rc = copy_widen(src->memory, src->dtype, src->router, L.router, static_cast<size_t>(E * H), stream, "router");
+  if (rc == UOCR_OK && p->d.router_bias)
+    rc = copy_widen(src->memory, src->dtype, src->router_bias, L.bias, static_cast<size_t>(E), stream, "router_bias");
+  if (rc == UOCR_OK && p->pre_norm) {
+    if (src->norm != nullptr)
+      rc = copy_widen(src->memory, src->dtype, src->norm, L.norm, static_cast<size_t>(H), stream, "norm");
+    else
+      UOCR_TRY(launch_fill_f32(L.norm, 1.0f, H, stream), "set_layer_parts: unit norm gain");
+  }
+  // Held expert i is expert e of the checkpoint (i == e without expert
+  // parallelism); its rows go to row block i of the stacks.
+  const size_t eb = p->elem_bytes();
+  for (int64_t i = 0; i < p->held_experts() && rc == UOCR_OK; ++i) {
+    const int64_t e = p->ep ? p->emap.global(p->emap.rank, static_cast<int>(i)) : i;
+    char* g = static_cast<char*>(L.gate) + static_cast<size_t>(i * F * H) * eb;
+    char* u = static_cast<char*>(L.up) + static_cast<size_t>(i * F * H) * eb;
+    char* dn = static_cast<char*>(L.down) + static_cast<size_t>(i * H * F) * eb;
+    float* gs = L.gate_s != nullptr ? L.gate_s + i * F : nullptr;
+    float* us = L.up_s != nullptr ? L.up_s + i * F : nullptr;
+    float* ds = L.down_s != nullptr ? L.down_s + i * H : nullptr;
+    rc = upload_matrix(p, ms, src->gate[e], F, H, g, gs, stream, "gate");
+    if (rc == UOCR_OK) rc = upload_matrix(p, ms, src->up[e], F, H, u, us, stream, "up");
+    if (rc == UOCR_OK) rc = upload_matrix(p, ms, src->down[e], H, F, dn, ds, stream, "down");
+  }
+  if (rc == UOCR_OK && S > 0) {
+    rc = upload_matrix(p, ms, src->shared_gate, S, H, L.sgate, L.sgate_s, stream, "shared_gate");
+    if (rc == UOCR_OK) rc = upload_matrix(p, ms, src->shared_up, S, H, L.sup, L.sup_s, stream, "shared_up");
+    if (rc == UOCR_OK) rc = upload_matrix(p, ms, src->shared_down, H, S, L.sdown, L.sdown_s, stream, "shared_down");
+  }
+  if (rc == UOCR_OK && src->memory == UOCR_MEMORY_HOST)
+    UOCR_TRY(cudaStreamSynchronize(stream), "set_layer_parts: host copies");
+  if (rc == UOCR_OK) L.loaded = true;
+  return rc;
+}
+
+namespace {
+
 constexpr int kMaxProfileKernels = 6;
 
 const __nv_bfloat16* as_bf16(void* v) { return static_cast<const __nv_bfloat16*>(v); }

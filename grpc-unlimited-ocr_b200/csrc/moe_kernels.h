@@ -80,6 +80,7 @@ cudaError_t launch_decode_experts_q8(const float* x, int T, int H, int F, int S,
 
 // ---- weights and synthetic inputs (weights.cu) ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n, cudaStream_t stream);
 // y[r, c] += bias[c]
 cudaError_t launch_add_bias(float* y, const float* bias, int64_t rows, int64_t cols, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const void* w, bool bf16, int64_t rows, int64_t cols, int64_t group, int8_t* q,

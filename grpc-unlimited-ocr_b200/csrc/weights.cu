@@ -18,6 +18,15 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16*
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
+// bf16 -> fp32 is exact (the bf16 bits are the float's upper half), the
+// widening the reference's CheckpointWeights applies to every tensor
+// (src/model/weight_source.cpp:21).
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float* __restrict__ dst, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = __bfloat162float(src[i]);
+}
+
 template <typename T>
 __device__ __forceinline__ float load_f(const T* p, int64_t i);
 template <>
@@ -184,6 +193,12 @@ cudaError_t launch_rms_norm_rows(const float* x, int64_t rows, int H, RowNorm no
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   f32_to_bf16_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  bf16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
   return cudaGetLastError();
 }
 

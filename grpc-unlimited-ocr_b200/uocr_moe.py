@@ -32,7 +32,7 @@ KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KI
 # Every symbol include/uocr_moe.h declares.
 EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
-    "uocr_moe_set_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
+    "uocr_moe_set_layer", "uocr_moe_set_layer_parts", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_moe_ep_handle", "uocr_moe_ep_connect", "uocr_moe_ep_connect_local", "uocr_moe_ep_forward_local",
     "uocr_expert_topk",
     "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
@@ -66,6 +66,14 @@ class LayerSrc(ctypes.Structure):
                 ("shared_down", ctypes.c_void_p), ("norm", ctypes.c_void_p)]
 
 
+class LayerParts(ctypes.Structure):
+    _fields_ = [("memory", ctypes.c_int32), ("dtype", ctypes.c_int32), ("router", ctypes.c_void_p),
+                ("router_bias", ctypes.c_void_p), ("gate", ctypes.POINTER(ctypes.c_void_p)),
+                ("up", ctypes.POINTER(ctypes.c_void_p)), ("down", ctypes.POINTER(ctypes.c_void_p)),
+                ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p), ("shared_down", ctypes.c_void_p),
+                ("norm", ctypes.c_void_p)]
+
+
 _lib = None
 
 
@@ -81,6 +89,7 @@ def lib() -> ctypes.CDLL:
         L.uocr_moe_plan_destroy.argtypes = [vp]
         L.uocr_moe_plan_bytes.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.uocr_moe_set_layer.argtypes = [vp, i64, ctypes.POINTER(LayerSrc), vp]
+        L.uocr_moe_set_layer_parts.argtypes = [vp, i64, ctypes.POINTER(LayerParts), vp]
         L.uocr_moe_forward.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp]
         L.uocr_moe_forward_stack.argtypes = [vp, vp, i64, vp]
         L.uocr_moe_check.argtypes = [vp, vp]
@@ -150,6 +159,7 @@ class Plan:
         desc = MoeDesc(dims.hidden, dims.experts, dims.top_k, dims.ffn, dims.shared_ffn, dims.layers, max_rows,
                        weight_format, int(renormalize), int(router_bias), device, flags, ep_world, ep_rank,
                        rms_norm_eps, 0)
+        self.desc = desc
         h = ctypes.c_void_p()
         _check(lib().uocr_moe_plan_create(ctypes.byref(desc), ctypes.byref(h)))
         self.h = h
@@ -177,6 +187,22 @@ class Plan:
         src = LayerSrc(memory, dtype, _ptr(router), _ptr(router_bias), _ptr(gate), _ptr(up), _ptr(down),
                        _ptr(shared_gate), _ptr(shared_up), _ptr(shared_down), _ptr(norm))
         _check(lib().uocr_moe_set_layer(self.h, layer, ctypes.byref(src), _stream(stream)))
+
+    def set_layer_parts(self, layer: int, router, gate, up, down, shared_gate=None, shared_up=None,
+                        shared_down=None, router_bias=None, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_BF16,
+                        stream=None, norm=None):
+        """One tensor (or raw address) per expert in gate/up/down, as a
+        checkpoint holds them; None entries are allowed for experts another
+        expert-parallel rank holds."""
+        def arr(items):
+            return (ctypes.c_void_p * len(items))(*[_ptr(t) for t in items]) if items is not None else None
+        g, u, d = arr(gate), arr(up), arr(down)
+        src = LayerParts(memory, dtype, _ptr(router), _ptr(router_bias),
+                         ctypes.cast(g, ctypes.POINTER(ctypes.c_void_p)) if g is not None else None,
+                         ctypes.cast(u, ctypes.POINTER(ctypes.c_void_p)) if u is not None else None,
+                         ctypes.cast(d, ctypes.POINTER(ctypes.c_void_p)) if d is not None else None,
+                         _ptr(shared_gate), _ptr(shared_up), _ptr(shared_down), _ptr(norm))
+        _check(lib().uocr_moe_set_layer_parts(self.h, layer, ctypes.byref(src), _stream(stream)))
 
     def forward(self, layer: int, x, y, ids=None, weights=None, stream=None, rows: int | None = None):
         rows = x.shape[0] if rows is None else rows

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define UOCR_MOE_ABI_VERSION 3
+#define UOCR_MOE_ABI_VERSION 4
 
 typedef enum uocr_status {
   UOCR_OK = 0,
@@ -126,6 +126,37 @@ typedef struct uocr_moe_layer_src {
 } uocr_moe_layer_src;
 
 int uocr_moe_set_layer(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_src* src, void* stream);
+
+/* The same layer as a checkpoint holds it: one tensor per routed expert and
+ * projection, each behind its own pointer (a view into a memory-mapped
+ * safetensors shard, say), all in `dtype` — bf16 in the published checkpoint,
+ * whose names are model.layers.{l}.mlp.experts.{e}.{gate,up,down}_proj.weight,
+ * mlp.shared_experts.*, mlp.gate.weight (the router) and
+ * post_attention_layernorm.weight (the pre-norm gain),
+ * src/weights/architecture.cpp:108-117. Expert e's rows land at rows e*F
+ * (gate/up) and e*H (down) of the plan's stacks; the router, bias and gain are
+ * widened to fp32 exactly, as CheckpointWeights does
+ * (src/model/weight_source.cpp:21), and the matrices are converted as
+ * uocr_moe_set_layer converts them. Replaces CudaDecoder's stack_experts and
+ * expert() (src/model/cuda/cuda_decoder.cpp:44-46, 67-69, 75-84) over
+ * stacked_weight (src/model/cuda/device_weight.cpp:63-72), without first
+ * stacking the experts on the host. In an expert-parallel plan only this
+ * rank's experts are read (the others may be NULL). */
+typedef struct uocr_moe_layer_parts {
+  int32_t memory;                 /* uocr_memory of every pointer below */
+  int32_t dtype;                  /* uocr_dtype of every tensor below */
+  const void* router;             /* [E, H] */
+  const void* router_bias;        /* [E], required iff desc.router_bias */
+  const void* const* gate;        /* E pointers, each [F, H] */
+  const void* const* up;          /* E pointers, each [F, H] */
+  const void* const* down;        /* E pointers, each [H, F] */
+  const void* shared_gate;        /* [S, H] (ignored when S == 0) */
+  const void* shared_up;          /* [S, H] */
+  const void* shared_down;        /* [H, S] */
+  const void* norm;               /* [H] gain with UOCR_PLAN_PRE_NORM (NULL: all ones); ignored otherwise */
+} uocr_moe_layer_parts;
+
+int uocr_moe_set_layer_parts(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_parts* parts, void* stream);
 
 /* y [rows, H] = MoE_layer(x [rows, H]) — the work of CudaDecoder::moe
  * (src/model/cuda/cuda_decoder.cpp:137-192) and MixtureOfExperts::forward

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = M.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.uocr_abi_version() == 3
+    assert lib.uocr_abi_version() == 4
 
 
 def test_struct_layouts_match_the_header(tmp_path):
@@ -36,7 +36,7 @@ def test_struct_layouts_match_the_header(tmp_path):
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no C compiler")
-    structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc}
+    structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc, "uocr_moe_layer_parts": M.LayerParts}
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "uocr_moe.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')

@@ -1,0 +1,181 @@
+"""Checkpoint readers on the CPU: one safetensors shard, the shard index, and
+the MoE tensor table of a layer. The failure cases are the reference's
+(tests/safetensors_test.cpp): each malformed header, file and index is
+rejected with the tensor or file named."""
+import json
+import struct
+
+import numpy as np
+import pytest
+
+import checkpoint as C
+
+
+def _raw_shard(path, header: dict | str, data: bytes, hlen: int | None = None):
+    h = header if isinstance(header, str) else json.dumps(header)
+    hb = h.encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hb) if hlen is None else hlen))
+        f.write(hb)
+        f.write(data)
+
+
+def test_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((3, 5)).astype(np.float32)
+    b = rng.integers(0, 1 << 16, size=(4, 2), dtype=np.uint16)
+    c = np.arange(7, dtype=np.uint8)
+    p = tmp_path / "one.safetensors"
+    C.write_safetensors(p, {"a": ("F32", a), "b": ("BF16", b), "c": ("U8", c)}, metadata={"format": "pt"})
+    f = C.SafetensorsFile(p)
+    assert sorted(f.tensors) == ["a", "b", "c"]
+    assert f.find("a").dtype == "F32" and f.find("a").shape == (3, 5)
+    np.testing.assert_array_equal(f.array("a"), a)
+    np.testing.assert_array_equal(f.array("b"), b)
+    np.testing.assert_array_equal(f.array("c"), c)
+    assert f.find("absent") is None
+    assert not f.array("a").flags.writeable  # a view into the read-only map
+
+
+def test_zero_sized_tensor(tmp_path):
+    p = tmp_path / "z.safetensors"
+    C.write_safetensors(p, {"e": ("F32", np.zeros((0, 4), np.float32)), "x": ("I32", np.arange(3, dtype=np.int32))})
+    f = C.SafetensorsFile(p)
+    assert f.array("e").shape == (0, 4)
+    np.testing.assert_array_equal(f.array("x"), [0, 1, 2])
+
+
+@pytest.mark.parametrize("header,size,why", [
+    ("[]", 0, "not a JSON object"),
+    ("{not json", 0, "not a JSON object"),
+    ('{"a":{"dtype":"F64","shape":[1],"data_offsets":[0,8]}}', 8, "unsupported dtype"),
+    ('{"a":{"dtype":"F32","shape":[-1],"data_offsets":[0,4]}}', 4, "negative dim"),
+    ('{"a":{"dtype":"F32","shape":[1.5],"data_offsets":[0,4]}}', 4, "non-integer"),
+    ('{"a":{"dtype":"F32","shape":[2],"data_offsets":[0,4]}}', 4, "bytes stored"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0,4]}}', 8, "data section is 8 bytes"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[4,8]}}', 8, "previous tensor ends at 0"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0,4]}}', 2, "outside a 2-byte"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0,4]},"b":{"dtype":"F32","shape":[1],"data_offsets":[2,6]}}',
+     6, "previous tensor ends at 4"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[8,4]}}', 8, "outside"),
+    ('{"a":{"dtype":"F32","shape":[1]}}', 4, "lacks dtype, shape or data_offsets"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0]}}', 4, "two unsigned integers"),
+    ('{"a":{"dtype":"U8","shape":[4294967296,4294967296,16],"data_offsets":[0,0]}}', 0, "overflows"),
+    ('{"a":{"dtype":"F32","shape":3,"data_offsets":[0,4]}}', 4, "not an array"),
+])
+def test_header_rejections(header, size, why):
+    with pytest.raises(C.CheckpointError, match=why):
+        C.parse_header(header, size)
+
+
+def test_metadata_is_skipped():
+    t = C.parse_header('{"__metadata__":{"k":"v"},"a":{"dtype":"I64","shape":[2],"data_offsets":[0,16]}}', 16)
+    assert list(t) == ["a"] and t["a"].element_count() == 2
+
+
+def test_file_rejections(tmp_path):
+    short = tmp_path / "short.safetensors"
+    short.write_bytes(b"\x01\x02\x03")
+    with pytest.raises(C.CheckpointError, match="too short"):
+        C.SafetensorsFile(short)
+    huge = tmp_path / "huge.safetensors"
+    _raw_shard(huge, "{}", b"", hlen=1 << 40)
+    with pytest.raises(C.CheckpointError, match="does not fit the file"):
+        C.SafetensorsFile(huge)
+    with pytest.raises(C.CheckpointError, match="cannot open"):
+        C.SafetensorsFile(tmp_path / "absent.safetensors")
+    bad = tmp_path / "bad.safetensors"
+    _raw_shard(bad, '{"a":{"dtype":"F32","shape":[2],"data_offsets":[0,4]}}', b"\0" * 4)
+    with pytest.raises(C.CheckpointError, match="bad.safetensors: tensor a"):
+        C.SafetensorsFile(bad)
+
+
+def _two_shards(d):
+    C.write_safetensors(d / "s1.safetensors", {"x": ("F32", np.ones(2, np.float32)), "y": ("U8", np.arange(3, dtype=np.uint8))})
+    C.write_safetensors(d / "s2.safetensors", {"z": ("I32", np.arange(4, dtype=np.int32))})
+
+
+def test_sharded_weights(tmp_path):
+    _two_shards(tmp_path)
+    C.write_index(tmp_path / "good.json", {"x": "s1.safetensors", "y": "s1.safetensors", "z": "s2.safetensors"})
+    w = C.ShardedWeights.open(tmp_path / "good.json")
+    assert w.tensor_count() == 3 and w.names() == ["x", "y", "z"]
+    np.testing.assert_array_equal(w.array("z"), [0, 1, 2, 3])
+    assert w.find("q") is None
+    with pytest.raises(KeyError, match="no tensor named q"):
+        w.at("q")
+
+
+@pytest.mark.parametrize("wmap,why", [
+    ({"x": "s2.safetensors", "y": "s1.safetensors", "z": "s2.safetensors"}, "holds x, which the index places in s2"),
+    ({"y": "s1.safetensors", "z": "s2.safetensors"}, "holds x, which the index does not list"),
+    ({"x": "s1.safetensors", "y": "s1.safetensors", "z": "s2.safetensors", "w": "s2.safetensors"},
+     "places w here but the shard lacks it"),
+    ({"x": "../s1.safetensors", "y": "s1.safetensors", "z": "s2.safetensors"}, "not a plain file name"),
+    ({"x": "..", "y": "s1.safetensors", "z": "s2.safetensors"}, "not a plain file name"),
+    ({"x": 3, "y": "s1.safetensors", "z": "s2.safetensors"}, "is not a file name"),
+    ({"x": "s1.safetensors", "y": "s1.safetensors", "z": "absent.safetensors"}, "cannot open"),
+])
+def test_index_rejections(tmp_path, wmap, why):
+    _two_shards(tmp_path)
+    C.write_index(tmp_path / "idx.json", wmap)
+    with pytest.raises(C.CheckpointError, match=why):
+        C.ShardedWeights.open(tmp_path / "idx.json")
+
+
+def test_index_file_rejections(tmp_path):
+    with pytest.raises(C.CheckpointError, match="cannot open the shard index"):
+        C.ShardedWeights.open(tmp_path / "absent.json")
+    (tmp_path / "bad.json").write_text('{"metadata": {}}')
+    with pytest.raises(C.CheckpointError, match="no weight_map object"):
+        C.ShardedWeights.open(tmp_path / "bad.json")
+
+
+def write_moe_checkpoint(d, layers, H, E, F, S, seed=0, shards=2, dtype="BF16", drop=None, reshape=None):
+    """A synthetic checkpoint of `layers` MoE layers under the published
+    names, spread over `shards` shards; returns (index path, name -> array)."""
+    rng = np.random.default_rng(seed)
+    arrays = {}
+    for l in layers:
+        for name, shape in C.moe_layer_tensors(l, H, E, F, S).items():
+            sigma = 1.0 if name.endswith("layernorm.weight") else 0.05
+            v = (rng.standard_normal(shape) * sigma + (1.0 if name.endswith("layernorm.weight") else 0.0))
+            v = v.astype(np.float32)
+            if dtype == "BF16":
+                u = v.view(np.uint32)
+                v = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+            arrays[name] = v
+    if drop is not None:
+        arrays.pop(drop)
+    if reshape is not None:
+        arrays[reshape] = arrays[reshape].reshape(-1)
+    names = sorted(arrays)
+    wmap = {}
+    for s in range(shards):
+        part = {n: (dtype, arrays[n]) for i, n in enumerate(names) if i % shards == s}
+        fn = f"model-{s + 1:05d}-of-{shards:05d}.safetensors"
+        C.write_safetensors(d / fn, part)
+        wmap.update({n: fn for n in part})
+    C.write_index(d / "model.safetensors.index.json", wmap)
+    return d / "model.safetensors.index.json", arrays
+
+
+def test_moe_layer_table(tmp_path):
+    idx, arrays = write_moe_checkpoint(tmp_path, [1, 2], H=64, E=4, F=32, S=64)
+    w = C.ShardedWeights.open(idx)
+    assert C.check_moe_layer(w, 1, 64, 4, 32, 64) == []
+    assert C.check_moe_layer(w, 2, 64, 4, 32, 64) == []
+    probs = C.check_moe_layer(w, 0, 64, 4, 32, 64)
+    assert len(probs) == 3 + 4 * 3 + 2 and all(p.startswith("missing model.layers.0.") for p in probs)
+    assert C.check_moe_layer(w, 1, 64, 4, 16, 64) != []  # wrong ffn width
+    name = "model.layers.1.mlp.experts.3.down_proj.weight"
+    np.testing.assert_array_equal(w.array(name), arrays[name])
+    assert w.at(name).shape == (64, 32)
+
+
+def test_moe_layer_table_names_each_problem(tmp_path):
+    gone = "model.layers.1.mlp.experts.2.up_proj.weight"
+    flat = "model.layers.1.mlp.shared_experts.down_proj.weight"
+    idx, _ = write_moe_checkpoint(tmp_path, [1], H=64, E=4, F=32, S=64, drop=gone, reshape=flat)
+    probs = C.check_moe_layer(C.ShardedWeights.open(idx), 1, 64, 4, 32, 64)
+    assert probs == [f"missing {gone}", f"{flat}: shape [4096], expected [64, 64]"]
