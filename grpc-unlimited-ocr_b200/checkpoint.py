@@ -65,8 +65,8 @@ class TensorInfo:
         return n
 
 
-def _is_uint(v) -> bool:
-    return isinstance(v, int) and not isinstance(v, bool) and v >= 0
+def _is_uint(v, bits: int = 64) -> bool:
+    return isinstance(v, int) and not isinstance(v, bool) and 0 <= v < (1 << bits)
 
 
 def parse_header(header_json, data_size: int) -> dict:
@@ -79,7 +79,7 @@ def parse_header(header_json, data_size: int) -> dict:
     if not isinstance(header, dict):
         raise CheckpointError("header is not a JSON object")
     tensors = {}
-    for name, entry in header.items():
+    for name, entry in sorted(header.items()):  # key order, as the reference's JSON object iterates
         if name == "__metadata__":
             continue
         if not isinstance(entry, dict) or not all(k in entry for k in ("dtype", "shape", "data_offsets")):
@@ -90,7 +90,7 @@ def parse_header(header_json, data_size: int) -> dict:
         shape = entry["shape"]
         if not isinstance(shape, list):
             raise CheckpointError(f"tensor {name}: shape is not an array")
-        if not all(_is_uint(d) for d in shape):
+        if not all(_is_uint(d, 63) for d in shape):
             raise CheckpointError(f"tensor {name}: shape holds a non-integer or negative dim")
         offsets = entry["data_offsets"]
         if not isinstance(offsets, list) or len(offsets) != 2 or not all(_is_uint(v) for v in offsets):
@@ -178,7 +178,7 @@ class ShardedWeights:
         w = cls()
         expected, by_file = {}, {}
         base = os.path.dirname(index_path)
-        for name, file in index["weight_map"].items():
+        for name, file in sorted(index["weight_map"].items()):
             if not isinstance(file, str):
                 raise CheckpointError(f"{index_path}: weight_map[{name}] is not a file name")
             if "/" in file or file == ".." or not file:
@@ -189,7 +189,7 @@ class ShardedWeights:
                 w.shards.append(by_file[file])
         for file in sorted(by_file):
             shard = by_file[file]
-            for name in shard.tensors:
+            for name in sorted(shard.tensors):
                 if name not in expected:
                     raise CheckpointError(f"{file}: holds {name}, which the index does not list")
                 if expected[name] != file:

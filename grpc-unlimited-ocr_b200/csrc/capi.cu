@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/uocr_moe.h"
+#include "checkpoint.h"
 #include "decode_tc.h"
 #include "ep.h"
 #include "moe_kernels.h"
@@ -588,6 +589,62 @@ int uocr_moe_set_layer_parts(uocr_moe_plan* p, int64_t layer, const uocr_moe_lay
     UOCR_TRY(cudaStreamSynchronize(stream), "set_layer_parts: host copies");
   if (rc == UOCR_OK) L.loaded = true;
   return rc;
+}
+
+int uocr_moe_load_layer(uocr_moe_plan* p, const uocr_checkpoint* ckpt, int64_t layer, int64_t plan_layer,
+                        void* stream) {
+  if (p == nullptr || ckpt == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "load_layer: null argument");
+  if (layer < 0) return fail(UOCR_ERR_INVALID_ARGUMENT, "load_layer: layer out of range");
+  if (p->d.router_bias)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "load_layer: the plan expects a router bias, which the checkpoint does not hold");
+  const int64_t H = p->d.hidden, E = p->d.routed_experts, F = p->d.expert_ffn, S = p->d.shared_ffn;
+  const std::string pre = "model.layers." + std::to_string(layer) + ".";
+  int dtype = -1;
+  // The tensor's data if it is present with this shape and the layer's one dtype.
+  auto get = [&](const std::string& name, std::vector<int64_t> shape, const void** out) -> int {
+    const CkTensor* t = checkpoint_find(ckpt, name);
+    if (t == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "load_layer: missing " + name);
+    if (t->dtype != UOCR_DTYPE_BF16 && t->dtype != UOCR_DTYPE_F32)
+      return fail(UOCR_ERR_INVALID_ARGUMENT,
+                  "load_layer: " + name + ": dtype " + dtype_name(t->dtype) + ", expected BF16 or F32");
+    if (dtype >= 0 && t->dtype != dtype)
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "load_layer: layer " + std::to_string(layer) + ": mixed dtypes");
+    dtype = t->dtype;
+    if (t->shape != shape) {
+      auto text = [](const std::vector<int64_t>& v) {
+        std::string s = "[";
+        for (size_t k = 0; k < v.size(); ++k) s += (k ? ", " : "") + std::to_string(v[k]);
+        return s + "]";
+      };
+      return fail(UOCR_ERR_INVALID_ARGUMENT,
+                  "load_layer: " + name + ": shape " + text(t->shape) + ", expected " + text(shape));
+    }
+    *out = t->data;
+    return UOCR_OK;
+  };
+  uocr_moe_layer_parts parts{};
+  parts.memory = UOCR_MEMORY_HOST;
+  std::vector<const void*> g(static_cast<size_t>(E)), u(static_cast<size_t>(E)), dn(static_cast<size_t>(E));
+  int rc = get(pre + "mlp.gate.weight", {E, H}, &parts.router);
+  if (rc == UOCR_OK) rc = get(pre + "post_attention_layernorm.weight", {H}, &parts.norm);
+  for (int64_t e = 0; e < E && rc == UOCR_OK; ++e) {
+    const std::string q = pre + "mlp.experts." + std::to_string(e) + ".";
+    rc = get(q + "gate_proj.weight", {F, H}, &g[static_cast<size_t>(e)]);
+    if (rc == UOCR_OK) rc = get(q + "up_proj.weight", {F, H}, &u[static_cast<size_t>(e)]);
+    if (rc == UOCR_OK) rc = get(q + "down_proj.weight", {H, F}, &dn[static_cast<size_t>(e)]);
+  }
+  if (rc == UOCR_OK && S > 0) {
+    const std::string q = pre + "mlp.shared_experts.";
+    rc = get(q + "gate_proj.weight", {S, H}, &parts.shared_gate);
+    if (rc == UOCR_OK) rc = get(q + "up_proj.weight", {S, H}, &parts.shared_up);
+    if (rc == UOCR_OK) rc = get(q + "down_proj.weight", {H, S}, &parts.shared_down);
+  }
+  if (rc != UOCR_OK) return rc;
+  parts.dtype = dtype;
+  parts.gate = g.data();
+  parts.up = u.data();
+  parts.down = dn.data();
+  return uocr_moe_set_layer_parts(p, plan_layer, &parts, stream);
 }
 
 namespace {

@@ -32,7 +32,8 @@ KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KI
 # Every symbol include/uocr_moe.h declares.
 EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
-    "uocr_moe_set_layer", "uocr_moe_set_layer_parts", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
+    "uocr_moe_set_layer", "uocr_moe_set_layer_parts", "uocr_checkpoint_open", "uocr_checkpoint_close",
+    "uocr_checkpoint_count", "uocr_checkpoint_tensor", "uocr_moe_load_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_moe_ep_handle", "uocr_moe_ep_connect", "uocr_moe_ep_connect_local", "uocr_moe_ep_forward_local",
     "uocr_expert_topk",
     "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
@@ -74,6 +75,14 @@ class LayerParts(ctypes.Structure):
                 ("norm", ctypes.c_void_p)]
 
 
+MAX_TENSOR_RANK = 8
+
+
+class TensorView(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("rank", ctypes.c_int32), ("shape", ctypes.c_int64 * MAX_TENSOR_RANK),
+                ("data", ctypes.c_void_p), ("bytes", ctypes.c_int64)]
+
+
 _lib = None
 
 
@@ -90,6 +99,11 @@ def lib() -> ctypes.CDLL:
         L.uocr_moe_plan_bytes.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.uocr_moe_set_layer.argtypes = [vp, i64, ctypes.POINTER(LayerSrc), vp]
         L.uocr_moe_set_layer_parts.argtypes = [vp, i64, ctypes.POINTER(LayerParts), vp]
+        L.uocr_checkpoint_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
+        L.uocr_checkpoint_close.argtypes = [vp]
+        L.uocr_checkpoint_count.argtypes = [vp, ctypes.POINTER(i64)]
+        L.uocr_checkpoint_tensor.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(TensorView)]
+        L.uocr_moe_load_layer.argtypes = [vp, vp, i64, i64, vp]
         L.uocr_moe_forward.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp]
         L.uocr_moe_forward_stack.argtypes = [vp, vp, i64, vp]
         L.uocr_moe_check.argtypes = [vp, vp]
@@ -244,6 +258,44 @@ class Plan:
                 raise ValueError("an EP handle is 256 bytes")
             ctypes.memmove(arr[i].bytes, b, EP_HANDLE_BYTES)
         _check(lib().uocr_moe_ep_connect(self.h, arr))
+
+
+DTYPE_NAMES = {0: "F32", 1: "BF16", 2: "F16", 3: "I64", 4: "I32", 5: "U8"}
+
+
+class Checkpoint:
+    """A checkpoint opened by the library's own reader (uocr_checkpoint_*):
+    a shard index or one .safetensors file, memory-mapped read-only."""
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib().uocr_checkpoint_open(os.fsencode(path), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().uocr_checkpoint_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self):
+        n = ctypes.c_int64()
+        _check(lib().uocr_checkpoint_count(self.h, ctypes.byref(n)))
+        return n.value
+
+    def tensor(self, name: str):
+        """(dtype name, shape, address, bytes) of a tensor in the mapping."""
+        v = TensorView()
+        _check(lib().uocr_checkpoint_tensor(self.h, name.encode(), ctypes.byref(v)))
+        return DTYPE_NAMES[v.dtype], tuple(v.shape[:v.rank]), v.data, v.bytes
+
+    def load_layer(self, plan: "Plan", layer: int, plan_layer: int, stream=None):
+        _check(lib().uocr_moe_load_layer(plan.h, self.h, layer, plan_layer, _stream(stream)))
 
 
 def ep_connect_local(plans: list[Plan]):

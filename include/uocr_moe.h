@@ -41,7 +41,15 @@ typedef enum uocr_status {
  * symmetric per-output-channel (one fp32 scale per weight row). */
 typedef enum uocr_weight_format { UOCR_WEIGHT_BF16 = 0, UOCR_WEIGHT_INT8 = 1 } uocr_weight_format;
 typedef enum uocr_memory { UOCR_MEMORY_HOST = 0, UOCR_MEMORY_DEVICE = 1 } uocr_memory;
-typedef enum uocr_dtype { UOCR_DTYPE_F32 = 0, UOCR_DTYPE_BF16 = 1 } uocr_dtype;
+typedef enum uocr_dtype {
+  UOCR_DTYPE_F32 = 0,
+  UOCR_DTYPE_BF16 = 1,
+  /* further dtypes a checkpoint may hold (src/tensor/dtype.cpp:15-22) */
+  UOCR_DTYPE_F16 = 2,
+  UOCR_DTYPE_I64 = 3,
+  UOCR_DTYPE_I32 = 4,
+  UOCR_DTYPE_U8 = 5
+} uocr_dtype;
 
 /* Message of the last failed call on this thread ("" when none). */
 const char* uocr_last_error(void);
@@ -157,6 +165,39 @@ typedef struct uocr_moe_layer_parts {
 } uocr_moe_layer_parts;
 
 int uocr_moe_set_layer_parts(uocr_moe_plan* plan, int64_t layer, const uocr_moe_layer_parts* parts, void* stream);
+
+/* ---- Checkpoints: safetensors shards, memory-mapped read-only ------------
+ * uocr_checkpoint_open takes a shard index (model.safetensors.index.json) or
+ * one .safetensors file and checks what the reference's readers check:
+ * SafetensorsFile (src/weights/safetensors.cpp:69-163: header length, JSON
+ * object, dtype, dims, offsets, sizes, extents tiling the data section
+ * exactly) and ShardedWeights::open (src/weights/sharded_weights.cpp:12-61:
+ * plain shard file names, every indexed tensor in the shard the index names,
+ * no unlisted tensor). Failures return UOCR_ERR_INVALID_ARGUMENT with the
+ * file and the first problem in uocr_last_error(). Host only: no GPU needed. */
+typedef struct uocr_checkpoint uocr_checkpoint;
+
+#define UOCR_MAX_TENSOR_RANK 8
+typedef struct uocr_tensor_view {
+  int32_t dtype;                         /* uocr_dtype */
+  int32_t rank;
+  int64_t shape[UOCR_MAX_TENSOR_RANK];
+  const void* data;                      /* into the mapping; valid until uocr_checkpoint_close */
+  int64_t bytes;
+} uocr_tensor_view;
+
+int uocr_checkpoint_open(const char* path, uocr_checkpoint** out);
+int uocr_checkpoint_close(uocr_checkpoint* ckpt);
+int uocr_checkpoint_count(const uocr_checkpoint* ckpt, int64_t* tensors);
+/* UOCR_ERR_INVALID_ARGUMENT ("no tensor named ...") when absent. */
+int uocr_checkpoint_tensor(const uocr_checkpoint* ckpt, const char* name, uocr_tensor_view* out);
+
+/* Checkpoint layer `layer`'s MoE tensors (the names above; all BF16 or all
+ * F32) into plan layer `plan_layer` through uocr_moe_set_layer_parts. A
+ * missing tensor, a shape other than the plan's or mixed dtypes fail with
+ * UOCR_ERR_INVALID_ARGUMENT naming the tensor, before anything is copied. */
+int uocr_moe_load_layer(uocr_moe_plan* plan, const uocr_checkpoint* ckpt, int64_t layer, int64_t plan_layer,
+                        void* stream);
 
 /* y [rows, H] = MoE_layer(x [rows, H]) — the work of CudaDecoder::moe
  * (src/model/cuda/cuda_decoder.cpp:137-192) and MixtureOfExperts::forward

@@ -36,7 +36,8 @@ def test_struct_layouts_match_the_header(tmp_path):
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no C compiler")
-    structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc, "uocr_moe_layer_parts": M.LayerParts}
+    structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc, "uocr_moe_layer_parts": M.LayerParts,
+               "uocr_tensor_view": M.TensorView}
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "uocr_moe.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')

@@ -45,7 +45,7 @@ def test_zero_sized_tensor(tmp_path):
     np.testing.assert_array_equal(f.array("x"), [0, 1, 2])
 
 
-@pytest.mark.parametrize("header,size,why", [
+HEADER_CASES = [
     ("[]", 0, "not a JSON object"),
     ("{not json", 0, "not a JSON object"),
     ('{"a":{"dtype":"F64","shape":[1],"data_offsets":[0,8]}}', 8, "unsupported dtype"),
@@ -62,7 +62,14 @@ def test_zero_sized_tensor(tmp_path):
     ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0]}}', 4, "two unsigned integers"),
     ('{"a":{"dtype":"U8","shape":[4294967296,4294967296,16],"data_offsets":[0,0]}}', 0, "overflows"),
     ('{"a":{"dtype":"F32","shape":3,"data_offsets":[0,4]}}', 4, "not an array"),
-])
+    ('{"a":{"dtype":"F32","shape":[9223372036854775808],"data_offsets":[0,4]}}', 4, "non-integer or negative dim"),
+    ('{"a":{"dtype":"F32","shape":[1],"data_offsets":[0,18446744073709551616]}}', 4, "two unsigned integers"),
+    ('{"b":{"dtype":"F32","shape":[1],"data_offsets":[0,4]},"a":{"dtype":"F64","shape":[1],"data_offsets":[4,12]}}',
+     12, "tensor a: unsupported"),  # entries are checked in name order
+]
+
+
+@pytest.mark.parametrize("header,size,why", HEADER_CASES)
 def test_header_rejections(header, size, why):
     with pytest.raises(C.CheckpointError, match=why):
         C.parse_header(header, size)
@@ -106,7 +113,7 @@ def test_sharded_weights(tmp_path):
         w.at("q")
 
 
-@pytest.mark.parametrize("wmap,why", [
+INDEX_CASES = [
     ({"x": "s2.safetensors", "y": "s1.safetensors", "z": "s2.safetensors"}, "holds x, which the index places in s2"),
     ({"y": "s1.safetensors", "z": "s2.safetensors"}, "holds x, which the index does not list"),
     ({"x": "s1.safetensors", "y": "s1.safetensors", "z": "s2.safetensors", "w": "s2.safetensors"},
@@ -115,7 +122,10 @@ def test_sharded_weights(tmp_path):
     ({"x": "..", "y": "s1.safetensors", "z": "s2.safetensors"}, "not a plain file name"),
     ({"x": 3, "y": "s1.safetensors", "z": "s2.safetensors"}, "is not a file name"),
     ({"x": "s1.safetensors", "y": "s1.safetensors", "z": "absent.safetensors"}, "cannot open"),
-])
+]
+
+
+@pytest.mark.parametrize("wmap,why", INDEX_CASES)
 def test_index_rejections(tmp_path, wmap, why):
     _two_shards(tmp_path)
     C.write_index(tmp_path / "idx.json", wmap)
@@ -179,3 +189,93 @@ def test_moe_layer_table_names_each_problem(tmp_path):
     idx, _ = write_moe_checkpoint(tmp_path, [1], H=64, E=4, F=32, S=64, drop=gone, reshape=flat)
     probs = C.check_moe_layer(C.ShardedWeights.open(idx), 1, 64, 4, 32, 64)
     assert probs == [f"missing {gone}", f"{flat}: shape [4096], expected [64, 64]"]
+
+
+# ---- the library's own reader (uocr_checkpoint_*, host only) --------------
+
+def _native(path):
+    import uocr_moe as M
+    return M.Checkpoint(path)
+
+
+def test_native_reader_matches(tmp_path):
+    import ctypes
+    idx, arrays = write_moe_checkpoint(tmp_path, [1, 3], H=64, E=4, F=32, S=64, shards=3)
+    ck = _native(idx)
+    py = C.ShardedWeights.open(idx)
+    assert len(ck) == py.tensor_count() == len(arrays)
+    for name, arr in arrays.items():
+        dtype, shape, addr, nbytes = ck.tensor(name)
+        assert (dtype, shape) == ("BF16", arr.shape)
+        assert nbytes == arr.nbytes and ctypes.string_at(addr, nbytes) == arr.tobytes()
+    one = tmp_path / "one.safetensors"
+    C.write_safetensors(one, {"a": ("F32", np.arange(6, dtype=np.float32).reshape(2, 3)), "b": ("I64", np.arange(2))})
+    ck1 = _native(one)
+    assert len(ck1) == 2
+    dtype, shape, addr, nbytes = ck1.tensor("a")
+    assert (dtype, shape, nbytes) == ("F32", (2, 3), 24)
+    assert np.frombuffer(ctypes.string_at(addr, nbytes), np.float32).tolist() == [0, 1, 2, 3, 4, 5]
+    import uocr_moe as M
+    with pytest.raises(M.UocrError, match="no tensor named q"):
+        ck1.tensor("q")
+    ck.close()
+    ck1.close()
+
+
+@pytest.mark.parametrize("header,size,why", HEADER_CASES)
+def test_native_header_rejections(tmp_path, header, size, why):
+    import uocr_moe as M
+    p = tmp_path / "h.safetensors"
+    _raw_shard(p, header, b"\0" * size)
+    with pytest.raises(M.UocrError, match=why) as e:
+        _native(p)
+    assert e.value.code == 1 and "h.safetensors: " in str(e.value)
+
+
+def test_native_file_rejections(tmp_path):
+    import uocr_moe as M
+    short = tmp_path / "short.safetensors"
+    short.write_bytes(b"\x01\x02\x03")
+    huge = tmp_path / "huge.safetensors"
+    _raw_shard(huge, "{}", b"", hlen=1 << 40)
+    for path, why in ((short, "too short"), (huge, "does not fit the file"),
+                      (tmp_path / "absent.safetensors", "cannot open")):
+        with pytest.raises(M.UocrError, match=why):
+            _native(path)
+    with pytest.raises(M.UocrError, match="cannot open the shard index"):
+        _native(tmp_path / "absent.json")
+    (tmp_path / "bad.json").write_text('{"metadata": {}}')
+    with pytest.raises(M.UocrError, match="no weight_map object"):
+        _native(tmp_path / "bad.json")
+
+
+@pytest.mark.parametrize("wmap,why", INDEX_CASES)
+def test_native_index_rejections(tmp_path, wmap, why):
+    import uocr_moe as M
+    _two_shards(tmp_path)
+    C.write_index(tmp_path / "idx.json", wmap)
+    with pytest.raises(M.UocrError, match=why):
+        _native(tmp_path / "idx.json")
+
+
+def test_native_json_strictness(tmp_path):
+    """What a strict JSON reader must refuse (trailing commas, bare words,
+    unterminated strings, bad escapes, content after the value) and accept
+    (escapes, surrogate pairs, nesting in the metadata)."""
+    import uocr_moe as M
+    for bad in ('{"a":1,}', "{a:1}", '{"a":"x}', '{"a":"\\q"}', '{} {}', '{"a":[1,2]', '{"a":01}',
+                '{"a":"\\ud800"}', '{"a":tru}'):
+        with pytest.raises(M.UocrError, match="header is not a JSON object"):
+            _native_header(tmp_path, bad, 0)
+    ok = ('{"__metadata__":{"k":["v",{"n":null,"t":true,"f":-1.5e3}]},'
+          '"\\u00e9\\ud83d\\ude00\\n":{"dtype":"U8","shape":[2],"data_offsets":[0,2]}}')
+    ck = _native_header(tmp_path, ok, 2)
+    assert ck.tensor("\u00e9\U0001F600\n")[1] == (2,)
+    py = C.parse_header(ok, 2)
+    assert list(py) == ["\u00e9\U0001F600\n"]
+
+
+def _native_header(tmp_path, header, size):
+    p = tmp_path / "j.safetensors"
+    _raw_shard(p, header, b"\0" * size)
+    return _native(p)

@@ -136,3 +136,54 @@ def test_checkpoint_load_into_expert_parallel_ranks(cuda, tmp_path, strided):
     single.forward(0, x, y)
     single.check()
     assert torch.equal(torch.cat(ys), y)
+
+
+@pytest.mark.parametrize("fmt,ckpt_dtype", [(M.WEIGHT_BF16, "BF16"), (M.WEIGHT_INT8, "BF16"), (M.WEIGHT_BF16, "F32")])
+def test_native_loader_matches_python_loader(cuda, tmp_path, fmt, ckpt_dtype):
+    """uocr_moe_load_layer (the library's own reader and packing) loads what
+    checkpoint.load_moe_layer loads, bit for bit."""
+    import torch
+    idx, _ = write_moe_checkpoint(tmp_path, LAYERS, H, E, F, S, seed=13, dtype=ckpt_dtype, shards=3)
+    dims = M.Dims(H, E, K, F, S, layers=len(LAYERS))
+    a = M.Plan(dims, max_rows=64, weight_format=fmt, flags=M.PLAN_PRE_NORM)
+    b = M.Plan(dims, max_rows=64, weight_format=fmt, flags=M.PLAN_PRE_NORM)
+    ck = M.Checkpoint(idx)
+    w = C.ShardedWeights.open(idx)
+    for i, l in enumerate(LAYERS):
+        ck.load_layer(a, l, i)
+        C.load_moe_layer(b, w, l, plan_layer=i)
+    rng = np.random.default_rng(6)
+    for T in (1, 8, 33):
+        x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(cuda)
+        ha, hb = x.clone(), x.clone()
+        a.forward_stack(ha)
+        b.forward_stack(hb)
+        a.check()
+        b.check()
+        assert torch.equal(ha.view(torch.int32), hb.view(torch.int32)), T
+    ck.close()
+    a.close()
+    b.close()
+
+
+def test_native_loader_rejects_a_bad_layer(cuda, tmp_path):
+    gone = "model.layers.1.mlp.experts.2.gate_proj.weight"
+    flat = "model.layers.1.mlp.shared_experts.up_proj.weight"
+    idx, _ = write_moe_checkpoint(tmp_path, [1], H, E, F, S, drop=gone)
+    plan = M.Plan(M.Dims(H, E, K, F, S), max_rows=16)
+    ck = M.Checkpoint(idx)
+    with pytest.raises(M.UocrError, match=f"load_layer: missing {gone}"):
+        ck.load_layer(plan, 1, 0)
+    with pytest.raises(M.UocrError, match="load_layer: missing model.layers.4.mlp.gate.weight"):
+        ck.load_layer(plan, 4, 0)
+    d2 = tmp_path / "flat"
+    d2.mkdir()
+    idx2, _ = write_moe_checkpoint(d2, [1], H, E, F, S, reshape=flat)
+    with pytest.raises(M.UocrError, match=f"{flat}: shape \\[65536\\], expected \\[256, 256\\]"):
+        M.Checkpoint(idx2).load_layer(plan, 1, 0)
+    biased = M.Plan(M.Dims(H, E, K, F, S), max_rows=16, router_bias=True)
+    with pytest.raises(M.UocrError, match="router bias"):
+        M.Checkpoint(idx2).load_layer(biased, 1, 0)
+    ck.close()
+    plan.close()
+    biased.close()
