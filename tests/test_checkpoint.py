@@ -279,3 +279,46 @@ def _native_header(tmp_path, header, size):
     p = tmp_path / "j.safetensors"
     _raw_shard(p, header, b"\0" * size)
     return _native(p)
+
+
+def test_native_and_python_readers_agree_on_mutated_headers(tmp_path):
+    """Random single-byte mutations of a valid shard: the library's reader and
+    the Python reader accept exactly the same files, and name the same first
+    problem when both reject (both restate the reference's checks and order)."""
+    import uocr_moe as M
+    good = tmp_path / "g.safetensors"
+    C.write_safetensors(good, {"b.w": ("BF16", np.arange(6, dtype=np.uint16).reshape(2, 3)),
+                               "a.w": ("F32", np.ones((2, 2), np.float32)), "c": ("U8", np.arange(5, dtype=np.uint8))},
+                        metadata={"format": "pt"})
+    raw = bytearray(good.read_bytes())
+    hlen = int.from_bytes(raw[:8], "little")
+    rng = np.random.default_rng(1)
+    alphabet = b'0123456789[]{},:"-.eE ABFIU'
+    agree = accepted = 0
+    for trial in range(400):
+        b = bytearray(raw)
+        pos = 8 + int(rng.integers(0, hlen))
+        b[pos] = alphabet[int(rng.integers(0, len(alphabet)))]
+        p = tmp_path / f"m{trial % 4}.safetensors"
+        p.write_bytes(bytes(b))
+        try:
+            C.SafetensorsFile(p)
+            py = None
+        except C.CheckpointError as e:
+            py = str(e)
+        try:
+            M.Checkpoint(p).close()
+            nat = None
+        except M.UocrError as e:
+            nat = str(e).split(": ", 1)[1]  # drop the status name
+        if py is None or nat is None:
+            assert py is None and nat is None, (bytes(b[8:8 + hlen]), py, nat)
+            accepted += py is None
+        else:
+            # Python's json module accepts a few texts a strict reader refuses
+            # (NaN, lone surrogates); everything else names the same problem.
+            if "header is not a JSON object" in nat and "header is not a JSON object" not in py:
+                continue
+            assert py == nat, (bytes(b[8:8 + hlen]), py, nat)
+        agree += 1
+    assert agree > 350 and accepted > 0
