@@ -420,7 +420,11 @@ int upload_matrix(const uocr_moe_plan* p, const uocr_moe_layer_src& src, const v
   void* staging = nullptr;
   if (src.memory == UOCR_MEMORY_HOST) {
     UOCR_TRY(cudaMallocAsync(&staging, n * sb, stream), "set_layer: staging allocation");
-    UOCR_TRY(cudaMemcpyAsync(staging, from, n * sb, cudaMemcpyHostToDevice, stream), "set_layer: upload");
+    const cudaError_t up = cudaMemcpyAsync(staging, from, n * sb, cudaMemcpyHostToDevice, stream);
+    if (up != cudaSuccess) {
+      cudaFreeAsync(staging, stream);
+      return cuda_fail(up, "set_layer: upload");
+    }
     dev_src = staging;
   }
   cudaError_t st = cudaSuccess;
