@@ -248,9 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __nv_bfloat16* __restrict__ act, const __nv_bfloat16* __restrict__ act_s,
                        const float* resid, float* y, ErrorWord* err, int stage_act) {
   using Fm = Fmt<Rows>;
-  // stage_act: the block copies the activations (shared rows [T, S], then the
-  // routed slots [slots, F]) into shared memory once, so the products read
-  // them at shared-memory latency instead of one L2 round trip per step.
+  // stage_act: the block copies activations into shared memory once, so the
+  // products read them at shared-memory latency instead of one L2 round trip
+  // per step: 1 = the shared rows [T, S] then the routed slots [slots, F];
+  // 2 = the routed slots only (when both do not fit: the many routed steps
+  // read shared memory, the shared row's few steps read L2); 0 = none.
   extern __shared__ __align__(16) __nv_bfloat16 act_sm[];
   __shared__ SmemRoute sroute;
   __shared__ uint64_t route_ready;
@@ -280,8 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int spr_f = (nch_f + 32 * kStep - 1) / (32 * kStep);
   float* sum = row_sum[warp];
   bool waited = false, have_route = false, staged = !stage_act;
-  const __nv_bfloat16* acts = stage_act ? act_sm : act_s;                      // [T, S]
-  const __nv_bfloat16* actr = stage_act ? act_sm + static_cast<int64_t>(T) * S : act;  // [slots, F]
+  const __nv_bfloat16* acts = stage_act == 1 ? act_sm : act_s;  // [T, S]
+  const __nv_bfloat16* actr =
+      stage_act == 1 ? act_sm + static_cast<int64_t>(T) * S : (stage_act == 2 ? act_sm : act);  // [slots, F]
   // Every streaming warp calls this exactly once (also on its error paths,
   // so that none waits at the barrier for a warp that left): wait for the
   // activations and the routing table, copy, and meet the other streaming warps.
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (good) {
       const int U = sroute.count;
       const int slots = U > 0 ? sroute.base[U - 1] + sroute.ntok[U - 1] : 0;
-      const int n_s = T * S / 8, n_r = slots * F / 8;  // 16-byte chunks
+      const int n_s = stage_act == 1 ? T * S / 8 : 0, n_r = slots * F / 8;  // 16-byte chunks
       const uint4* src_s = reinterpret_cast<const uint4*>(act_s);
       const uint4* src_r = reinterpret_cast<const uint4*>(act);
       uint4* dst = reinterpret_cast<uint4*>(act_sm);
@@ -535,14 +538,16 @@ cudaError_t launch_decode_experts_t(const float* x, int T, int H, int F, int S, 
   }
   rs.ids_out = nullptr;
   rs.w_out = nullptr;
-  // Activations staged in shared memory when they fit (T*S + T*k*F bf16).
+  // Activations staged in shared memory when they fit (T*S + T*k*F bf16), else
+  // the routed slots alone (T*k*F) when those fit.
   int dev = 0;
   if ((st = cudaGetDevice(&dev)) != cudaSuccess) return st;
-  const size_t need = (static_cast<size_t>(T) * S + static_cast<size_t>(T) * routing.top_k * F) * 2;
-  int stage = dev < kMaxDevices && need <= g_down_dyn_limit[dev] ? 1 : 0;
+  const size_t need_s = static_cast<size_t>(T) * S * 2, need_r = static_cast<size_t>(T) * routing.top_k * F * 2;
+  const size_t limit = dev < kMaxDevices ? g_down_dyn_limit[dev] : 0;
+  int stage = need_s + need_r <= limit ? 1 : (need_r <= limit ? 2 : 0);
+  const size_t dn_smem = stage == 1 ? need_s + need_r : (stage == 2 ? need_r : 0);
   void* args[] = {&T, &H, &F, &S, &down, &sdown, &rs, &act, &act_s, &resid, &y, &err, &stage};
-  return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), stage ? need : 0, stream, args,
-                          pdl && between == nullptr);
+  return launch_maybe_pdl(dn, dim3(sm_count), dim3(kThreads), dn_smem, stream, args, pdl && between == nullptr);
 }
 
 }  // namespace
