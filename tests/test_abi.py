@@ -104,7 +104,13 @@ def test_null_arguments_are_rejected():
     assert lib.uocr_moe_plan_create(None, None) == 1
     assert lib.uocr_moe_forward(None, 0, None, 1, None, None, None, None) == 1
     assert lib.uocr_moe_set_layer(None, 0, None, None) == 1
+    assert lib.uocr_moe_set_layer_parts(None, 0, None, None) == 1
+    assert lib.uocr_moe_load_layer(None, None, 0, 0, None) == 1
     assert lib.uocr_moe_plan_destroy(None) == 0
+    assert lib.uocr_checkpoint_open(None, None) == 1
+    assert lib.uocr_checkpoint_count(None, None) == 1
+    assert lib.uocr_checkpoint_tensor(None, b"x", None) == 1
+    assert lib.uocr_checkpoint_close(None) == 0
 
 
 def test_op_mirror_argument_checks():
