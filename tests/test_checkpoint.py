@@ -322,3 +322,20 @@ def test_native_and_python_readers_agree_on_mutated_headers(tmp_path):
             assert py == nat, (bytes(b[8:8 + hlen]), py, nat)
         agree += 1
     assert agree > 350 and accepted > 0
+
+
+def test_moe_layer_table_dtype_problems(tmp_path):
+    """A layer must be all BF16 or all F32: another dtype, or a mix, is named."""
+    H, E, F, S = 64, 2, 32, 64
+    tensors = {}
+    for name, shape in C.moe_layer_tensors(1, H, E, F, S).items():
+        tensors[name] = ("BF16", np.zeros(shape, np.uint16))
+    f16 = "model.layers.1.mlp.experts.1.up_proj.weight"
+    f32 = "model.layers.1.mlp.gate.weight"
+    tensors[f16] = ("F16", np.zeros((F, H), np.float16))
+    tensors[f32] = ("F32", np.zeros((E, H), np.float32))
+    C.write_safetensors(tmp_path / "one.safetensors", tensors)
+    C.write_index(tmp_path / "idx.json", {n: "one.safetensors" for n in tensors})
+    probs = C.check_moe_layer(C.ShardedWeights.open(tmp_path / "idx.json"), 1, H, E, F, S)
+    assert f"{f16}: dtype F16, expected BF16 or F32" in probs
+    assert probs[-1] == "layer 1: mixed dtypes ['BF16', 'F16', 'F32']"
