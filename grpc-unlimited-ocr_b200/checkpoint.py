@@ -146,6 +146,17 @@ class SafetensorsFile:
     def find(self, name: str):
         return self.tensors.get(name)
 
+    def close(self) -> None:
+        """Unmaps the file. Arrays from array() must be gone first (the map
+        refuses to close under live views: BufferError)."""
+        self._map.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
     def array(self, name: str) -> np.ndarray:
         info = self.tensors[name]
         typ, _ = DTYPES[info.dtype]
@@ -219,6 +230,16 @@ class ShardedWeights:
 
     def tensor_count(self) -> int:
         return len(self._where)
+
+    def close(self) -> None:
+        for shard in self.shards:
+            shard.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def write_safetensors(path, tensors: dict, metadata: dict | None = None) -> None:

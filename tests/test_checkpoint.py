@@ -339,3 +339,17 @@ def test_moe_layer_table_dtype_problems(tmp_path):
     probs = C.check_moe_layer(C.ShardedWeights.open(tmp_path / "idx.json"), 1, H, E, F, S)
     assert f"{f16}: dtype F16, expected BF16 or F32" in probs
     assert probs[-1] == "layer 1: mixed dtypes ['BF16', 'F16', 'F32']"
+
+
+def test_readers_close(tmp_path):
+    _two_shards(tmp_path)
+    C.write_index(tmp_path / "good.json", {"x": "s1.safetensors", "y": "s1.safetensors", "z": "s2.safetensors"})
+    with C.ShardedWeights.open(tmp_path / "good.json") as w:
+        assert w.array("z").sum() == 6  # the view is gone before the close
+    assert all(s._map.closed for s in w.shards)
+    f = C.SafetensorsFile(tmp_path / "s1.safetensors")
+    view = f.array("x")
+    with pytest.raises(BufferError):
+        f.close()  # a live view keeps the map open
+    del view
+    f.close()
