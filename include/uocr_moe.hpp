@@ -16,6 +16,7 @@
 #define UOCR_MOE_HPP
 
 #include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -31,6 +32,19 @@ inline void check(int status) {
   const std::string what = std::string("uocr: ") + uocr_last_error();
   if (status == UOCR_ERR_INVALID_ARGUMENT || status == UOCR_ERR_UNSUPPORTED) throw std::invalid_argument(what);
   throw std::runtime_error(what);
+}
+
+// GRPC_UOCR_WEIGHT_FORMAT as the engine reads it for the cuda backend
+// (src/service/config.cpp:28-39, 53-55; default bf16, config.h:20): unset or
+// empty is bf16, "bf16" and "int8" select, anything else throws
+// std::invalid_argument naming the variable and its choices.
+inline uocr_weight_format weight_format_from_env() {
+  const char* raw = std::getenv("GRPC_UOCR_WEIGHT_FORMAT");
+  if (raw == nullptr || *raw == '\0') return UOCR_WEIGHT_BF16;
+  const std::string value(raw);
+  if (value == "bf16") return UOCR_WEIGHT_BF16;
+  if (value == "int8") return UOCR_WEIGHT_INT8;
+  throw std::invalid_argument("GRPC_UOCR_WEIGHT_FORMAT must be one of bf16, int8");
 }
 
 // ---- the reference's op shapes (stream first instead of the Context) --------

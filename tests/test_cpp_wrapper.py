@@ -15,6 +15,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 PROGRAM = r"""
 #include <cstdio>
 #include <stdexcept>
+#include <string>
 #include "uocr_moe.hpp"
 
 template <typename E, typename F>
@@ -30,6 +31,14 @@ static void expect(const char* what, F&& f) {
 }
 
 int main(int argc, char** argv) {
+  if (argc > 1 && std::string(argv[1]) == "format") {
+    try {
+      std::printf("format %d\n", static_cast<int>(uocr_b200::weight_format_from_env()));
+    } catch (const std::invalid_argument& e) {
+      std::printf("format error: %s\n", e.what());
+    }
+    return 0;
+  }
   // ops.cu:655 throws invalid_argument above 128 experts; so does the wrapper
   expect<std::invalid_argument>("topk experts", [] {
     uocr_b200::expert_topk(nullptr, nullptr, 1, 129, 2, nullptr, nullptr);
@@ -74,3 +83,11 @@ def test_cpp_wrapper_exceptions_and_ownership(tmp_path):
     assert out[4] == f"tensors {len(arrays)}"
     assert out[5] == f"rank 2 bytes {arrays[name].nbytes}"
     assert out[6] == "absent tensor: ok: uocr: no tensor named nope"
+
+    for value, want in ((None, "format 0"), ("", "format 0"), ("bf16", "format 0"), ("int8", "format 1"),
+                        ("fp32", "format error: GRPC_UOCR_WEIGHT_FORMAT must be one of bf16, int8")):
+        env = {k: v for k, v in os.environ.items() if k != "GRPC_UOCR_WEIGHT_FORMAT"}
+        if value is not None:
+            env["GRPC_UOCR_WEIGHT_FORMAT"] = value
+        r = subprocess.run([str(exe), "format"], check=True, capture_output=True, text=True, env=env)
+        assert r.stdout.strip() == want, value
