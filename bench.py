@@ -248,6 +248,23 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         h = x.clone()
         prof = plan.profile_stack(h, iters=3, stream=stream)
         plan.check(stream=stream)
+    ep_equal = None
+    if world > 1:
+        # The same rows through a one-GPU plan on this rank: the expert-parallel
+        # output must equal it bit for bit (an output row depends on its own
+        # input row only, and the combine order is the same).
+        single = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0)
+        C.load_layer(single, cfg, 0, t)
+        y1 = torch.empty_like(x)
+        with torch.cuda.stream(stream):
+            single.forward(0, x, y1, stream=stream)
+            single.check(stream=stream)
+        torch.cuda.synchronize()
+        eq = torch.tensor([1 if torch.equal(y, y1) else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(eq, op=dist.ReduceOp.MIN)
+        ep_equal = bool(eq.item())
+        single.close()
+        del y1
     counts_t = torch.bincount(ids.view(-1).long(), minlength=cfg.experts)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -289,6 +306,11 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
                            "peak_source": peak_src, "unit": "TFLOP/s", "frac": per_gpu / peak,
                            "algorithmic_flops_per_layer": total_flops}
         out["rows_received_per_rank"] = owner_rows
+        out["rows_received_max_over_mean"] = max(owner_rows) / (sum(owner_rows) / world)
+        out["ep_bitwise_equal"] = ep_equal
+    if world == 1 and rank == 0:
+        out["ids_check"] = route_check(cfg, [x.cpu().numpy()], [ids.cpu().numpy()], norm=False,
+                                       bias=t["router_bias"].cpu().numpy())
     if want_cpu:
         cpu_rows = min(512, T)
         hw = host_layer_weights(cfg)
@@ -346,10 +368,128 @@ def run_reference_arm(args, cfg, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def route_check(cfg, inputs, got_ids, eps=1e-6, norm=True, bias=None):
+    """Expert ids of every layer against the oracle (outside the timed region):
+    the oracle's exact-order router on the layer's input rows (RMSNorm'd when
+    `norm`, plus the router `bias` when given).
+    Returns rows checked, rows whose ids differ inside the north-star margin
+    exemption (k-th vs (k+1)-th gate-logit gap or an order gap below 1e-3),
+    and rows that differ outside it (must be 0)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    H, E, K = cfg.hidden, cfg.experts, cfg.top_k
+    Fd = 1  # the ids depend on the router alone: zero expert stacks of width 1
+    z = np.zeros
+    rows = exempt = bad = 0
+    for layer, (h, ids) in enumerate(zip(inputs, got_ids)):
+        r = O.synth(cfg.seed, layer, O.KIND_ROUTER, 0, E * H, 0.02)
+        r = (O.round_bf16(r) if cfg.bf16_values else r).reshape(E, H)
+        w = O.MoeWeights(r, z((E * Fd, H), np.float32), z((E * Fd, H), np.float32), z((E * H, Fd), np.float32),
+                         z((0, H), np.float32), z((0, H), np.float32), z((H, 0), np.float32))
+        if bias is not None:
+            w.router_bias = np.asarray(bias, np.float32)
+        want = O.moe_forward(w, O.rms_norm(h, None, eps) if norm else h, K, renormalize=True)
+        for t in range(h.shape[0]):
+            rows += 1
+            if np.array_equal(ids[t], want.ids[t]):
+                continue
+            if want.margin[t] < 1e-3 or want.order_margin[t] < 1e-3:
+                exempt += 1
+            else:
+                bad += 1
+    return {"rows_checked": rows, "margin_exempt_rows": exempt, "mismatched_rows_outside_margin": bad,
+            "rule": "ids and order equal to the oracle's except rows whose k-th vs (k+1)-th gate-logit margin "
+                    "(or an order gap) is below 1e-3"}
+
+
+def time_decode(plan, x, steps, warmup, stream, clocks=None, barrier=None):
+    """Device time per step of the stack at batch x.shape[0] (CUDA events on
+    the launching stream, inputs resident in HBM)."""
+    import torch
+    h = torch.empty_like(x)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            h.copy_(x)
+            plan.forward_stack(h, stream=stream)
+        plan.check(stream=stream)
+        if clocks is not None:
+            clocks.start()
+            clocks.wait_first()
+        if barrier is not None:
+            barrier()
+        torch.cuda.synchronize()
+        if clocks is not None:
+            clocks.mark()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            h.copy_(x)
+            plan.forward_stack(h, stream=stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        if barrier is not None:
+            barrier()
+        clk = clocks.stop() if clocks is not None else None
+        plan.check(stream=stream)
+    return start.elapsed_time(end) / steps, clk
+
+
+def decode_ids_and_inputs(plan, cfg, x, stream):
+    """Layer by layer (outside any timed region): each layer's input rows and
+    produced ids, the distinct experts per layer, and whether the stack's
+    output is finite. The layer is h <- h + MoE(RMSNorm(h))."""
+    import torch
+    T = x.shape[0]
+    hh = x.clone()
+    y = torch.empty_like(hh)
+    ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=x.device)
+    inputs, got, active = [], [], []
+    with torch.cuda.stream(stream):
+        for layer in range(cfg.layers):
+            plan.forward(layer, hh, y, ids, None, stream=stream)
+            torch.cuda.synchronize()
+            inputs.append(hh.cpu().numpy())
+            got.append(ids.cpu().numpy())
+            active.append(len(set(got[-1].ravel().tolist())))
+            hh = hh + y
+        plan.check(stream=stream)
+    return inputs, got, active, bool(torch.isfinite(hh).all().item())
+
+
+def decode_section(plan, cfg, T, fmt_int8, steps, stream, dev, check_routes):
+    """One named decode configuration: tokens/s, the step's algorithmic bytes
+    (from the distinct experts the produced ids touched) against the measured
+    HBM peak, the gate/up kernel's fraction, and the ids check."""
+    import moe_configs as C
+    x = C.device_input(cfg, T, device=dev)
+    ms, _ = time_decode(plan, x, steps, 3, stream)
+    h = x.clone()
+    prof = plan.profile_stack(h, iters=5, stream=stream)
+    inputs, got, active, finite = decode_ids_and_inputs(plan, cfg, x, stream)
+    step_bytes, gu_bytes = decode_bytes(cfg, active, fmt_int8)
+    hbm_peak, peak_kind = measured_peaks()
+    gu = (sum(gu_bytes) / len(gu_bytes)) / (prof["gate_up"] * 1e-3) / 1e9
+    step_gbs = step_bytes / (ms * 1e-3) / 1e9
+    out = {"workload": f"{cfg.name}: {cfg.layers}-layer MoE stack, batch {T}, "
+                       + ("int8 per-channel" if fmt_int8 else "bf16") + " weights",
+           "batch": T, "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+           "roofline": {"bound": "hbm", "kernel": "gate_up_decode", "achieved": gu, "peak": hbm_peak,
+                        "peak_source": peak_kind, "unit": "GB/s", "frac": gu / hbm_peak,
+                        "step_achieved": step_gbs, "step_frac": step_gbs / hbm_peak,
+                        "algorithmic_bytes_per_step": step_bytes,
+                        "kernel_ms": {k: round(v, 5) for k, v in prof.items()}},
+           "distinct_experts_per_layer": active, "stack_output_finite": finite}
+    if check_routes:
+        out["ids_check"] = route_check(cfg, inputs, got)
+    return out, (inputs, got)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=1)
@@ -357,7 +497,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None, help="override the stack depth (default 24)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill section")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sections")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the other named decode configurations (config 1 at batch 4/8, config 2)")
     ap.add_argument("--prefill-rows", type=int, default=None, help="shrink the prefill batch (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -388,53 +530,35 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    barrier = (lambda: dist.barrier()) if world > 1 else None
 
     T = args.batch
     fmt_int8 = args.format == "int8"
+    sub_configs = not args.no_configs and world == 1 and args.layers is None
     # Each layer is the decoder's feed-forward block, h <- h + MoE(RMSNorm(h))
     # with unit gains: the layer inputs stay ~N(0, 1) as config 1 specifies
     # (a bare residual stack of N(0, 0.02) SwiGLU layers grows quadratically
     # and overflows by the last layers, which would collapse their routing).
-    plan = M.Plan(cfg.dims(), max_rows=max(T, 1), weight_format=M.WEIGHT_INT8 if fmt_int8 else M.WEIGHT_BF16,
-                  renormalize=True, device=local, flags=M.PLAN_PRE_NORM, rms_norm_eps=1e-6)
-    host_layer0 = None
-    for layer in range(cfg.layers):
-        t = C.device_layer(cfg, layer, device=dev)
-        C.load_layer(plan, cfg, layer, t)
-        del t
-    torch.cuda.synchronize()
+    def make_plan(c, int8, max_rows):
+        pl = M.Plan(c.dims(), max_rows=max_rows, weight_format=M.WEIGHT_INT8 if int8 else M.WEIGHT_BF16,
+                    renormalize=True, device=local, flags=M.PLAN_PRE_NORM, rms_norm_eps=1e-6)
+        for layer in range(c.layers):
+            t = C.device_layer(c, layer, device=dev)
+            C.load_layer(pl, c, layer, t)
+            del t
+        torch.cuda.synchronize()
+        return pl
+
+    other_batches = [b for b in cfg.rows if b != T] if sub_configs else []
+    plan = make_plan(cfg, fmt_int8, max(T, *other_batches) if other_batches else T)
     stream = torch.cuda.Stream(device=dev)
     x = C.device_input(cfg, T, device=dev)
     h = torch.empty_like(x)
 
-    def step():
-        h.copy_(x)
-        plan.forward_stack(h, stream=stream)
+    clocks = ClockSampler(local)
+    ms, clk = time_decode(plan, x, args.steps, args.warmup, stream, clocks=clocks, barrier=barrier)
 
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-        plan.check(stream=stream)
-        clocks = ClockSampler(local)
-        clocks.start()
-        clocks.wait_first()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        clocks.mark()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        end.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        clk = clocks.stop()
-        ms = start.elapsed_time(end) / args.steps
-        plan.check(stream=stream)
-
         # End to end through the public call with host buffers: pinned x in,
         # h out, both copies inside the timed region.
         x_host = x.cpu().pin_memory()
@@ -458,18 +582,7 @@ def main():
         # Per-kernel device times (same workload, events between the kernels).
         h.copy_(x)
         prof = plan.profile_stack(h, iters=5, stream=stream)
-        # Distinct experts per layer, from the ids the stack produces.
-        hh = x.clone()
-        y = torch.empty_like(hh)
-        ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
-        active = []
-        for layer in range(cfg.layers):
-            plan.forward(layer, hh, y, ids, None, stream=stream)
-            torch.cuda.synchronize()
-            active.append(len(set(ids.cpu().numpy().ravel().tolist())))
-            hh = hh + y
-        plan.check(stream=stream)
-        finite = bool(torch.isfinite(hh).all().item())
+    inputs, got_ids, active, finite = decode_ids_and_inputs(plan, cfg, x, stream)
 
     times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -482,23 +595,44 @@ def main():
     step_gbs = step_bytes / (ms_max * 1e-3) / 1e9
     traffic = traffic_from_profile(f"decode_gate_up_{args.format}_t{T}.txt")
 
-    prefill = None
+    # The other named decode configurations (one GPU): config 1 (or 2) at its
+    # other batch sizes on the same plan, then the other weight format.
+    configs = []
+    if sub_configs:
+        for b in other_batches:
+            configs.append(decode_section(plan, cfg, b, fmt_int8, max(20, args.steps // 4), stream, dev,
+                                          check_routes=rank == 0)[0])
+    plan.close()  # free the stack's weights first
+    if sub_configs:
+        ocfg = C.CONFIGS[1 if fmt_int8 else 2]
+        oplan = make_plan(ocfg, not fmt_int8, max(ocfg.rows))
+        for b in ocfg.rows:
+            configs.append(decode_section(oplan, ocfg, b, not fmt_int8, max(20, args.steps // 4), stream, dev,
+                                          check_routes=rank == 0)[0])
+        oplan.close()
+
+    prefill = prefill_int8 = None
     if not args.no_prefill:
-        plan.close()  # free the decode stack's 20 GB first
         # Expert parallelism (world > 1) assigns expert e to rank e % G: with
         # the Zipf-skewed router that spreads the hot experts over the ranks.
         # Contiguous ranges (rank e // (E / G)) are measured beside it.
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
                               want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
-                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1,
-                              int8=fmt_int8 and world == 1)
+                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1)
         if world > 1:
             alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
                               rows=args.prefill_rows, world=world, rank=rank, strided=False)
             prefill["contiguous_experts"] = {k: alt[k] for k in ("value", "ms_per_layer", "kernel_ms",
-                                                               "rows_received_per_rank", "parallelism")}
+                                                               "rows_received_per_rank", "parallelism",
+                                                               "ep_bitwise_equal")}
+        elif sub_configs:
+            prefill_int8 = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
+                                       rows=args.prefill_rows, int8=True)
 
     cpu = None
+    ids_check = None
+    if rank == 0:
+        ids_check = route_check(cfg, inputs, got_ids)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host_layer0 = host_layer_weights(cfg)
         t_layer, kind, cores, reps = cpu_reference_layer_time(cfg, host_layer0, T, args.cpu_budget,
@@ -529,6 +663,7 @@ def main():
                          "algorithmic_bytes_per_step": step_bytes,
                          "kernel_ms": {k: round(v, 5) for k, v in prof.items()},
                          "distinct_experts_per_layer": active, "stack_output_finite": finite},
+            "ids_check": ids_check,
             "cpu_baseline": cpu,
             "e2e": {"value": world * T / (e2e_max * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * cfg.hidden * 4, "d2h_bytes_per_step": T * cfg.hidden * 4,
@@ -536,10 +671,13 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if configs:
+            line["decode_configs"] = configs
         if prefill is not None:
             line["prefill"] = prefill
+        if prefill_int8 is not None:
+            line["prefill_int8"] = prefill_int8
         print(json.dumps(line), flush=True)
-    plan.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -17,7 +17,6 @@
 
 #include "../../include/uocr_moe.h"
 #include "checkpoint.h"
-#include "decode_tc.h"
 #include "ep.h"
 #include "moe_kernels.h"
 #include "prefill.h"
@@ -123,9 +122,6 @@ struct uocr_moe_plan {
   bool prefill = false;
   PrefillDims pdims{};
   PrefillScratch pscratch{};
-  // bf16 decode batches on the tensor cores.
-  bool decode_tc = false;
-  DecodeTcScratch dtc{};
   // Expert parallelism (ep_world > 1): this rank's exchange region, the peers'
   // (IPC mappings, closed on destroy) and the EP scratch in the arena.
   bool ep = false;
@@ -201,18 +197,15 @@ struct uocr_moe_plan {
       char* base = c.take<char>(ep_scratch_bytes(pdims, elay, emap));
       carve_ep_scratch(pdims, elay, emap, base, &escr);
     }
-    if (decode_tc) {
-      const int H = static_cast<int>(d.hidden), F = static_cast<int>(d.expert_ffn), S = static_cast<int>(d.shared_ffn);
-      char* base = c.take<char>(decode_tc_scratch_bytes(H, F, S));
-      carve_decode_tc_scratch(H, F, S, base, &dtc);
-    }
   }
 };
 
 namespace {
 
 // Shared body of the expert_ffn_one mirrors: scratch from cudaMallocAsync on
-// the stream, as the reference's expert_ffn does (gemv_ops.cu:176,182).
+// the stream, as the reference's expert_ffn does (gemv_ops.cu:176,182). A bad
+// expert id is recorded in the device's op-level error word, which
+// uocr_ops_check reads.
 template <typename Launch>
 int ffn_one(const float* x, int64_t hidden, int64_t ffn, const int64_t* ids, const float* weights, int64_t k,
             float* out, int64_t experts_hint, cudaStream_t stream, Launch&& launch) {
@@ -222,16 +215,15 @@ int ffn_one(const float* x, int64_t hidden, int64_t ffn, const int64_t* ids, con
   if (x == nullptr || ids == nullptr || weights == nullptr || out == nullptr)
     return fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one: null pointer");
   const size_t route_off = 0, act_off = align_up(sizeof(DecodeRoute), 256),
-               err_off = align_up(act_off + static_cast<size_t>(k * ffn) * 2, 256),
-               total = err_off + sizeof(ErrorWord);
+               total = act_off + static_cast<size_t>(k * ffn) * 2;
+  ErrorWord* err = nullptr;
+  UOCR_TRY(ops_error_word(&err), "expert_ffn_one: error word");
   char* scratch = nullptr;
   UOCR_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), total, stream), "expert_ffn_one: scratch");
   auto* route = reinterpret_cast<DecodeRoute*>(scratch + route_off);
   auto* act = reinterpret_cast<__nv_bfloat16*>(scratch + act_off);
-  auto* err = reinterpret_cast<ErrorWord*>(scratch + err_off);
-  cudaError_t st = cudaMemsetAsync(err, 0, sizeof(ErrorWord), stream);
-  if (st == cudaSuccess)
-    st = launch_route_from_ids(ids, weights, static_cast<int>(k), static_cast<int>(experts_hint), route, err, stream);
+  cudaError_t st =
+      launch_route_from_ids(ids, weights, static_cast<int>(k), static_cast<int>(experts_hint), route, err, stream);
   if (st == cudaSuccess) st = launch(route, act, err);
   cudaFreeAsync(scratch, stream);
   if (st != cudaSuccess) return cuda_fail(st, "expert_ffn_one");
@@ -333,10 +325,6 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
       if (ms > 0) p->ep_wait_ns = static_cast<uint64_t>(ms) * 1000000ull;
     }
   }
-  p->decode_tc = dr > 0 && d.weight_format == UOCR_WEIGHT_BF16 && (d.flags & UOCR_PLAN_TENSOR_DECODE) != 0 &&
-                 !pre_norm &&
-                 decode_tc_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn),
-                                     static_cast<int>(d.shared_ffn));
 
   Carver probe{nullptr};
   LayerDev tmp;
@@ -764,31 +752,7 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   if (ev != nullptr) UOCR_TRY(cudaEventRecord(ev[0], stream), "forward: event");
   cudaEvent_t between = ev != nullptr ? ev[1] : nullptr;
   const DecodeRouting routing{nullptr, p->route, E, K, d.renormalize, nullptr, nullptr};
-  if (p->decode_tc) {
-    auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
-    DecodeTcCall c{};
-    c.x = x;
-    c.T = T;
-    c.H = H;
-    c.F = F;
-    c.S = S;
-    c.E = E;
-    c.gate = b(L.gate);
-    c.up = b(L.up);
-    c.down = b(L.down);
-    c.sgate = b(L.sgate);
-    c.sup = b(L.sup);
-    c.sdown = b(L.sdown);
-    c.routing = routing;
-    c.resid = resid;
-    c.y = y;
-    c.scratch = p->dtc;
-    c.err = p->err;
-    c.sm_count = p->sm_count;
-    c.pdl = pdl;
-    c.between = between;
-    UOCR_TRY(launch_decode_tc(c, stream), "forward: experts (tensor cores)");
-  } else if (d.weight_format == UOCR_WEIGHT_BF16) {
+  if (d.weight_format == UOCR_WEIGHT_BF16) {
     auto b = [](void* v) { return static_cast<const __nv_bfloat16*>(v); };
     UOCR_TRY(launch_decode_experts_bf16(x, T, H, F, S, b(L.gate), b(L.up), b(L.down), b(L.sgate), b(L.sup),
                                         b(L.sdown), routing, p->act, p->act_s, resid, y, p->err, p->sm_count,
@@ -1120,6 +1084,23 @@ int uocr_moe_ep_forward_local(uocr_moe_plan* const* plans, int32_t n, int64_t la
 }
 
 // ---- op-level mirrors ----------------------------------------------------
+
+int uocr_ops_check(void* stream) {
+  UOCR_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "ops_check: stream");
+  ErrorWord* word = nullptr;
+  UOCR_TRY(ops_error_word(&word), "ops_check: error word");
+  ErrorWord e{};
+  UOCR_TRY(cudaMemcpy(&e, word, sizeof(e), cudaMemcpyDeviceToHost), "ops_check: read");
+  if (e.code == kDevOk) return UOCR_OK;
+  UOCR_TRY(cudaMemset(word, 0, sizeof(ErrorWord)), "ops_check: clear");
+  char buf[160];
+  if (e.code == kDevBadIndex && e.where == 2)
+    std::snprintf(buf, sizeof(buf), "expert_ffn_one: expert id %d at position %d is outside [0, %d)", e.b, e.a,
+                  kMaxExperts);
+  else
+    std::snprintf(buf, sizeof(buf), "device error %d at site %d (%d, %d)", e.code, e.where, e.a, e.b);
+  return fail(e.code == kDevWaitTimeout ? UOCR_ERR_TIMEOUT : UOCR_ERR_DEVICE, buf);
+}
 
 int uocr_expert_topk(const float* logits, int64_t rows, int64_t experts, int64_t k, int32_t renormalize,
                      int64_t* ids, float* weights, void* stream) {

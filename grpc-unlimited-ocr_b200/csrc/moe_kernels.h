@@ -44,6 +44,10 @@ cudaError_t launch_topk_rows(const float* logits, int64_t rows, int E, int K, in
                              float* weights, cudaStream_t stream);
 cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int K, int E, DecodeRoute* route,
                                   ErrorWord* err, cudaStream_t stream);
+// Device address of the current device's op-level error word (looked up once
+// per device): the expert_ffn_one mirrors record bad ids there, and
+// uocr_ops_check reads and clears it.
+cudaError_t ops_error_word(ErrorWord** out);
 
 // ---- decode experts (decode.cu) ----
 // Where the decode expert kernels take their routing from: the router's

@@ -10,13 +10,15 @@
 // cudaMallocAsync, as the reference's expert_ffn does; this variant takes it
 // from one static device array instead and allocates nothing.
 //
-// The scratch (routing table, error word and the [k, ffn] bf16 activation
-// rows) lives in g_noalloc_scratch below: about 146 KiB that every GPU which
-// loads this library holds until the process exits. Every call shares it and
-// it keeps the last call's contents; the call clears the error word and fully
-// rewrites the routing table and the activation rows it reads. Calls that
-// overlap on the GPU (different streams, or different host threads, on the
-// same device) race on the array and must be serialised by the caller.
+// The scratch (routing table and the [k, ffn] bf16 activation rows) lives in
+// g_noalloc_scratch below: about 146 KiB that every GPU which loads this
+// library holds until the process exits. Every call shares it and it keeps
+// the last call's contents; each call fully rewrites the routing table and
+// the activation rows it reads, so nothing in it has to start at zero. Calls
+// that overlap on the GPU (different streams, or different host threads, on
+// the same device) race on the array and must be serialised by the caller.
+// A bad expert id goes to the device's op-level error word (also static
+// device memory), which uocr_ops_check reads and clears.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,8 +34,7 @@ namespace {
 constexpr int64_t kNoAllocMaxK = kMaxTopK;  // 8 routed experts per call
 constexpr int64_t kNoAllocMaxFfn = 8192;    // expert width
 constexpr size_t kRouteOffset = 0;
-constexpr size_t kErrOffset = (sizeof(DecodeRoute) + 255) / 256 * 256;
-constexpr size_t kActOffset = kErrOffset + 256;
+constexpr size_t kActOffset = (sizeof(DecodeRoute) + 255) / 256 * 256;
 constexpr size_t kScratchBytes = kActOffset + static_cast<size_t>(kNoAllocMaxK * kNoAllocMaxFfn) * 2;
 
 // The only storage this entry point uses. In host code this name is a
@@ -45,8 +46,8 @@ int noalloc_fail(int code, const std::string& what) { return set_last_error(code
 
 // Device address of g_noalloc_scratch on the current device, looked up once
 // per device (the first call on a device does this; make that first call
-// before any stream capture).
-int scratch_address(unsigned char** out) {
+// before any stream capture), and the current device's ordinal.
+int scratch_address(unsigned char** out, int* device) {
   static std::mutex mu;
   static unsigned char* addr[kMaxDevices] = {};
   int dev = 0;
@@ -62,6 +63,7 @@ int scratch_address(unsigned char** out) {
     addr[dev] = static_cast<unsigned char*>(p);
   }
   *out = addr[dev];
+  *device = dev;
   return UOCR_OK;
 }
 
@@ -82,18 +84,22 @@ extern "C" int uocr_expert_ffn_one_noalloc(const float* x, int64_t hidden, int64
       out == nullptr)
     return noalloc_fail(UOCR_ERR_INVALID_ARGUMENT, "expert_ffn_one_noalloc: null pointer");
   unsigned char* base = nullptr;
-  const int rc = scratch_address(&base);
+  int dev = 0;
+  const int rc = scratch_address(&base, &dev);
   if (rc != UOCR_OK) return rc;
+  ErrorWord* err = nullptr;
+  cudaError_t st = ops_error_word(&err);
+  if (st != cudaSuccess)
+    return noalloc_fail(UOCR_ERR_CUDA, std::string("expert_ffn_one_noalloc: error word: ") + cudaGetErrorString(st));
+  int sms = 0;
+  st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (st != cudaSuccess)
+    return noalloc_fail(UOCR_ERR_CUDA, std::string("expert_ffn_one_noalloc: SM count: ") + cudaGetErrorString(st));
   auto stream = static_cast<cudaStream_t>(stream_v);
   auto* route = reinterpret_cast<DecodeRoute*>(base + kRouteOffset);
-  auto* err = reinterpret_cast<ErrorWord*>(base + kErrOffset);
   auto* act = reinterpret_cast<__nv_bfloat16*>(base + kActOffset);
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   auto b = [](const uint16_t* v) { return reinterpret_cast<const __nv_bfloat16*>(v); };
-  cudaError_t st = cudaMemsetAsync(err, 0, sizeof(ErrorWord), stream);  // the only state that must start at zero
-  if (st == cudaSuccess) st = launch_route_from_ids(ids, weights, static_cast<int>(k), kMaxExperts, route, err, stream);
+  st = launch_route_from_ids(ids, weights, static_cast<int>(k), kMaxExperts, route, err, stream);
   const DecodeRouting routing{nullptr, route, kMaxExperts, static_cast<int>(k), 0, nullptr, nullptr};
   if (st == cudaSuccess)
     st = launch_decode_experts_bf16(x, 1, static_cast<int>(hidden), static_cast<int>(ffn), 0, b(gate), b(up),

@@ -8,6 +8,8 @@
 // reference only where its float exp and CUDA's expf round a near-tie apart.
 // Softmax and top-k selection live in route.cuh (each expert-kernel block
 // runs them on these logits).
+#include <mutex>
+
 #include "moe_kernels.h"
 #include "ptx.cuh"
 #include "rms_norm.cuh"
@@ -291,15 +293,20 @@ __global__ void route_from_ids_kernel(const int64_t* ids, const float* weights, 
   route->slot_total = K;
   for (int j = 0; j < K; ++j) {
     int64_t id = ids[j];
+    float w = weights[j];
     if (id < 0 || id >= E) {
+      // Recorded in the op-level error word (uocr_ops_check reports it);
+      // the slot reads expert 0's rows with weight 0, so nothing outside
+      // the stacks is touched and the bad id adds nothing to the output.
       raise_error(err, kDevBadIndex, 2, j, static_cast<int>(id));
       id = 0;
+      w = 0.0f;
     }
     route->active_expert[j] = static_cast<int>(id);
     route->tok_count[j] = 1;
     route->slot_base[j] = j;
     route->slot_tok[j] = 0;
-    route->slot_w[j] = weights[j];
+    route->slot_w[j] = w;
   }
 }
 
@@ -375,6 +382,28 @@ cudaError_t launch_route_from_ids(const int64_t* ids, const float* weights, int 
                                   ErrorWord* err, cudaStream_t stream) {
   route_from_ids_kernel<<<1, 32, 0, stream>>>(ids, weights, K, E, route, err);
   return cudaGetLastError();
+}
+
+// The op-level mirrors' error word: one per device, in module memory (zero
+// at load), never cleared by a call, so the first bad index since the last
+// uocr_ops_check stays recorded until that check reads and clears it.
+static __device__ ErrorWord g_ops_error;
+
+cudaError_t ops_error_word(ErrorWord** out) {
+  static std::mutex mu;
+  static ErrorWord* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if ((st = cudaGetSymbolAddress(&p, g_ops_error)) != cudaSuccess) return st;
+    addr[dev] = static_cast<ErrorWord*>(p);
+  }
+  *out = addr[dev];
+  return cudaSuccess;
 }
 
 }  // namespace uocr_b200

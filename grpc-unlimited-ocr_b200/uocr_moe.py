@@ -21,7 +21,6 @@ WEIGHT_BF16, WEIGHT_INT8 = 0, 1
 MEMORY_HOST, MEMORY_DEVICE = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
-PLAN_TENSOR_DECODE = 2
 PLAN_EP_STRIDED = 4
 PLAN_PRE_NORM = 8
 EP_HANDLE_BYTES = 256
@@ -35,7 +34,7 @@ EXPORTS = [
     "uocr_moe_set_layer", "uocr_moe_set_layer_parts", "uocr_checkpoint_open", "uocr_checkpoint_close",
     "uocr_checkpoint_count", "uocr_checkpoint_tensor", "uocr_moe_load_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_moe_ep_handle", "uocr_moe_ep_connect", "uocr_moe_ep_connect_local", "uocr_moe_ep_forward_local",
-    "uocr_expert_topk",
+    "uocr_ops_check", "uocr_expert_topk",
     "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
 ]
 
@@ -113,6 +112,7 @@ def lib() -> ctypes.CDLL:
         L.uocr_moe_ep_connect_local.argtypes = [ctypes.POINTER(vp), i32]
         L.uocr_moe_ep_forward_local.argtypes = [ctypes.POINTER(vp), i32, i64, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                                 ctypes.POINTER(vp), vp]
+        L.uocr_ops_check.argtypes = [vp]
         L.uocr_expert_topk.argtypes = [vp, i64, i64, i64, i32, vp, vp, vp]
         L.uocr_expert_ffn_one.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
         L.uocr_expert_ffn_one_noalloc.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, i64, vp, vp]
@@ -313,6 +313,12 @@ def ep_forward_local(plans: list[Plan], layer: int, xs, ys, stream=None, rows=No
     yarr = (ctypes.c_void_p * n)(*[_ptr(y) for y in ys])
     rarr = (ctypes.c_int64 * n)(*rows)
     _check(lib().uocr_moe_ep_forward_local(parr, n, layer, xarr, rarr, yarr, _stream(stream)))
+
+
+def ops_check(stream=None):
+    """Synchronises the stream and raises UocrError (UOCR_ERR_DEVICE) when an
+    op-level mirror recorded a bad expert id since the last check."""
+    _check(lib().uocr_ops_check(_stream(stream)))
 
 
 def expert_topk(logits, k: int, renormalize: bool, ids, weights, stream=None):

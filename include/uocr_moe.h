@@ -86,15 +86,7 @@ typedef struct uocr_moe_desc {
  * layer. This flag turns the cache off. A stream that is already capturing,
  * or the legacy default stream, always gets plain launches. */
 #define UOCR_PLAN_NO_GRAPHS 1
-/* Decode batches (rows <= 16) stream the selected experts' weights through
- * the CUDA cores by default. This flag runs bf16 decode batches on the
- * tensor cores instead (tcgen05, weights as the 128-row operand, split-K);
- * hidden, expert_ffn and shared_ffn must be multiples of 128, hidden <= 8192,
- * else the flag is ignored. The int8 format always streams, and so does a
- * UOCR_PLAN_PRE_NORM plan. Measured on B200 at the config-1 shapes it is 4-6x
- * slower than the default (2.98 against 0.77 ms per 24-layer step at one
- * row); it is kept as a second implementation the tests compare against. */
-#define UOCR_PLAN_TENSOR_DECODE 2
+/* (Flag bit 2 is unused.) */
 /* Expert parallelism: expert e lives on rank e % ep_world instead of the
  * default contiguous ranges (rank e / (routed_experts / ep_world)). */
 #define UOCR_PLAN_EP_STRIDED 4
@@ -272,6 +264,18 @@ int uocr_moe_ep_forward_local(uocr_moe_plan* const* plans, int32_t n, int64_t la
                               const int64_t* rows, float* const* y, void* stream);
 
 /* ---- Op-level mirrors of the reference's uocr::cuda MoE ops -------------- */
+
+/* Device errors of the op-level mirrors. The reference's kernels index the
+ * stacks with whatever id they are given (gemv_ops.cu:145-169) and surface
+ * only CUDA statuses through check() (src/backend/cuda/context.cu:24-34).
+ * Here uocr_expert_ffn_one, _q8 and _noalloc record an expert id outside
+ * [0, 128) in a per-device error word (that slot then reads expert 0 with
+ * weight 0, so no memory outside the stacks is touched) and still return
+ * UOCR_OK, as they only enqueue work. The word is sticky: the first such
+ * error stays recorded until this call, which synchronises the stream, reads
+ * the current device's word, clears it, and returns UOCR_ERR_DEVICE with the
+ * offending id and position in uocr_last_error() (UOCR_OK when clean). */
+int uocr_ops_check(void* stream);
 
 /* src/backend/cuda/ops.h:80-81 expert_topk: softmax over each row of
  * logits [rows, experts <= 128], then the top k (lower index on a tie) as

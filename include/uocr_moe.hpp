@@ -62,6 +62,10 @@ inline void expert_ffn_one(void* stream, const float* x, std::int64_t hidden, st
   check(uocr_expert_ffn_one(x, hidden, ffn, gate, up, down, ids, weights, k, out, stream));
 }
 
+// Throws std::runtime_error when an op above recorded a bad expert id on the
+// current device since the last call (synchronises the stream).
+inline void ops_check(void* stream) { check(uocr_ops_check(stream)); }
+
 // int8 stacks with one fp32 scale per weight row (the reference's Q8Weights
 // holds one per 32 inputs; uocr_quantize_q8 with group = cols makes these).
 struct Q8Weights {

@@ -1,6 +1,10 @@
-"""The checkpoint side of the decoder MoE path: safetensors shards, the shard
-index, and loading a layer's MoE weights into a plan straight from the mapped
-files (no host-side stacking or widening).
+"""TEST INFRASTRUCTURE: a second, independent reader of the checkpoint
+format in Python — safetensors shards, the shard index, and a layer's MoE
+weights loaded into a plan straight from the mapped files through
+uocr_moe_set_layer_parts — against which the library's own reader
+(uocr_checkpoint_open / uocr_checkpoint_tensor / uocr_moe_load_layer) is
+checked; it also writes the fixture shards the tests use. The product loads
+checkpoints through the library alone.
 
 The readers keep the reference's checks and failure cases:
   * one shard — parse_safetensors_header and SafetensorsFile

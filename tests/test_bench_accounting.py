@@ -34,3 +34,31 @@ def test_traffic_figures_are_read_from_the_profiles():
     t1 = bench.traffic_from_profile("decode_gate_up_bf16_t1.txt")
     assert t1 is not None and abs(t1 - 67_108_864) / 67_108_864 < 0.05  # DRAM bytes ~ algorithmic bytes
     assert bench.traffic_from_profile("no_such_profile.txt") is None
+
+
+def test_route_check_counts_exempt_and_bad_rows():
+    """The bench's ids check against the oracle: the oracle's own ids pass,
+    a swapped pair in a row with a wide margin counts as a mismatch outside
+    the exemption (a mistake planted on the CPU)."""
+    import dataclasses
+
+    import numpy as np
+    import oracle as O
+    cfg = dataclasses.replace(C.CONFIGS[1], hidden=64, experts=8, top_k=2, layers=2)
+    rng = np.random.default_rng(5)
+    inputs, ids = [], []
+    for layer in range(cfg.layers):
+        h = rng.standard_normal((6, cfg.hidden)).astype(np.float32)
+        r = O.round_bf16(O.synth(cfg.seed, layer, O.KIND_ROUTER, 0, cfg.experts * cfg.hidden, 0.02))
+        z = np.zeros
+        w = O.MoeWeights(r.reshape(cfg.experts, cfg.hidden), z((cfg.experts, cfg.hidden), np.float32),
+                         z((cfg.experts, cfg.hidden), np.float32), z((cfg.experts * cfg.hidden, 1), np.float32),
+                         z((0, cfg.hidden), np.float32), z((0, cfg.hidden), np.float32), z((cfg.hidden, 0), np.float32))
+        want = O.moe_forward(w, O.rms_norm(h, None, 1e-6), cfg.top_k, True)
+        inputs.append(h)
+        ids.append(want.ids.copy())
+    ok = bench.route_check(cfg, inputs, ids)
+    assert ok["rows_checked"] == 12 and ok["margin_exempt_rows"] == 0 and ok["mismatched_rows_outside_margin"] == 0
+    ids[1][3] = ids[1][3][::-1].copy()  # order swapped: wrong unless the two logits are within 1e-3
+    bad = bench.route_check(cfg, inputs, ids)
+    assert bad["margin_exempt_rows"] + bad["mismatched_rows_outside_margin"] == 1

@@ -7,7 +7,7 @@ import subprocess
 
 import pytest
 
-import checkpoint as C
+import safetensors_py as C
 import uocr_moe as M
 
 HERE = os.path.dirname(os.path.abspath(__file__))

@@ -8,7 +8,7 @@ import struct
 import numpy as np
 import pytest
 
-import checkpoint as C
+import safetensors_py as C
 
 
 def _raw_shard(path, header: dict | str, data: bytes, hlen: int | None = None):

@@ -10,7 +10,7 @@ checkpoint's pre-norm gain.
 import numpy as np
 import pytest
 
-import checkpoint as C
+import safetensors_py as C
 import uocr_moe as M
 from test_checkpoint import write_moe_checkpoint
 from test_decode_gpu import run_plan
@@ -141,7 +141,7 @@ def test_checkpoint_load_into_expert_parallel_ranks(cuda, tmp_path, strided):
 @pytest.mark.parametrize("fmt,ckpt_dtype", [(M.WEIGHT_BF16, "BF16"), (M.WEIGHT_INT8, "BF16"), (M.WEIGHT_BF16, "F32")])
 def test_native_loader_matches_python_loader(cuda, tmp_path, fmt, ckpt_dtype):
     """uocr_moe_load_layer (the library's own reader and packing) loads what
-    checkpoint.load_moe_layer loads, bit for bit."""
+    safetensors_py.load_moe_layer loads, bit for bit."""
     import torch
     idx, _ = write_moe_checkpoint(tmp_path, LAYERS, H, E, F, S, seed=13, dtype=ckpt_dtype, shards=3)
     dims = M.Dims(H, E, K, F, S, layers=len(LAYERS))

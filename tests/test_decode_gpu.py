@@ -108,14 +108,13 @@ SMALL_SHAPES = [
     (1, 64, 8, 3, 32, 32, True, 0), (5, 128, 16, 1, 48, 0, True, 0), (16, 256, 128, 8, 64, 64, True, 0),
     (3, 96, 12, 4, 32, 48, False, 0), (16, 64, 2, 2, 16, 16, True, 0), (7, 128, 32, 6, 64, 128, True, 1),
     (16, 512, 64, 6, 256, 512, True, 1), (2, 1024, 16, 2, 1536, 2560, True, 0), (9, 2048, 16, 4, 2560, 128, True, 1)]
-# shapes the tensor-core decode takes (hidden, ffn, shared all multiples of 128)
+# hidden, ffn and shared widths that are all multiples of 128
 TC_SHAPES = [(1, 256, 8, 3, 128, 128, True, 0), (5, 128, 128, 8, 128, 0, True, 0),
              (16, 512, 64, 6, 256, 256, False, 0), (11, 384, 24, 5, 384, 128, True, 0)]
 
 
 @pytest.mark.parametrize("T,H,E,K,F,S,renorm,fmt,flags",
-                         [s + (0,) for s in SMALL_SHAPES + TC_SHAPES] + [s + (M.PLAN_TENSOR_DECODE,) for s in TC_SHAPES]
-)
+                         [s + (0,) for s in SMALL_SHAPES + TC_SHAPES])
 def test_small_shapes_against_oracle(cuda, T, H, E, K, F, S, renorm, fmt, flags):
     import torch
     rng = np.random.default_rng(T * 7919 + E)
@@ -231,7 +230,7 @@ def test_pre_norm_against_oracle(cuda, T, H, E, K, F, S, fmt):
 
 
 @pytest.mark.parametrize("T,fmt,flags", [(1, 0, M.PLAN_PRE_NORM), (8, 0, M.PLAN_PRE_NORM), (1, 1, M.PLAN_PRE_NORM),
-                                         (8, 0, M.PLAN_TENSOR_DECODE), (300, 0, M.PLAN_PRE_NORM),
+                                         (8, 0, 0), (300, 0, M.PLAN_PRE_NORM),
                                          (300, 1, M.PLAN_PRE_NORM)])
 def test_checkpoint_dims(cuda, T, fmt, flags):
     """The checkpoint's own MoE shapes (src/weights/architecture.h:21-30:
@@ -282,9 +281,9 @@ def c1_layer(cuda):
     return cfg, t, host_weights(t)
 
 
-# The decode kernel sets: CUDA-core weight streaming (default) and the
-# tensor-core GEMV variant.
-DECODE_PATHS = {"layered": 0, "tensor_cores": M.PLAN_TENSOR_DECODE}
+# The decode kernel set: CUDA-core weight streaming, one PDL-chained launch
+# per phase.
+DECODE_PATHS = {"layered": 0}
 
 
 # 14 and 16 rows: the down kernel's activations no longer all fit in shared
@@ -305,7 +304,7 @@ def test_config1_layer_bf16(cuda, c1_layer, T, path):
     assert err <= BF16_TOL
 
 
-@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
+@pytest.mark.parametrize("path", list(DECODE_PATHS))
 @pytest.mark.parametrize("T", [1, 8, 16])
 def test_config2_layer_int8(cuda, c1_layer, T, path):
     import torch
@@ -327,7 +326,7 @@ def test_config2_layer_int8(cuda, c1_layer, T, path):
     assert err <= INT8_TOL
 
 
-@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
+@pytest.mark.parametrize("path", list(DECODE_PATHS))
 def test_stack_residual_two_layers(cuda, path):
     import torch
     cfg = C.CONFIGS[1]
@@ -381,7 +380,7 @@ def test_pre_norm_stack_two_layers_and_24_stay_finite(cuda):
     assert min(distinct) >= 20  # eight rows with independent routing touch ~35 of 64 experts
 
 
-@pytest.mark.parametrize("path", ["layered", "tensor_cores"])
+@pytest.mark.parametrize("path", list(DECODE_PATHS))
 def test_stack_graph_replay_matches_plain_launches(cuda, path):
     """forward_stack on a capturable stream is captured once (with programmatic
     dependent launches between the kernels) and replayed; the replays give the
@@ -455,6 +454,42 @@ def test_op_mirrors(cuda, c1_layer):
     M.expert_ffn_one_q8(x, H, F, q["gate"], s["gate"], q["up"], s["up"], q["down"], s["down"], ids, wts, K, out8)
     torch.cuda.synchronize()
     assert max_rel(to_np(out8), want) <= INT8_TOL
+
+
+def test_op_mirrors_report_bad_expert_ids(cuda):
+    """An expert id outside [0, 128) given to the expert_ffn_one mirrors is
+    reported by uocr_ops_check as UOCR_ERR_DEVICE (a host-visible status, the
+    word is cleared by the check); the slot adds nothing to the output."""
+    import torch
+    H, F, E, K = 256, 128, 8, 4
+    gate = torch.empty(E * F, H, dtype=torch.bfloat16, device=cuda)
+    up = torch.empty_like(gate)
+    down = torch.empty(E * H, F, dtype=torch.bfloat16, device=cuda)
+    for i, t in enumerate((gate, up, down)):
+        M.synth_fill(t, 31, 0, M.KIND_GATE + i, 0, 0.02)
+    x = torch.empty(1, H, device=cuda)
+    M.synth_fill(x, 31, 0, M.KIND_X, 0, 1.0)
+    w = torch.tensor([[0.4, 0.3, 0.2, 0.1]], device=cuda)
+    M.ops_check()  # clean before the test
+    fns = {"bf16": lambda ids, ww, out: M.expert_ffn_one(x, H, F, gate, up, down, ids, ww, K, out),
+           "noalloc": lambda ids, ww, out: M.expert_ffn_one_noalloc(x, H, F, gate, up, down, ids, ww, K, out)}
+    for name, fn in fns.items():
+        for bad in (200, -1):
+            ids = torch.tensor([[3, bad, 1, 6]], dtype=torch.int64, device=cuda)
+            got = torch.empty(H, device=cuda)
+            fn(ids, w, got)
+            with pytest.raises(M.UocrError) as e:
+                M.ops_check()
+            assert e.value.code == 5, name
+            assert f"expert id {bad} at position 1" in str(e.value), name
+            M.ops_check()  # the check cleared the word
+            ids0 = torch.tensor([[3, 0, 1, 6]], dtype=torch.int64, device=cuda)
+            w0 = w.clone()
+            w0[0, 1] = 0.0
+            want = torch.empty(H, device=cuda)
+            fn(ids0, w0, want)
+            M.ops_check()
+            assert torch.equal(got, want), name
 
 
 def test_forward_errors(cuda):
