@@ -334,6 +334,95 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     return out
 
 
+def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None):
+    """the 24-layer synthetic page decoder (RMSNorm, GQA
+    attention 16 q / 4 kv heads of 128 with RoPE 1e4, the config-1 MoE block,
+    vocab 102400) on one GPU: prefill of 4096 bf16-valued embedding rows, then
+    1024 greedy decode steps, each a replayed CUDA graph. Reports prefill
+    seconds, decode tokens/s, and the end-to-end figure through the public
+    calls with the prompt copied from pinned host memory and the tokens read
+    back inside the timed region."""
+    import torch
+    cfg = C.PAGE_DECODER
+    n = prefill_rows or cfg.prefill_rows
+    steps = steps or cfg.decode_steps
+    dec = M.Decoder(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.vocab, max_positions=n + steps,
+                    max_prefill=n, experts=cfg.experts, top_k=cfg.top_k, ffn=cfg.ffn, shared_ffn=cfg.shared_ffn,
+                    weight_format=M.WEIGHT_INT8 if int8 else M.WEIGHT_BF16, rope_theta=cfg.rope_theta,
+                    rms_norm_eps=cfg.eps, device=dev.index or 0)
+    for layer in range(cfg.layers):
+        t = C.decoder_device_layer(cfg, layer, device=dev)
+        dec.set_layer(layer, t, dtype=M.DTYPE_BF16)
+        del t
+    emb, fnorm, head = C.decoder_device_head(cfg, device=dev)
+    dec.set_head(emb, fnorm, head, dtype=M.DTYPE_BF16)
+    del emb, head
+    torch.cuda.synchronize()
+    wbytes, obytes = dec.bytes()
+    x = C.decoder_prompt(cfg, n, device=dev)
+    toks = torch.empty(steps, dtype=torch.int32, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # warm-up: captures the decode graph
+            dec.prefill(x, stream=stream)
+            dec.decode(8, toks, stream=stream)
+        dec.check(stream=stream)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        dec.prefill(x, stream=stream)
+        ev[1].record(stream)
+        dec.decode(steps, toks, stream=stream)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        dec.check(stream=stream)
+        prefill_ms = ev[0].elapsed_time(ev[1])
+        decode_ms = ev[1].elapsed_time(ev[2])
+        tokens = toks.cpu().numpy()
+        # End to end through the public calls from host memory.
+        x_host = x.cpu().pin_memory()
+        t_host = torch.empty(steps, dtype=torch.int32).pin_memory()
+        xd = torch.empty_like(x)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        xd.copy_(x_host, non_blocking=True)
+        dec.prefill(xd, stream=stream)
+        dec.decode(steps, toks, stream=stream)
+        t_host.copy_(toks, non_blocking=True)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = ev[0].elapsed_time(ev[1])
+    import numpy as np
+    same = bool(np.array_equal(tokens, t_host.numpy()))
+    dec.close()
+    # Bytes a decode step must read: every layer's attention and MoE weights
+    # (the distinct experts of one row: k), the KV cache up to the position,
+    # and the head.
+    H, A, KV = cfg.hidden, cfg.heads * 128, cfg.kv_heads * 128
+    eb = 1 if int8 else 2
+    attn_w = (A + 2 * KV) * H * eb + H * A * eb
+    moe_w = (cfg.top_k * 3 * cfg.ffn * H + 3 * cfg.shared_ffn * H) * eb + cfg.experts * H * 4
+    head_w = cfg.vocab * H * eb
+    mean_pos = n + steps / 2
+    kv_bytes = cfg.layers * mean_pos * 2 * KV * 2
+    step_bytes = cfg.layers * (attn_w + moe_w) + head_w + kv_bytes
+    hbm_peak, peak_kind = measured_peaks()
+    step_s = decode_ms * 1e-3 / steps
+    return {"workload": f"{cfg.name}: {cfg.layers}-layer decoder, GQA {cfg.heads}q/{cfg.kv_heads}kv x 128, "
+                        f"RoPE 1e4, config-1 MoE, vocab {cfg.vocab}; prefill {n} rows then {steps} greedy steps, "
+                        + ("int8 per-channel" if int8 else "bf16") + " weights",
+            "prefill_s": prefill_ms * 1e-3, "prefill_tokens_per_s": n / (prefill_ms * 1e-3),
+            "decode_tokens_per_s": steps / (decode_ms * 1e-3), "decode_ms_per_step": decode_ms / steps,
+            "e2e": {"value": steps / (e2e_ms * 1e-3), "unit": "decode tokens/s (prefill included)",
+                    "seconds": e2e_ms * 1e-3, "h2d_bytes": n * H * 4, "d2h_bytes": steps * 4,
+                    "tokens_equal_device_run": same},
+            "roofline": {"bound": "hbm", "achieved": step_bytes / step_s / 1e9, "peak": hbm_peak,
+                         "peak_source": peak_kind, "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / hbm_peak,
+                         "algorithmic_bytes_per_step": step_bytes,
+                         "note": "weights of every layer (k distinct experts), mean KV read, lm_head"},
+            "device_bytes": {"weights": wbytes, "kv_cache_and_scratch": obytes},
+            "first_tokens": tokens[:8].tolist(), "distinct_tokens": int(len(set(tokens.tolist())))}
+
+
 def run_reference_arm(args, cfg, world, rank):
     """--impl reference: the reference's CPU MoE on the host cores, same metric."""
     if rank != 0:
@@ -501,6 +590,7 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the other named decode configurations (config 1 at batch 4/8, config 2)")
     ap.add_argument("--prefill-rows", type=int, default=None, help="shrink the prefill batch (profiling captures)")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the config-4 page decoder section")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -611,6 +701,11 @@ def main():
                                           check_routes=rank == 0)[0])
         oplan.close()
 
+    page_decode = []
+    if not args.no_decoder and world == 1 and args.layers is None:
+        for int8 in (False, True):
+            page_decode.append(run_page_decode(M, C, dev, stream, int8))
+
     prefill = prefill_int8 = None
     if not args.no_prefill:
         # Expert parallelism (world > 1) assigns expert e to rank e % G: with
@@ -673,6 +768,8 @@ def main():
         }
         if configs:
             line["decode_configs"] = configs
+        if page_decode:
+            line["page_decode"] = page_decode
         if prefill is not None:
             line["prefill"] = prefill
         if prefill_int8 is not None:

@@ -19,6 +19,7 @@
 #include "checkpoint.h"
 #include "ep.h"
 #include "moe_kernels.h"
+#include "plan_internal.h"
 #include "prefill.h"
 
 using namespace uocr_b200;
@@ -1229,3 +1230,8 @@ int uocr_synth_fill(uint64_t seed, uint64_t stream_id, float sigma, int64_t offs
 }
 
 }  // extern "C"
+
+int uocr_b200::moe_layer_inplace(uocr_moe_plan* p, int64_t layer, float* h, int64_t rows, cudaStream_t stream) {
+  if (rows == 0) return UOCR_OK;
+  return run_layer(p, p->layers[static_cast<size_t>(layer)], h, rows, h, h, stream);
+}

@@ -50,6 +50,7 @@ struct KernelArgs {
   void* out_shared;
   int64_t ld_out_shared;
   int shared_out_f32;
+  int shared_accumulate;  // with shared_out_f32: out += A.B^T
   ErrorWord* err;
 };
 
@@ -98,6 +99,17 @@ __device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
   float4* d = reinterpret_cast<float4*>(dst);
 #pragma unroll
   for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// dst += v (each output element belongs to one thread of one tile).
+__device__ __forceinline__ void add_f32x32(float* dst, const float (&v)[32]) {
+  float4* d = reinterpret_cast<float4*>(dst);
+  float4 o[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[q] = d[q];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    d[q] = make_float4(o[q].x + v[4 * q], o[q].y + v[4 * q + 1], o[q].z + v[4 * q + 2], o[q].w + v[4 * q + 3]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __grid_constant__ KernelArgs args) {
@@ -276,7 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
           float v[32];
           tmem_ld32(taddr + c, v);
           if (valid) {
-            if (f32)
+            if (f32 && args.shared_accumulate)
+              add_f32x32(static_cast<float*>(args.out_shared) + out_row * ld + tl.n * kBN + c, v);
+            else if (f32)
               store_f32x32(static_cast<float*>(args.out_shared) + out_row * ld + tl.n * kBN + c, v);
             else
               store_bf16x32(static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared) + out_row * ld +
@@ -377,6 +391,7 @@ cudaError_t launch_grouped_gemm(const GroupedGemm& g, cudaStream_t stream) {
   a.out_shared = g.out_shared;
   a.ld_out_shared = g.ld_out_shared;
   a.shared_out_f32 = g.shared_out_f32 ? 1 : 0;
+  a.shared_accumulate = g.shared_accumulate ? 1 : 0;
   a.err = g.err;
   tc_grouped_gemm_kernel<<<g.blocks, kThreads, grouped_gemm_smem_bytes(), stream>>>(a);
   return cudaGetLastError();

@@ -48,6 +48,7 @@ struct GroupedGemm {
   void* out_shared;
   int64_t ld_out_shared;
   bool shared_out_f32;
+  bool shared_accumulate;  // with shared_out_f32: out_shared += A.B^T (a residual add)
   ErrorWord* err;
   int blocks;  // persistent grid size (the SM count)
 };

@@ -114,3 +114,77 @@ def load_layer(plan: M.Plan, cfg: MoeConfig, layer: int, tensors: dict, plan_lay
                    tensors["down"], tensors.get("shared_gate"), tensors.get("shared_up"), tensors.get("shared_down"),
                    router_bias=tensors.get("router_bias"), memory=M.MEMORY_DEVICE,
                    dtype=M.DTYPE_BF16 if cfg.bf16_values else M.DTYPE_F32)
+
+
+# ---- config 4: the synthetic page decoder around the config-1 MoE ---------
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    seed: int
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    vocab: int
+    experts: int
+    top_k: int
+    ffn: int
+    shared_ffn: int
+    prefill_rows: int
+    decode_steps: int
+    rope_theta: float = 1e4
+    eps: float = 1e-6
+
+
+PAGE_DECODER = DecoderConfig("c4_page_decode", 4, 2048, 24, 16, 4, 102400, 64, 6, 1024, 2048, 4096, 1024)
+
+
+def decoder_device_layer(cfg: DecoderConfig, layer: int, device="cuda"):
+    """One decoder layer generated on the device (the streams the CPU
+    restatement's synth_weights reads): bf16 matrices, fp32 router, unit
+    norm gains."""
+    import torch
+    H, A, KV = cfg.hidden, cfg.heads * 128, cfg.kv_heads * 128
+    E, F, S = cfg.experts, cfg.ffn, cfg.shared_ffn
+    bf = torch.bfloat16
+
+    def mat(kind, idx, rows, cols):
+        t = torch.empty(rows, cols, dtype=bf, device=device)
+        M.synth_fill(t, cfg.seed, layer, kind, idx, 0.02)
+        return t
+    t = {"input_norm": torch.ones(H, device=device), "post_norm": torch.ones(H, device=device),
+         "wq": mat(M.KIND_WQ, 0, A, H), "wk": mat(M.KIND_WK, 0, KV, H), "wv": mat(M.KIND_WV, 0, KV, H),
+         "wo": mat(M.KIND_WO, 0, H, A)}
+    r = torch.empty(E * H, dtype=bf, device=device)
+    M.synth_fill(r, cfg.seed, layer, M.KIND_ROUTER, 0, 0.02)
+    t["router"] = r.float().view(E, H)
+    for name, kind, rows, cols in (("gate", M.KIND_GATE, F, H), ("up", M.KIND_UP, F, H), ("down", M.KIND_DOWN, H, F)):
+        st = torch.empty(E * rows, cols, dtype=bf, device=device)
+        for e in range(E):
+            M.synth_fill(st[e * rows:(e + 1) * rows], cfg.seed, layer, kind, e, 0.02)
+        t[name] = st
+    t["shared_gate"] = mat(M.KIND_SGATE, 0, S, H)
+    t["shared_up"] = mat(M.KIND_SUP, 0, S, H)
+    t["shared_down"] = mat(M.KIND_SDOWN, 0, H, S)
+    return t
+
+
+def decoder_device_head(cfg: DecoderConfig, device="cuda"):
+    """(embed, final_norm, lm_head) on the device; the head tensors use the
+    layer index past the last layer."""
+    import torch
+    top = cfg.layers
+    emb = torch.empty(cfg.vocab, cfg.hidden, dtype=torch.bfloat16, device=device)
+    M.synth_fill(emb, cfg.seed, top, M.KIND_EMBED, 0, 0.02)
+    head = torch.empty(cfg.vocab, cfg.hidden, dtype=torch.bfloat16, device=device)
+    M.synth_fill(head, cfg.seed, top, M.KIND_LM_HEAD, 0, 0.02)
+    return emb, torch.ones(cfg.hidden, device=device), head
+
+
+def decoder_prompt(cfg: DecoderConfig, rows: int, device="cuda"):
+    """rows bf16-valued N(0, 1) embedding rows standing in for image tokens (fp32)."""
+    import torch
+    x = torch.empty(rows, cfg.hidden, dtype=torch.bfloat16, device=device)
+    M.synth_fill(x, cfg.seed, 0, M.KIND_PROMPT, 0, 1.0)
+    return x.float()

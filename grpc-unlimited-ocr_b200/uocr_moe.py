@@ -1,4 +1,5 @@
-"""Python binding of the C ABI in include/uocr_moe.h (ctypes over libuocr_moe.so).
+"""Python binding of the C ABI in include/uocr_moe.h and include/uocr_decoder.h
+(ctypes over libuocr_moe.so).
 
 This is the host-side mirror tests and bench.py call: torch supplies device
 memory and streams; every computation happens in libuocr_moe.so's sm_100a
@@ -27,6 +28,14 @@ EP_HANDLE_BYTES = 256
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).
 KIND_ROUTER, KIND_GATE, KIND_UP, KIND_DOWN, KIND_SGATE, KIND_SUP, KIND_SDOWN, KIND_X = 1, 2, 3, 4, 5, 6, 7, 8
+# ... and the page decoder's tensors (attention, embedding, head, prompt rows, norm gains).
+KIND_WQ, KIND_WK, KIND_WV, KIND_WO, KIND_EMBED, KIND_LM_HEAD, KIND_PROMPT, KIND_NORM = 9, 10, 11, 12, 13, 14, 15, 16
+
+# Every symbol include/uocr_decoder.h declares.
+DECODER_EXPORTS = [
+    "uocr_decoder_create", "uocr_decoder_destroy", "uocr_decoder_bytes", "uocr_decoder_set_layer",
+    "uocr_decoder_set_head", "uocr_decoder_prefill", "uocr_decoder_decode", "uocr_decoder_check",
+]
 
 # Every symbol include/uocr_moe.h declares.
 EXPORTS = [
@@ -85,6 +94,22 @@ class TensorView(ctypes.Structure):
 _lib = None
 
 
+class DecoderDesc(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int64), ("layers", ctypes.c_int64), ("heads", ctypes.c_int64),
+                ("kv_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("vocab", ctypes.c_int64),
+                ("max_positions", ctypes.c_int64), ("max_prefill", ctypes.c_int64),
+                ("routed_experts", ctypes.c_int64), ("experts_per_token", ctypes.c_int64),
+                ("expert_ffn", ctypes.c_int64), ("shared_ffn", ctypes.c_int64), ("rope_theta", ctypes.c_float),
+                ("rms_norm_eps", ctypes.c_float), ("weight_format", ctypes.c_int32), ("renormalize", ctypes.c_int32),
+                ("device", ctypes.c_int32), ("flags", ctypes.c_int32)]
+
+
+class DecoderLayerSrc(ctypes.Structure):
+    _fields_ = [("memory", ctypes.c_int32), ("dtype", ctypes.c_int32)] + [
+        (n, ctypes.c_void_p) for n in ("input_norm", "wq", "wk", "wv", "wo", "post_norm", "router", "gate", "up",
+                                       "down", "shared_gate", "shared_up", "shared_down")]
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -122,6 +147,14 @@ def lib() -> ctypes.CDLL:
         L.uocr_synth_fill.argtypes = [ctypes.c_uint64, ctypes.c_uint64, f32, i64, i64, i32, vp, vp]
         L.uocr_synth_stream.argtypes = [ctypes.c_uint64] * 3
         L.uocr_synth_stream.restype = ctypes.c_uint64
+        L.uocr_decoder_create.argtypes = [ctypes.POINTER(DecoderDesc), ctypes.POINTER(vp)]
+        L.uocr_decoder_destroy.argtypes = [vp]
+        L.uocr_decoder_bytes.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.uocr_decoder_set_layer.argtypes = [vp, i64, ctypes.POINTER(DecoderLayerSrc), vp]
+        L.uocr_decoder_set_head.argtypes = [vp, i32, i32, vp, vp, vp, vp]
+        L.uocr_decoder_prefill.argtypes = [vp, vp, i64, vp, vp, vp]
+        L.uocr_decoder_decode.argtypes = [vp, i64, vp, vp, vp]
+        L.uocr_decoder_check.argtypes = [vp, vp]
         _lib = L
     return _lib
 
@@ -372,3 +405,57 @@ def linear(x, w_bf16, y, bias=None, stream=None):
     m, k = x.shape
     n = w_bf16.shape[0]
     _check(lib().uocr_linear(_ptr(x), m, k, _ptr(w_bf16), n, _ptr(bias), _ptr(y), _stream(stream)))
+
+
+class Decoder:
+    """The page decoder around the MoE (uocr_decoder): attention layers with a
+    bf16 KV cache, the MoE block of every layer, lm_head and greedy tokens."""
+
+    def __init__(self, hidden, layers, heads, kv_heads, vocab, max_positions, max_prefill, experts, top_k, ffn,
+                 shared_ffn, weight_format: int = WEIGHT_BF16, renormalize: bool = True, rope_theta: float = 1e4,
+                 rms_norm_eps: float = 1e-6, device: int = 0):
+        self.desc = DecoderDesc(hidden, layers, heads, kv_heads, 128, vocab, max_positions, max_prefill, experts,
+                                top_k, ffn, shared_ffn, rope_theta, rms_norm_eps, weight_format, int(renormalize),
+                                device, 0)
+        h = ctypes.c_void_p()
+        _check(lib().uocr_decoder_create(ctypes.byref(self.desc), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            lib().uocr_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def bytes(self):
+        w, o = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib().uocr_decoder_bytes(self.h, ctypes.byref(w), ctypes.byref(o)))
+        return w.value, o.value
+
+    def set_layer(self, layer: int, t: dict, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_BF16, stream=None):
+        """t: input_norm, wq, wk, wv, wo, post_norm (fp32 gains), router (fp32)
+        and the MoE stacks gate, up, down, shared_gate, shared_up, shared_down."""
+        src = DecoderLayerSrc(memory, dtype, *[_ptr(t[n]) for n in (
+            "input_norm", "wq", "wk", "wv", "wo", "post_norm", "router", "gate", "up", "down", "shared_gate",
+            "shared_up", "shared_down")])
+        _check(lib().uocr_decoder_set_layer(self.h, layer, ctypes.byref(src), _stream(stream)))
+
+    def set_head(self, embed, final_norm, lm_head, memory: int = MEMORY_DEVICE, dtype: int = DTYPE_BF16,
+                 stream=None):
+        _check(lib().uocr_decoder_set_head(self.h, memory, dtype, _ptr(embed), _ptr(final_norm), _ptr(lm_head),
+                                           _stream(stream)))
+
+    def prefill(self, embeds, logits=None, token=None, stream=None):
+        _check(lib().uocr_decoder_prefill(self.h, _ptr(embeds), embeds.shape[0], _ptr(logits), _ptr(token),
+                                          _stream(stream)))
+
+    def decode(self, steps: int, tokens=None, logits=None, stream=None):
+        _check(lib().uocr_decoder_decode(self.h, steps, _ptr(tokens), _ptr(logits), _stream(stream)))
+
+    def check(self, stream=None):
+        _check(lib().uocr_decoder_check(self.h, _stream(stream)))

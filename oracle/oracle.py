@@ -82,6 +82,13 @@ def ref():
         _ref.ref_get_threads.restype = ctypes.c_uint
         _ref.ref_rms_norm.argtypes = [_f32p, _i64, _i64, _f32p, ctypes.c_float]
         _ref.ref_rms_norm.restype = ctypes.c_int
+        _ref.ref_attention_head.argtypes = [_f32p, _i64, _f32p, _i64, _i64, _f32p, _i64, _f32p, ctypes.c_float,
+                                            _f32p]
+        _ref.ref_attention_head.restype = ctypes.c_int
+        _i64p = ctypes.POINTER(ctypes.c_int64)
+        _ref.ref_page_rope.argtypes = [_f32p, _i64, _i64, _i64, ctypes.c_double, ctypes.c_double, _i64, _i64, _i64p,
+                                       _i64p, _f32p]
+        _ref.ref_page_rope.restype = ctypes.c_int
     return _ref
 
 
@@ -247,3 +254,28 @@ class RefMoe:
 
 def set_ref_threads(n: int) -> None:
     ref().ref_set_threads(n)
+
+
+def ref_attention_head(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """The reference's own attention_head (ops.cpp:219-251), no bias."""
+    q, k, v = _c(q), _c(k), _c(v)
+    out = np.empty((q.shape[0], v.shape[1]), np.float32)
+    if ref().ref_attention_head(_p(q), q.shape[0], _p(k), k.shape[0], q.shape[1], _p(v), v.shape[1], None, scale,
+                                _p(out)) != 0:
+        raise RuntimeError(ref().ref_last_error().decode())
+    return out
+
+
+def ref_page_rope(x: np.ndarray, dim: int, tok_theta: float, page_theta: float, page_pairs: int, page_mod: int,
+                  tok: np.ndarray, page: np.ndarray):
+    """The reference's own PageRope::apply on x [rows, width] in place
+    (page_rope.cpp:8-56); returns (rotated x, its frequency table)."""
+    out = np.array(_c(x), copy=True)
+    inv = np.empty(dim // 2, np.float32)
+    t = np.ascontiguousarray(tok, np.int64)
+    pg = np.ascontiguousarray(page, np.int64)
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    if ref().ref_page_rope(_p(out), out.shape[0], out.shape[1], dim, tok_theta, page_theta, page_pairs, page_mod,
+                           t.ctypes.data_as(i64p), pg.ctypes.data_as(i64p), _p(inv)) != 0:
+        raise RuntimeError(ref().ref_last_error().decode())
+    return out, inv

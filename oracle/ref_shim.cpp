@@ -6,6 +6,7 @@
 //   src/backend/reference/ops.cpp linear/dot (:25-38, :91-109), softmax_rows (:169-187), silu (:163-167),
 //                                 rms_norm (:129-141, the decoder's pre-feed-forward norm)
 //   src/model/weight_source.cpp   TableWeights (:77-83)
+//   src/model/page_rope.cpp       PageRope (:8-56, the decoder's rotate-half rotation)
 //   src/tensor/dtype.cpp
 // The shim only packs caller arrays into a TableWeights under the tensor names
 // the reference reads (src/weights/architecture.cpp:113-117) and calls
@@ -24,6 +25,7 @@
 #include "backend/reference/ops.h"
 #include "backend/reference/parallel.h"
 #include "model/feed_forward.h"
+#include "model/page_rope.h"
 #include "model/weight_source.h"
 #include "weights/architecture.h"
 #include "weights/sharded_weights.h"
@@ -117,6 +119,46 @@ int ref_rms_norm(float* x, std::int64_t rows, std::int64_t cols, const float* we
     uocr::Tensor t = copy_tensor({rows, cols}, x);
     uocr::reference::rms_norm(t, copy_tensor({cols}, weight), eps);
     std::memcpy(x, t.data(), static_cast<std::size_t>(t.numel()) * sizeof(float));
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+// out [lq, dv] = attention_head(q [lq, d], k [lk, d], v [lk, dv], bias [lq, lk]
+// or null, scale): ops.cpp:219-251 unchanged. 0 on success.
+int ref_attention_head(const float* q, std::int64_t lq, const float* k, std::int64_t lk, std::int64_t d,
+                       const float* v, std::int64_t dv, const float* bias, float scale, float* out) {
+  try {
+    const uocr::Tensor tq = copy_tensor({lq, d}, q), tk = copy_tensor({lk, d}, k), tv = copy_tensor({lk, dv}, v);
+    uocr::Tensor tb;
+    if (bias != nullptr) tb = copy_tensor({lq, lk}, bias);
+    const uocr::Tensor o = uocr::reference::attention_head(tq, tk, tv, bias != nullptr ? &tb : nullptr, scale);
+    std::memcpy(out, o.data(), static_cast<std::size_t>(o.numel()) * sizeof(float));
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+// x [rows, width] rotated in place by PageRope(dim, tok_theta, page_theta,
+// page_pairs, page_mod) at coordinates (tok[r], page[r]); also returns the
+// rope's frequency tables (inv_tok then inv_page) in inv. 0 on success.
+int ref_page_rope(float* x, std::int64_t rows, std::int64_t width, std::int64_t dim, double tok_theta,
+                  double page_theta, std::int64_t page_pairs, std::int64_t page_mod, const std::int64_t* tok,
+                  const std::int64_t* page, float* inv) {
+  try {
+    const uocr::PageRope rope(dim, tok_theta, page_theta, page_pairs, page_mod);
+    uocr::Tensor t = copy_tensor({rows, width}, x);
+    std::vector<uocr::RopeCoord> coords(static_cast<std::size_t>(rows));
+    for (std::int64_t r = 0; r < rows; ++r) coords[static_cast<std::size_t>(r)] = {tok[r], page[r]};
+    rope.apply(t, coords);
+    std::memcpy(x, t.data(), static_cast<std::size_t>(t.numel()) * sizeof(float));
+    float* o = inv;
+    for (float f : rope.inv_tok()) *o++ = f;
+    for (float f : rope.inv_page()) *o++ = f;
     return 0;
   } catch (const std::exception& e) {
     g_error = e.what();

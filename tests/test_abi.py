@@ -9,16 +9,22 @@ import pytest
 
 import uocr_moe as M
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "uocr_moe.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADER = os.path.join(INCLUDE, "uocr_moe.h")
+DECODER_HEADER = os.path.join(INCLUDE, "uocr_decoder.h")
 
 
-def declared_symbols():
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\**\s+\**(uocr_[a-z_0-9]+)\s*\(", text, re.M)))
+def declared_symbols(header=None):
+    names = set()
+    for h in ([header] if header else [HEADER, DECODER_HEADER]):
+        text = open(h).read()
+        names |= set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\**\s+\**(uocr_[a-z_0-9]+)\s*\(", text, re.M))
+    return sorted(names)
 
 
 def test_header_and_binding_agree():
-    assert declared_symbols() == sorted(M.EXPORTS)
+    assert declared_symbols(HEADER) == sorted(M.EXPORTS)
+    assert declared_symbols(DECODER_HEADER) == sorted(M.DECODER_EXPORTS)
 
 
 def test_library_exports_every_declared_symbol():
@@ -37,8 +43,9 @@ def test_struct_layouts_match_the_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"uocr_moe_desc": M.MoeDesc, "uocr_moe_layer_src": M.LayerSrc, "uocr_moe_layer_parts": M.LayerParts,
-               "uocr_tensor_view": M.TensorView}
-    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "uocr_moe.h"', "int main(void) {"]
+               "uocr_tensor_view": M.TensorView, "uocr_decoder_desc": M.DecoderDesc,
+               "uocr_decoder_layer_src": M.DecoderLayerSrc}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "uocr_decoder.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
         for field, _ in cls._fields_:
@@ -126,3 +133,30 @@ def test_op_mirror_argument_checks():
 
 def test_synth_stream_layout():
     assert M.synth_stream(3, M.KIND_DOWN, 17) == (3 << 40) | (M.KIND_DOWN << 32) | 17
+
+
+def _ddesc(**kw):
+    d = dict(hidden=512, layers=1, heads=4, kv_heads=1, head_dim=128, vocab=1024, max_positions=64, max_prefill=32,
+             routed_experts=8, experts_per_token=2, expert_ffn=128, shared_ffn=256, rope_theta=1e4,
+             rms_norm_eps=1e-6, weight_format=0, renormalize=1, device=0, flags=0)
+    d.update(kw)
+    return M.DecoderDesc(**d)
+
+
+@pytest.mark.parametrize("bad,code", [(dict(head_dim=64), 2), (dict(heads=3), 1), (dict(kv_heads=3), 1),
+                                      (dict(heads=16, kv_heads=1, hidden=2048), 1), (dict(hidden=384, heads=3), 1),
+                                      (dict(max_positions=32), 1), (dict(vocab=1), 1), (dict(weight_format=2), 1),
+                                      (dict(layers=0), 1), (dict(rope_theta=0.0), 1)])
+def test_decoder_create_rejects_bad_shapes(bad, code):
+    h = ctypes.c_void_p()
+    rc = M.lib().uocr_decoder_create(ctypes.byref(_ddesc(**bad)), ctypes.byref(h))
+    assert rc == code and not h.value
+    assert M.lib().uocr_last_error().decode().startswith("decoder_create")
+
+
+def test_decoder_calls_reject_null_handles():
+    lib = M.lib()
+    assert lib.uocr_decoder_prefill(None, None, 1, None, None, None) == 1
+    assert lib.uocr_decoder_decode(None, 1, None, None, None) == 1
+    assert lib.uocr_decoder_set_layer(None, 0, None, None) == 1
+    assert lib.uocr_decoder_destroy(None) == 0
