@@ -334,7 +334,7 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     return out
 
 
-def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None):
+def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None, layers=None):
     """the 24-layer synthetic page decoder (RMSNorm, GQA
     attention 16 q / 4 kv heads of 128 with RoPE 1e4, the config-1 MoE block,
     vocab 102400) on one GPU: prefill of 4096 bf16-valued embedding rows, then
@@ -342,8 +342,10 @@ def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None):
     seconds, decode tokens/s, and the end-to-end figure through the public
     calls with the prompt copied from pinned host memory and the tokens read
     back inside the timed region."""
+    import dataclasses
+
     import torch
-    cfg = C.PAGE_DECODER
+    cfg = C.PAGE_DECODER if layers is None else dataclasses.replace(C.PAGE_DECODER, layers=layers)
     n = prefill_rows or cfg.prefill_rows
     steps = steps or cfg.decode_steps
     dec = M.Decoder(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.vocab, max_positions=n + steps,
@@ -391,6 +393,12 @@ def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None):
         ev[1].record(stream)
         torch.cuda.synchronize()
         e2e_ms = ev[0].elapsed_time(ev[1])
+        # Per-phase device times over the last positions of the sequence
+        # (plain launches, events between the phases).
+        prof_steps = min(16, steps)
+        dec.prefill(xd, stream=stream)
+        dec.decode(steps - prof_steps, toks, stream=stream)
+        phases = dec.profile_decode(prof_steps, stream=stream)
     import numpy as np
     same = bool(np.array_equal(tokens, t_host.numpy()))
     dec.close()
@@ -419,6 +427,7 @@ def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None):
                          "peak_source": peak_kind, "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / hbm_peak,
                          "algorithmic_bytes_per_step": step_bytes,
                          "note": "weights of every layer (k distinct experts), mean KV read, lm_head"},
+            "phase_ms_per_step": phases,
             "device_bytes": {"weights": wbytes, "kv_cache_and_scratch": obytes},
             "first_tokens": tokens[:8].tolist(), "distinct_tokens": int(len(set(tokens.tolist())))}
 
@@ -591,6 +600,13 @@ def main():
                     help="skip the other named decode configurations (config 1 at batch 4/8, config 2)")
     ap.add_argument("--prefill-rows", type=int, default=None, help="shrink the prefill batch (profiling captures)")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-4 page decoder section")
+    ap.add_argument("--decoder-only", action="store_true",
+                    help="run only the config-4 page decoder section (profiling captures)")
+    ap.add_argument("--decoder-steps", type=int, default=None, help="decode steps of the page decoder section")
+    ap.add_argument("--decoder-prefill", type=int, default=None, help="prefill rows of the page decoder section")
+    ap.add_argument("--decoder-format", default="both", choices=["both", "bf16", "int8"])
+    ap.add_argument("--decoder-layers", type=int, default=None,
+                    help="shrink the page decoder's depth (profiling captures with a few GB on the device)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -621,6 +637,16 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     barrier = (lambda: dist.barrier()) if world > 1 else None
+
+    def page_decode_sections():
+        fmts = {"both": (False, True), "bf16": (False,), "int8": (True,)}[args.decoder_format]
+        return [run_page_decode(M, C, dev, stream, int8, steps=args.decoder_steps, prefill_rows=args.decoder_prefill,
+                                layers=args.decoder_layers) for int8 in fmts]
+
+    if args.decoder_only:
+        stream = torch.cuda.Stream(device=dev)
+        print(json.dumps({"page_decode": page_decode_sections()}), flush=True)
+        return
 
     T = args.batch
     fmt_int8 = args.format == "int8"
@@ -703,8 +729,7 @@ def main():
 
     page_decode = []
     if not args.no_decoder and world == 1 and args.layers is None:
-        for int8 in (False, True):
-            page_decode.append(run_page_decode(M, C, dev, stream, int8))
+        page_decode = page_decode_sections()
 
     prefill = prefill_int8 = None
     if not args.no_prefill:

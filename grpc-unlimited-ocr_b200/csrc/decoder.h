@@ -51,14 +51,17 @@ cudaError_t launch_dec_qkv(const DecShape& s, bool int8, float* x, const __nv_bf
                            DecMatrix wqkv, const float* inv_freq, const DecState* st, float* q_out,
                            __nv_bfloat16* kcache, __nv_bfloat16* vcache, int sm_count, cudaStream_t stream, bool pdl);
 
-// Decode step, layer part 2: split-key GQA attention of q over keys 0..pos;
-// the last block of each key/value head merges its splits into `merged`
-// (bf16 values, fp32 storage). part: [heads][splits][130] floats; counters:
-// [kv], zero between launches (the merging block resets its own).
-size_t dec_attn_smem(const DecShape& s, int splits);
+// Decode step, layer part 2: split-key GQA attention of q over keys 0..pos,
+// one thread-block cluster of `splits` blocks per key/value head; the blocks
+// merge their partials through distributed shared memory into merged
+// ([heads * 128], bf16 values). plan_dec_attn picks the split count (16, or
+// 8 where a 16-block cluster cannot be placed) and whether a split's V rows
+// fit in shared memory; dec_attn_smem is the launch's dynamic shared memory.
+size_t dec_attn_smem(const DecShape& s, int splits, bool v_smem);
+cudaError_t plan_dec_attn(const DecShape& s, int* splits, bool* v_smem);
 cudaError_t launch_dec_attn(const DecShape& s, const float* q, const __nv_bfloat16* kcache,
-                            const __nv_bfloat16* vcache, const DecState* st, float* part, unsigned* counters,
-                            float* merged, int splits, cudaStream_t stream, bool pdl);
+                            const __nv_bfloat16* vcache, const DecState* st, float* merged, int splits, bool v_smem,
+                            cudaStream_t stream, bool pdl);
 
 // Decode step, layer part 3: x += wo . merged.
 cudaError_t launch_dec_oproj(const DecShape& s, bool int8, const float* merged, DecMatrix wo, float* x, int sm_count,

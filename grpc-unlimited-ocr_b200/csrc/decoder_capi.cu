@@ -68,7 +68,8 @@ struct uocr_decoder {
   DecShape shape{};
   bool int8 = false;
   int sm_count = 1;
-  int splits = 1;
+  int splits = 1;        // attention blocks (one cluster) per key/value head
+  bool v_smem = true;    // the attention keeps a split's V rows in shared memory
   int64_t qkv_rows = 0;  // (heads + 2 kv) * 128
   uocr_moe_plan* moe = nullptr;
   std::vector<DecLayer> layers;
@@ -84,9 +85,8 @@ struct uocr_decoder {
   size_t weight_bytes = 0;
   float* x = nullptr;             // [max_prefill, H] residual stream (a decode step uses row 0)
   float* q = nullptr;             // [heads * 128]
-  float* part = nullptr;          // [heads][splits][130]
-  unsigned* counters = nullptr;   // [kv] attention tickets, then the lm_head ticket
-  float* merged = nullptr;        // [heads * 128]
+  float* merged = nullptr;        // [heads * 128] attention output (bf16 values)
+  unsigned* counters = nullptr;   // the lm_head's ticket
   int2* lm_part = nullptr;        // [sm_count]
   float* logits = nullptr;        // [vocab]
   DecState* state = nullptr;
@@ -199,25 +199,39 @@ const __nv_bfloat16* gemm_operand(const uocr_decoder* p, const void* w, const fl
 }
 
 // One decode step: every layer (norm + q/k/v + RoPE + cache, attention,
-// output projection, the MoE block) and the head with the greedy choice.
-int decode_step(uocr_decoder* p, cudaStream_t stream) {
+// output projection, the MoE block) and the head with the greedy choice. For
+// measurement, ev (kProfilePhases + 1 events per layer slot) receives an event
+// before the first kernel and after each phase, and the launches are plain
+// (no programmatic overlap) so that the events bracket each phase.
+constexpr int kProfilePhases = 4;  // q/k/v, attention, output projection, MoE block
+
+int decode_step(uocr_decoder* p, cudaStream_t stream, cudaEvent_t* ev = nullptr) {
   const DecShape& s = p->shape;
-  const bool pdl = true;
+  const bool pdl = ev == nullptr;
+  auto mark = [&](int64_t l, int k) -> cudaError_t {
+    return ev != nullptr ? cudaEventRecord(ev[l * (kProfilePhases + 1) + k], stream) : cudaSuccess;
+  };
   for (int64_t l = 0; l < p->d.layers; ++l) {
     const DecLayer& L = p->layers[static_cast<size_t>(l)];
+    DEC_TRY(mark(l, 0), "decode: event");
     DEC_TRY(launch_dec_qkv(s, p->int8, p->x, l == 0 ? p->embed : nullptr, L.input_norm, DecMatrix{L.wqkv, L.wqkv_s},
                            p->inv_freq, p->state, p->q, kc_of(p, l), vc_of(p, l), p->sm_count, stream, pdl),
             "decode: q/k/v");
-    DEC_TRY(launch_dec_attn(s, p->q, kc_of(p, l), vc_of(p, l), p->state, p->part, p->counters, p->merged, p->splits,
-                            stream, pdl),
+    DEC_TRY(mark(l, 1), "decode: event");
+    DEC_TRY(launch_dec_attn(s, p->q, kc_of(p, l), vc_of(p, l), p->state, p->merged, p->splits, p->v_smem, stream,
+                            pdl),
             "decode: attention");
+    DEC_TRY(mark(l, 2), "decode: event");
     DEC_TRY(launch_dec_oproj(s, p->int8, p->merged, DecMatrix{L.wo, L.wo_s}, p->x, p->sm_count, stream, pdl),
             "decode: output projection");
+    DEC_TRY(mark(l, 3), "decode: event");
     DEC_RC(moe_layer_inplace(p->moe, l, p->x, 1, stream));
+    DEC_TRY(mark(l, 4), "decode: event");
   }
   DEC_TRY(launch_dec_lmhead(s, p->int8, p->x, p->final_norm, DecMatrix{p->lm_head, p->lm_head_s}, p->logits, p->state,
-                            p->lm_part, p->counters + p->d.kv_heads, p->tokens, 1, 0, p->sm_count, stream, pdl),
+                            p->lm_part, p->counters, p->tokens, 1, 0, p->sm_count, stream, pdl),
           "decode: lm_head");
+  if (ev != nullptr) DEC_TRY(cudaEventRecord(ev[p->d.layers * (kProfilePhases + 1)], stream), "decode: event");
   return UOCR_OK;
 }
 
@@ -256,14 +270,12 @@ int uocr_decoder_create(const uocr_decoder_desc* desc, uocr_decoder** out) {
   int sms = 0;
   cudaError_t st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.device);
   if (st == cudaSuccess) st = prepare_decoder_kernels();
+  if (st == cudaSuccess) st = plan_dec_attn(p->shape, &p->splits, &p->v_smem);
   if (st != cudaSuccess) {
     delete p;
     return dcuda(st, "decoder_create: device set-up");
   }
   p->sm_count = sms > 0 ? sms : 1;
-  // Two blocks per SM over the key/value heads.
-  p->splits = static_cast<int>(std::max<int64_t>(1, (2 * p->sm_count + d.kv_heads - 1) / d.kv_heads));
-  if (p->splits > d.max_positions) p->splits = static_cast<int>(d.max_positions);
 
   uocr_moe_desc md{};
   md.hidden = d.hidden;
@@ -330,9 +342,8 @@ int uocr_decoder_create(const uocr_decoder_desc* desc, uocr_decoder** out) {
   const size_t sizes[] = {
       static_cast<size_t>(R * H) * 4,                                     // x
       static_cast<size_t>(A) * 4,                                         // q
-      static_cast<size_t>(d.heads) * p->splits * (kDecHeadDim + 2) * 4,  // part
-      static_cast<size_t>(d.kv_heads + 1) * 4,                            // counters
       static_cast<size_t>(A) * 4,                                         // merged
+      static_cast<size_t>(4),                                             // counters
       static_cast<size_t>(p->sm_count) * 8,                               // lm_part
       static_cast<size_t>(d.vocab) * 4,                                   // logits
       sizeof(DecState),                                                   // state
@@ -364,9 +375,8 @@ int uocr_decoder_create(const uocr_decoder_desc* desc, uocr_decoder** out) {
     };
     take(reinterpret_cast<void**>(&p->x));
     take(reinterpret_cast<void**>(&p->q));
-    take(reinterpret_cast<void**>(&p->part));
-    take(reinterpret_cast<void**>(&p->counters));
     take(reinterpret_cast<void**>(&p->merged));
+    take(reinterpret_cast<void**>(&p->counters));
     take(reinterpret_cast<void**>(&p->lm_part));
     take(reinterpret_cast<void**>(&p->logits));
     take(reinterpret_cast<void**>(&p->state));
@@ -504,7 +514,7 @@ int uocr_decoder_prefill(uocr_decoder* p, const float* embeds, int64_t rows, flo
     DEC_RC(moe_layer_inplace(p->moe, l, p->x, rows, stream));
   }
   DEC_TRY(launch_dec_lmhead(s, p->int8, p->x + (rows - 1) * H, p->final_norm, DecMatrix{p->lm_head, p->lm_head_s},
-                            p->logits, p->state, p->lm_part, p->counters + p->d.kv_heads, p->tokens, 0,
+                            p->logits, p->state, p->lm_part, p->counters, p->tokens, 0,
                             static_cast<int>(rows), p->sm_count, stream, false),
           "decoder_prefill: lm_head");
   if (logits != nullptr)
@@ -562,6 +572,46 @@ int uocr_decoder_decode(uocr_decoder* p, int64_t steps, int32_t* tokens, float* 
     DEC_TRY(cudaMemcpyAsync(tokens, p->tokens + p->generated, static_cast<size_t>(steps) * 4,
                             cudaMemcpyDeviceToDevice, stream),
             "decoder_decode: token copy");
+  p->length += steps;
+  p->generated += steps;
+  return UOCR_OK;
+}
+
+int uocr_decoder_profile_decode(uocr_decoder* p, int64_t steps, float* ms, void* stream_v) {
+  if (p == nullptr || ms == nullptr || steps <= 0)
+    return dfail(UOCR_ERR_INVALID_ARGUMENT, "decoder_profile_decode: bad argument");
+  if (!p->started) return dfail(UOCR_ERR_INVALID_ARGUMENT, "decoder_profile_decode: no prefill started a sequence");
+  if (p->length + steps > p->d.max_positions)
+    return dfail(UOCR_ERR_INVALID_ARGUMENT, "decoder_profile_decode: the sequence would pass max_positions");
+  Guard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const size_t nev = static_cast<size_t>(p->d.layers * (kProfilePhases + 1) + 1);
+  std::vector<cudaEvent_t> ev(nev, nullptr);
+  int rc = UOCR_OK;
+  for (auto& e : ev)
+    if (cudaEventCreate(&e) != cudaSuccess) rc = dfail(UOCR_ERR_CUDA, "decoder_profile_decode: event");
+  double acc[kProfilePhases + 1] = {};
+  for (int64_t i = 0; i < steps && rc == UOCR_OK; ++i) {
+    rc = decode_step(p, stream, ev.data());
+    if (rc != UOCR_OK) break;
+    if (cudaEventSynchronize(ev[nev - 1]) != cudaSuccess) {
+      rc = dfail(UOCR_ERR_CUDA, "decoder_profile_decode: synchronise");
+      break;
+    }
+    for (int64_t l = 0; l < p->d.layers; ++l)
+      for (int k = 0; k < kProfilePhases; ++k) {
+        float t = 0.0f;
+        cudaEventElapsedTime(&t, ev[l * (kProfilePhases + 1) + k], ev[l * (kProfilePhases + 1) + k + 1]);
+        acc[k] += t;
+      }
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, ev[(p->d.layers - 1) * (kProfilePhases + 1) + kProfilePhases], ev[nev - 1]);
+    acc[kProfilePhases] += t;
+  }
+  for (auto& e : ev)
+    if (e != nullptr) cudaEventDestroy(e);
+  if (rc != UOCR_OK) return rc;
+  for (int k = 0; k <= kProfilePhases; ++k) ms[k] = static_cast<float>(acc[k] / static_cast<double>(steps));
   p->length += steps;
   p->generated += steps;
   return UOCR_OK;

@@ -34,7 +34,8 @@ KIND_WQ, KIND_WK, KIND_WV, KIND_WO, KIND_EMBED, KIND_LM_HEAD, KIND_PROMPT, KIND_
 # Every symbol include/uocr_decoder.h declares.
 DECODER_EXPORTS = [
     "uocr_decoder_create", "uocr_decoder_destroy", "uocr_decoder_bytes", "uocr_decoder_set_layer",
-    "uocr_decoder_set_head", "uocr_decoder_prefill", "uocr_decoder_decode", "uocr_decoder_check",
+    "uocr_decoder_set_head", "uocr_decoder_prefill", "uocr_decoder_decode", "uocr_decoder_profile_decode",
+    "uocr_decoder_check",
 ]
 
 # Every symbol include/uocr_moe.h declares.
@@ -155,6 +156,7 @@ def lib() -> ctypes.CDLL:
         L.uocr_decoder_prefill.argtypes = [vp, vp, i64, vp, vp, vp]
         L.uocr_decoder_decode.argtypes = [vp, i64, vp, vp, vp]
         L.uocr_decoder_check.argtypes = [vp, vp]
+        L.uocr_decoder_profile_decode.argtypes = [vp, i64, ctypes.POINTER(f32), vp]
         _lib = L
     return _lib
 
@@ -459,3 +461,9 @@ class Decoder:
 
     def check(self, stream=None):
         _check(lib().uocr_decoder_check(self.h, _stream(stream)))
+
+    def profile_decode(self, steps: int, stream=None) -> dict:
+        """Mean ms per step of each phase (plain launches, events between)."""
+        ms = (ctypes.c_float * 5)()
+        _check(lib().uocr_decoder_profile_decode(self.h, steps, ms, _stream(stream)))
+        return dict(zip(("qkv", "attention", "out_proj", "moe", "lm_head"), [round(v, 5) for v in ms]))

@@ -16,7 +16,8 @@
  *
  * Conventions are uocr_moe.h's: plain pointers, a cudaStream_t passed as
  * void*, status codes with uocr_last_error(), nothing synchronises the stream
- * except uocr_decoder_check.
+ * except uocr_decoder_check and the measurement call
+ * uocr_decoder_profile_decode.
  */
 #ifndef UOCR_DECODER_H
 #define UOCR_DECODER_H
@@ -97,6 +98,12 @@ int uocr_decoder_prefill(uocr_decoder* dec, const float* embeds, int64_t rows, f
  * launches on a capturing or legacy stream). UOCR_ERR_INVALID_ARGUMENT when
  * the sequence would pass max_positions or no prefill started it. */
 int uocr_decoder_decode(uocr_decoder* dec, int64_t steps, int32_t* tokens, float* logits, void* stream);
+/* Measurement: `steps` decode steps with plain launches and events between
+ * the phases (synchronises after each step); ms[0..4] receive the mean time
+ * per step of the q/k/v kernels, attention, the output projections, the MoE
+ * blocks (all layers summed) and lm_head. Advances the sequence like
+ * uocr_decoder_decode. */
+int uocr_decoder_profile_decode(uocr_decoder* dec, int64_t steps, float* ms, void* stream);
 /* Synchronises the stream and reports device errors recorded by the
  * decoder's kernels or its MoE block (UOCR_ERR_DEVICE / UOCR_ERR_TIMEOUT). */
 int uocr_decoder_check(uocr_decoder* dec, void* stream);

@@ -68,13 +68,18 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda):
     x0, ids0, w0 = inputs[0]
     M.expert_ffn_one_noalloc(x0, H, F, gate, up, down, ids0, w0, K, warm)
     torch.cuda.synchronize()
+    # Nothing may be allocated across the two calls: the device's free bytes
+    # and torch's allocated bytes must not grow (a collection of other
+    # tests' garbage may shrink the latter meanwhile).
+    import gc
+    gc.collect()
     free_before = torch.cuda.mem_get_info()[0]
     torch_before = torch.cuda.memory_allocated()
     for (x, ids, w), got in zip(inputs, outs):
         M.expert_ffn_one_noalloc(x, H, F, gate, up, down, ids, w, K, got)
     torch.cuda.synchronize()
     assert torch.cuda.mem_get_info()[0] >= free_before
-    assert torch.cuda.memory_allocated() == torch_before
+    assert torch.cuda.memory_allocated() <= torch_before
     M.ops_check()
     for got, want in zip(outs, wants):
         assert torch.equal(got, want)
