@@ -199,35 +199,57 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0, strided=False,
+def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=None, world=1, rank=0, placement="",
                 int8=False):
     """one MoE layer over 32768 rows (8 pages x 4096),
     Zipf-skewed router bias; tokens/s of the layer, per-kernel times, and the
     gate/up GEMM against the bf16 tensor roofline. With world > 1 the layer
-    runs expert-parallel: each rank holds 64 / world experts and 32768 / world
-    rows (strong scaling), and the time is the max over ranks. `rows` shrinks
-    the batch (profiling captures only); `strided` assigns expert e to rank
-    e % world instead of contiguous ranges. `int8` (one GPU) quantises the
-    layer per output channel; the prefill path then expands it to bf16 per
-    layer before the GEMMs (the expansion is timed inside the router's
-    interval of kernel_ms)."""
+    runs expert-parallel: each rank holds its share of the experts and
+    32768 / world rows (strong scaling), and the time is the max over ranks.
+    `placement` (world > 1): "balanced" = an owner table from the routing
+    histogram of a calibration pass (ep.balanced_owner_table: hot experts
+    replicated, longest-processing-time assignment), "contiguous" = ranges
+    e // (E / G) as the north star names them, "strided" = e % G. The
+    calibration pass is this rank's rows through a one-GPU plan, which also
+    gives the reference output the expert-parallel rows must equal bit for
+    bit. `rows` shrinks the batch (profiling captures only). `int8` (one
+    GPU) quantises the layer per output channel; the prefill path then expands
+    it to bf16 per layer before the GEMMs (the expansion is timed inside the
+    router's interval of kernel_ms)."""
     import torch
     cfg = C.CONFIGS[3]
     total = rows or cfg.rows[0]
     import ep
     start, T = ep.rows_of(total, world, rank)
-    plan = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0,
-                  weight_format=M.WEIGHT_INT8 if int8 else M.WEIGHT_BF16,
-                  ep_world=world if world > 1 else 0, ep_rank=rank, flags=M.PLAN_EP_STRIDED if strided else 0)
+    E = cfg.experts
     t = C.device_layer(cfg, 0, device=dev)
-    C.load_layer(plan, cfg, 0, t)
-    if world > 1:
-        ep.connect(plan)
     x = C.device_input(cfg, total, device=dev)[start:start + T].contiguous()
     y = torch.empty_like(x)
     ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
+    owner, cbs, y1 = None, None, None
     if world > 1:
         import torch.distributed as dist
+        # Calibration and reference: this rank's rows through a one-GPU plan.
+        single = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0)
+        C.load_layer(single, cfg, 0, t)
+        y1 = torch.empty_like(x)
+        with torch.cuda.stream(stream):
+            single.forward(0, x, y1, ids, stream=stream)
+            single.check(stream=stream)
+        torch.cuda.synchronize()
+        single.close()
+        mine = torch.bincount(ids.view(-1).long(), minlength=E).to(torch.int64)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        cbs = [g.cpu().tolist() for g in gathered]
+        owner = ep.balanced_owner_table(cbs, world) if placement == "balanced" else \
+            ep.owner_table(E, world, placement == "strided")
+    plan = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0,
+                  weight_format=M.WEIGHT_INT8 if int8 else M.WEIGHT_BF16,
+                  ep_world=world if world > 1 else 0, ep_rank=rank, ep_owner=owner)
+    C.load_layer(plan, cfg, 0, t)
+    if world > 1:
+        ep.connect(plan)
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             plan.forward(0, x, y, ids, stream=stream)
@@ -249,23 +271,23 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         prof = plan.profile_stack(h, iters=3, stream=stream)
         plan.check(stream=stream)
     ep_equal = None
+    H, F, S = cfg.hidden, cfg.ffn, cfg.shared_ffn
     if world > 1:
-        # The same rows through a one-GPU plan on this rank: the expert-parallel
-        # output must equal it bit for bit (an output row depends on its own
-        # input row only, and the combine order is the same).
-        single = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0)
-        C.load_layer(single, cfg, 0, t)
-        y1 = torch.empty_like(x)
-        with torch.cuda.stream(stream):
-            single.forward(0, x, y1, stream=stream)
-            single.check(stream=stream)
-        torch.cuda.synchronize()
         eq = torch.tensor([1 if torch.equal(y, y1) else 0], dtype=torch.int32, device=dev)
         dist.all_reduce(eq, op=dist.ReduceOp.MIN)
         ep_equal = bool(eq.item())
-        single.close()
         del y1
-    counts_t = torch.bincount(ids.view(-1).long(), minlength=cfg.experts)
+        # Bytes this rank moves over NVLink: the rows it pulls from other
+        # ranks for its experts, and the expert outputs its combine pulls
+        # from other owners (bf16 rows of H).
+        pulled = sum(cbs[s][e] for e in range(E) for s in range(world)
+                     if owner[e * world + s] == rank and s != rank) * H * 2
+        combined = sum(cbs[rank][e] for e in range(E) if owner[e * world + rank] != rank) * H * 2
+        link = torch.tensor([pulled, prof["pull"], combined, prof["combine"]], dtype=torch.float64, device=dev)
+        links = [torch.empty_like(link) for _ in range(world)]
+        dist.all_gather(links, link)
+        links = [v.cpu().tolist() for v in links]
+    counts_t = torch.bincount(ids.view(-1).long(), minlength=E)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(counts_t)
@@ -273,7 +295,6 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         dist.barrier()
     ms = float(ms_t[0])
     counts = counts_t.cpu().tolist()
-    H, F, S = cfg.hidden, cfg.ffn, cfg.shared_ffn
     R = total * cfg.top_k
     gu_flops = R * 4 * F * H + total * 4 * S * H
     dn_flops = R * 2 * F * H + total * 2 * S * H
@@ -298,16 +319,27 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
                            "algorithmic_flops_per_layer": total_flops}
     else:
         per_gpu = total_flops / (ms * 1e-3) / 1e12 / world
-        owner_rows = [sum(counts[e] for e in ep.local_experts(r, cfg.experts, world, strided)) for r in range(world)]
-        out["parallelism"] = f"expert-parallel x{world}: {cfg.experts // world} experts " \
-                             f"({'e % G' if strided else 'contiguous ranges'}) and {total // world} rows per GPU; " \
-                             "rows and outputs pulled over NVLink by peer loads"
+        owner_rows = ep.rows_received(owner, cbs, E, world)
+        slots = [len(ep.slots_of(owner, E, world, d)) for d in range(world)]
+        desc = {"balanced": "load-balanced owner table (hot experts replicated)",
+                "strided": "e % G", "contiguous": "contiguous ranges e // (E / G)"}[placement]
+        out["parallelism"] = f"expert-parallel x{world}: {desc}, {min(slots)}-{max(slots)} experts and " \
+                             f"{total // world} rows per GPU; rows and outputs pulled over NVLink by peer loads"
         out["roofline"] = {"bound": "tensor", "kernel": "whole layer per GPU", "achieved": per_gpu, "peak": peak,
                            "peak_source": peak_src, "unit": "TFLOP/s", "frac": per_gpu / peak,
                            "algorithmic_flops_per_layer": total_flops}
         out["rows_received_per_rank"] = owner_rows
         out["rows_received_max_over_mean"] = max(owner_rows) / (sum(owner_rows) / world)
+        out["experts_per_rank"] = slots
         out["ep_bitwise_equal"] = ep_equal
+        # NVLink: bytes each rank pulls / its pull (or combine) kernel time.
+        out["nvlink"] = {
+            "pull_gbs_per_rank": [round(v[0] / (v[1] * 1e-3) / 1e9, 1) if v[1] > 0 else None for v in links],
+            "combine_gbs_per_rank": [round(v[2] / (v[3] * 1e-3) / 1e9, 1) if v[3] > 0 else None for v in links],
+            "pull_bytes_per_rank": [int(v[0]) for v in links], "combine_bytes_per_rank": [int(v[2]) for v in links],
+            "note": "bytes crossing NVLink (rows from or to other ranks only) / the kernel's device time "
+                    "(the combine's time includes its HBM traffic); peer copy measured on this pool: 770 GB/s per "
+                    "direction"}
     if world == 1 and rank == 0:
         out["ids_check"] = route_check(cfg, [x.cpu().numpy()], [ids.cpu().numpy()], norm=False,
                                        bias=t["router_bias"].cpu().numpy())
@@ -733,18 +765,20 @@ def main():
 
     prefill = prefill_int8 = None
     if not args.no_prefill:
-        # Expert parallelism (world > 1) assigns expert e to rank e % G: with
-        # the Zipf-skewed router that spreads the hot experts over the ranks.
-        # Contiguous ranges (rank e // (E / G)) are measured beside it.
+        # Expert parallelism (world > 1) places the experts from a calibration
+        # histogram (hot experts replicated, load-balanced); the contiguous
+        # ranges the north star names and the strided map are measured beside it.
         prefill = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=min(10.0, args.cpu_budget),
                               want_cpu=not args.no_cpu_baseline and world == 1 and rank == 0,
-                              rows=args.prefill_rows, world=world, rank=rank, strided=world > 1)
+                              rows=args.prefill_rows, world=world, rank=rank,
+                              placement="balanced" if world > 1 else "")
         if world > 1:
-            alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
-                              rows=args.prefill_rows, world=world, rank=rank, strided=False)
-            prefill["contiguous_experts"] = {k: alt[k] for k in ("value", "ms_per_layer", "kernel_ms",
-                                                               "rows_received_per_rank", "parallelism",
-                                                               "ep_bitwise_equal")}
+            for alt_map in ("contiguous", "strided"):
+                alt = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
+                                  rows=args.prefill_rows, world=world, rank=rank, placement=alt_map)
+                prefill[f"{alt_map}_experts"] = {k: alt[k] for k in (
+                    "value", "ms_per_layer", "kernel_ms", "rows_received_per_rank", "rows_received_max_over_mean",
+                    "parallelism", "ep_bitwise_equal")}
         elif sub_configs:
             prefill_int8 = run_prefill(M, C, dev, stream, steps=10, warmup=3, cpu_budget=0, want_cpu=False,
                                        rows=args.prefill_rows, int8=True)

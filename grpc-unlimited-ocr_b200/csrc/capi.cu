@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/uocr_moe.h"
@@ -126,6 +127,7 @@ struct uocr_moe_plan {
   // Expert parallelism (ep_world > 1): this rank's exchange region, the peers'
   // (IPC mappings, closed on destroy) and the EP scratch in the arena.
   bool ep = false;
+  EpTables etab;  // host copy of the placement tables
   EpMap emap{};
   EpLayout elay{};
   EpScratch escr{};
@@ -152,6 +154,10 @@ struct uocr_moe_plan {
 
   // Routed experts whose weights this plan holds (its own under expert parallelism).
   int64_t held_experts() const { return ep ? emap.local : d.routed_experts; }
+  // Global id of held expert i (slot i under expert parallelism).
+  int64_t held_expert(int64_t i) const {
+    return ep ? etab.slot_expert[static_cast<size_t>(emap.rank) * etab.max_local + static_cast<size_t>(i)] : i;
+  }
 
   void carve_layer(Carver& c, LayerDev& L) const {
     const size_t H = d.hidden, F = d.expert_ffn, S = d.shared_ffn, eb = elem_bytes();
@@ -197,6 +203,9 @@ struct uocr_moe_plan {
     if (ep) {
       char* base = c.take<char>(ep_scratch_bytes(pdims, elay, emap));
       carve_ep_scratch(pdims, elay, emap, base, &escr);
+      emap.owner = c.take<int>(etab.owner.size());
+      emap.slot = c.take<int>(etab.slot.size());
+      emap.slot_expert = c.take<int>(etab.slot_expert.size());
     }
   }
 };
@@ -272,13 +281,18 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   if (ep) {
     if (d.ep_rank < 0 || d.ep_rank >= d.ep_world)
       return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: ep_rank must be in [0, ep_world)");
-    if (d.routed_experts % d.ep_world != 0)
-      return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: routed_experts must be a multiple of ep_world");
     if (d.weight_format != UOCR_WEIGHT_BF16 ||
         !prefill_shapes_ok(static_cast<int>(d.hidden), static_cast<int>(d.expert_ffn), static_cast<int>(d.shared_ffn)))
       return fail(UOCR_ERR_UNSUPPORTED,
                   "plan_create: expert parallelism runs the prefill path: bf16 weights, hidden % 256 == 0, "
                   "expert_ffn and shared_ffn % 128 == 0");
+  }
+  EpTables tabs;
+  if (ep) {
+    std::string why;
+    if (!build_ep_tables(static_cast<int>(d.routed_experts), d.ep_world, d.ep_owner,
+                         (d.flags & UOCR_PLAN_EP_STRIDED) != 0, &tabs, &why))
+      return fail(UOCR_ERR_INVALID_ARGUMENT, "plan_create: expert placement: " + why);
   }
   int ndev = 0;
   UOCR_TRY(cudaGetDeviceCount(&ndev), "plan_create: cudaGetDeviceCount");
@@ -318,8 +332,9 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   if (ep) {
     p->ep = true;
     const int W = d.ep_world;
-    p->emap = EpMap{W, d.ep_rank, static_cast<int>(d.routed_experts), static_cast<int>(d.routed_experts) / W,
-                    (d.flags & UOCR_PLAN_EP_STRIDED) != 0 ? 1 : 0};
+    p->etab = std::move(tabs);
+    p->emap = EpMap{W, d.ep_rank, static_cast<int>(d.routed_experts),
+                    p->etab.slot_count[static_cast<size_t>(d.ep_rank)], p->etab.max_local, nullptr, nullptr, nullptr};
     p->elay = ep_layout(p->pdims, p->emap);
     if (const char* v = std::getenv("UOCR_EP_WAIT_MS")) {
       const long long ms = std::atoll(v);
@@ -354,6 +369,15 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
   Carver ac{p->arena};
   p->carve_arena(ac);
   st = cudaMemset(p->arena, 0, p->arena_bytes);
+  if (st == cudaSuccess && p->ep) {
+    const EpTables& t = p->etab;
+    st = cudaMemcpy(const_cast<int*>(p->emap.owner), t.owner.data(), t.owner.size() * 4, cudaMemcpyHostToDevice);
+    if (st == cudaSuccess)
+      st = cudaMemcpy(const_cast<int*>(p->emap.slot), t.slot.data(), t.slot.size() * 4, cudaMemcpyHostToDevice);
+    if (st == cudaSuccess)
+      st = cudaMemcpy(const_cast<int*>(p->emap.slot_expert), t.slot_expert.data(), t.slot_expert.size() * 4,
+                      cudaMemcpyHostToDevice);
+  }
   if (st != cudaSuccess) {
     uocr_moe_plan_destroy(p);
     return cuda_fail(st, "plan_create: arena clear");
@@ -476,7 +500,7 @@ int uocr_moe_set_layer(uocr_moe_plan* p, int64_t layer, const uocr_moe_layer_src
       return base == nullptr ? nullptr : static_cast<const char*>(base) + bytes;
     };
     for (int i = 0; i < p->emap.local && rc == UOCR_OK; ++i) {
-      const int64_t e = p->emap.global(p->emap.rank, i);
+      const int64_t e = p->held_expert(i);
       char* g = static_cast<char*>(L.gate) + static_cast<size_t>(i * F * H) * eb;
       char* u = static_cast<char*>(L.up) + static_cast<size_t>(i * F * H) * eb;
       char* dn = static_cast<char*>(L.down) + static_cast<size_t>(i * H * F) * eb;
@@ -562,7 +586,7 @@ int uocr_moe_set_layer_parts(uocr_moe_plan* p, int64_t layer, const uocr_moe_lay
   // parallelism); its rows go to row block i of the stacks.
   const size_t eb = p->elem_bytes();
   for (int64_t i = 0; i < p->held_experts() && rc == UOCR_OK; ++i) {
-    const int64_t e = p->ep ? p->emap.global(p->emap.rank, static_cast<int>(i)) : i;
+    const int64_t e = p->held_expert(i);
     char* g = static_cast<char*>(L.gate) + static_cast<size_t>(i * F * H) * eb;
     char* u = static_cast<char*>(L.up) + static_cast<size_t>(i * F * H) * eb;
     char* dn = static_cast<char*>(L.down) + static_cast<size_t>(i * H * F) * eb;
@@ -705,7 +729,7 @@ int run_layer(uocr_moe_plan* p, const LayerDev& L, const float* x, int64_t rows,
   if (p->ep) {
     EpCall c = ep_call(p, L, x, rows, resid, y);
     UOCR_TRY(ep_forward(c, stream, ev), "forward: expert-parallel prefill");
-    if (nev != nullptr) *nev = 5;
+    if (nev != nullptr) *nev = 6;
     return UOCR_OK;
   }
   if (rows > p->decode_rows) {
@@ -889,6 +913,13 @@ int uocr_moe_profile_stack(uocr_moe_plan* p, float* h, int64_t rows, int32_t ite
   for (auto& e : ev) UOCR_TRY(cudaEventCreate(&e), "profile_stack: event");
   int rc = UOCR_OK;
   int nk = 0;
+  if (p->ep) {
+    // The ranks start the timed passes together: a device barrier first, so
+    // that the skew of their host launches is not counted in the first wait.
+    EpCall c = ep_call(p, p->layers[0], h, rows, h, h);
+    UOCR_TRY(ep_arrive(c, stream), "profile_stack: barrier");
+    UOCR_TRY(ep_wait(c, 63, stream), "profile_stack: barrier");
+  }
   for (size_t j = 0; j < passes && rc == UOCR_OK; ++j) {
     rc = cudaEventRecord(ev[j * kSlot], stream) == cudaSuccess ? UOCR_OK : fail(UOCR_ERR_CUDA, "profile_stack: event");
     if (rc == UOCR_OK) rc = run_layer(p, p->layers[j % nl], h, rows, h, h, stream, &ev[j * kSlot + 1], &nk);
@@ -942,6 +973,7 @@ struct EpFingerprint {
   unsigned char uuid[16];
   int64_t hidden, experts, top_k, ffn, shared_ffn, max_rows, layers;
   uint64_t region_bytes;
+  uint64_t map_hash;  // the expert placement: every rank must use the same
 };
 static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(EpFingerprint) <= sizeof(uocr_ep_handle), "handle size");
 
@@ -950,7 +982,8 @@ EpFingerprint fingerprint(const uocr_moe_plan* p) {
   f.magic = kEpMagic;
   f.world = p->emap.world;
   f.rank = p->emap.rank;
-  f.strided = p->emap.strided;
+  f.strided = (p->d.flags & UOCR_PLAN_EP_STRIDED) != 0 ? 1 : 0;
+  f.map_hash = p->etab.hash;
   cudaDeviceProp prop{};
   if (cudaGetDeviceProperties(&prop, p->d.device) == cudaSuccess) std::memcpy(f.uuid, &prop.uuid, 16);
   f.hidden = p->d.hidden;
@@ -967,7 +1000,8 @@ EpFingerprint fingerprint(const uocr_moe_plan* p) {
 bool same_shape(const EpFingerprint& a, const EpFingerprint& b) {
   return a.magic == b.magic && a.world == b.world && a.strided == b.strided && a.hidden == b.hidden &&
          a.experts == b.experts && a.top_k == b.top_k && a.ffn == b.ffn && a.shared_ffn == b.shared_ffn &&
-         a.max_rows == b.max_rows && a.layers == b.layers && a.region_bytes == b.region_bytes;
+         a.max_rows == b.max_rows && a.layers == b.layers && a.region_bytes == b.region_bytes &&
+         a.map_hash == b.map_hash;
 }
 
 }  // namespace

@@ -32,15 +32,15 @@ __device__ __forceinline__ uint4 ld_cg16(const void* p) { return __ldcg(reinterp
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 // Every rank's per-expert counts and starts (peer loads), the receive layout
-// of every rank's experts, and where this rank's selections land in the
+// of every rank's expert slots, and where this rank's selections land in the
 // owners' yrecv. One block.
 __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es,
                                                          ErrorWord* err) {
   __shared__ int cnt[kMaxEpRanks][kMaxExperts];
-  __shared__ int tot[kMaxExperts];     // [d * local + i] rows expert i of rank d receives
-  __shared__ int rstart[kMaxExperts];  // [d * local + i] its first row in rank d's yrecv
+  __shared__ int tot[kMaxEpRanks * kMaxExperts];     // [d * max_local + i] rows slot i of rank d receives
+  __shared__ int rstart[kMaxEpRanks * kMaxExperts];  // its first row in rank d's yrecv
   __shared__ int overflow;
-  const int W = m.world, E = m.experts, L = m.local;
+  const int W = m.world, E = m.experts, ML = m.max_local;
   if (threadIdx.x == 0) overflow = 0;
   for (int idx = threadIdx.x; idx < W * E; idx += blockDim.x) {
     const int s = idx / E, e = idx % E;
@@ -51,19 +51,20 @@ __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers,
     es.seg_start_all[idx] = st;
   }
   __syncthreads();
-  for (int q = threadIdx.x; q < W * L; q += blockDim.x) {
-    const int e = m.global(q / L, q % L);
+  for (int q = threadIdx.x; q < W * ML; q += blockDim.x) {
+    const int d = q / ML, e = m.slot_expert[q];
     int t = 0;
-    for (int s = 0; s < W; ++s) t += cnt[s][e];
+    if (e >= 0)
+      for (int s = 0; s < W; ++s) t += m.owner[e * W + s] == d ? cnt[s][e] : 0;
     tot[q] = t;
   }
   __syncthreads();
   if (threadIdx.x < W) {
     const int d = threadIdx.x;
     int64_t acc = 0;
-    for (int i = 0; i < L; ++i) {
-      rstart[d * L + i] = static_cast<int>(acc);
-      acc += tot[d * L + i];
+    for (int i = 0; i < ML; ++i) {
+      rstart[d * ML + i] = static_cast<int>(acc);
+      acc += tot[d * ML + i];
     }
     if (acc > lay.max_recv) {
       raise_error(err, kDevCapacity, 60, d, static_cast<int>(acc));
@@ -71,32 +72,33 @@ __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers,
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+  for (int i = threadIdx.x; i < m.local; i += blockDim.x) {
     // On overflow nothing is received (the error word reports it).
-    es.recv_count[i] = overflow ? 0 : tot[m.rank * L + i];
-    es.recv_start[i] = overflow ? 0 : rstart[m.rank * L + i];
+    es.recv_count[i] = overflow ? 0 : tot[m.rank * ML + i];
+    es.recv_start[i] = overflow ? 0 : rstart[m.rank * ML + i];
   }
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int d = m.owner(e), i = m.local_index(e);
-    int b = rstart[d * L + i];
-    for (int s = 0; s < m.rank; ++s) b += cnt[s][e];
+    const int d = m.owner[e * W + m.rank], i = m.slot[e * W + m.rank];
+    int b = rstart[d * ML + i];
+    for (int s = 0; s < m.rank; ++s) b += m.owner[e * W + s] == d ? cnt[s][e] : 0;
     es.remote_base[e] = b - es.seg_start_all[m.rank * E + e];
   }
 }
 
-// xrecv rows of this rank's experts: expert-major, then source rank, each
-// (expert, source) segment a contiguous run of the source's xperm. One warp
-// per row, grid-stride; 16-byte peer loads, all of a row in flight at once.
+// xrecv rows of this rank's expert slots: slot-major, then source rank (the
+// sources this slot takes; the others' segments are empty), each (slot,
+// source) segment a contiguous run of the source's xperm. One warp per row,
+// grid-stride; 16-byte peer loads, all of a row in flight at once.
 __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es, int H) {
-  __shared__ int seg_dst[kMaxExperts];
-  __shared__ int seg_src[kMaxExperts];
-  __shared__ int seg_rank[kMaxExperts];
+  __shared__ int seg_dst[kMaxEpRanks * kMaxExperts];
+  __shared__ int seg_src[kMaxEpRanks * kMaxExperts];
+  __shared__ int seg_rank[kMaxEpRanks * kMaxExperts];
   __shared__ int total;
   const int W = m.world, L = m.local, E = m.experts, n = W * L;
   for (int q = threadIdx.x; q < n; q += blockDim.x) {
-    const int i = q / W, s = q % W, e = m.global(m.rank, i);
+    const int i = q / W, s = q % W, e = m.slot_expert[m.rank * m.max_local + i];
     int d = es.recv_start[i];
-    for (int s2 = 0; s2 < s; ++s2) d += es.cnt_all[s2 * E + e];
+    for (int s2 = 0; s2 < s; ++s2) d += m.owner[e * W + s2] == m.rank ? es.cnt_all[s2 * E + e] : 0;
     seg_dst[q] = d;
     seg_src[q] = es.seg_start_all[s * E + e];
     seg_rank[q] = s;
@@ -107,7 +109,7 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
   const int nch = H / 8;  // 16-byte chunks per row
   for (int r = warp; r < total; r += nwarps) {
-    int lo = 0, hi = n - 1;  // last segment starting at or before r
+    int lo = 0, hi = n - 1;  // last segment starting at or before r (empty segments share the next one's start)
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (seg_dst[mid] <= r) lo = mid;
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, Ep
     r.w[j] = weights[static_cast<int64_t>(t) * K + j];
     r.src[j] = (p < 0 || e < 0 || e >= m.experts)
                    ? nullptr
-                   : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner(e)] + lay.yrecv) +
+                   : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner[e * m.world + m.rank]] + lay.yrecv) +
                          (static_cast<int64_t>(remote_base[e]) + p) * H;
   }
   sort_selections(r);
@@ -195,6 +197,71 @@ __global__ void ep_wait_kernel(const unsigned* flags, int world, const unsigned*
 
 }  // namespace
 
+bool build_ep_tables(int experts, int world, const int32_t* owner_in, bool strided, EpTables* t, std::string* why) {
+  const int E = experts, W = world;
+  t->world = W;
+  t->experts = E;
+  t->owner.assign(static_cast<size_t>(E) * W, 0);
+  for (int e = 0; e < E; ++e)
+    for (int s = 0; s < W; ++s) {
+      int d;
+      if (owner_in != nullptr) {
+        d = owner_in[e * W + s];
+        if (d < 0 || d >= W) {
+          *why = "owner of expert " + std::to_string(e) + " for rank " + std::to_string(s) + " is not a rank";
+          return false;
+        }
+      } else {
+        if (E % W != 0) {
+          *why = "routed_experts must be a multiple of ep_world without an owner table";
+          return false;
+        }
+        d = strided ? e % W : e / (E / W);
+      }
+      t->owner[static_cast<size_t>(e) * W + s] = d;
+    }
+  // Slots: rank d's experts in ascending id.
+  std::vector<std::vector<int>> held(static_cast<size_t>(W));
+  for (int e = 0; e < E; ++e)
+    for (int d = 0; d < W; ++d)
+      for (int s = 0; s < W; ++s)
+        if (t->owner[static_cast<size_t>(e) * W + s] == d) {
+          held[static_cast<size_t>(d)].push_back(e);
+          break;
+        }
+  t->max_local = 0;
+  t->slot_count.assign(static_cast<size_t>(W), 0);
+  for (int d = 0; d < W; ++d) {
+    const int n = static_cast<int>(held[static_cast<size_t>(d)].size());
+    if (n == 0) {
+      *why = "rank " + std::to_string(d) + " holds no expert";
+      return false;
+    }
+    t->slot_count[static_cast<size_t>(d)] = n;
+    if (n > t->max_local) t->max_local = n;
+  }
+  t->slot_expert.assign(static_cast<size_t>(W) * t->max_local, -1);
+  t->slot.assign(static_cast<size_t>(E) * W, 0);
+  for (int d = 0; d < W; ++d)
+    for (size_t i = 0; i < held[static_cast<size_t>(d)].size(); ++i)
+      t->slot_expert[static_cast<size_t>(d) * t->max_local + i] = held[static_cast<size_t>(d)][i];
+  for (int e = 0; e < E; ++e)
+    for (int s = 0; s < W; ++s) {
+      const int d = t->owner[static_cast<size_t>(e) * W + s];
+      const auto& h = held[static_cast<size_t>(d)];
+      int i = 0;
+      while (h[static_cast<size_t>(i)] != e) ++i;
+      t->slot[static_cast<size_t>(e) * W + s] = i;
+    }
+  uint64_t h = 1469598103934665603ull;  // FNV-1a over the owner table
+  for (int v : t->owner) {
+    h ^= static_cast<uint64_t>(static_cast<uint32_t>(v));
+    h *= 1099511628211ull;
+  }
+  t->hash = h;
+  return true;
+}
+
 EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
   EpLayout l{};
   size_t off = 0;
@@ -209,9 +276,8 @@ EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
   l.seg_count = take(E * 4);
   l.seg_start = take(E * 4);
   l.xperm = take(T * K * H * 2);
-  l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) * (K < static_cast<size_t>(m.local)
-                                                                            ? static_cast<int64_t>(K)
-                                                                            : static_cast<int64_t>(m.local));
+  l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) *
+               (K < static_cast<size_t>(m.max_local) ? static_cast<int64_t>(K) : static_cast<int64_t>(m.max_local));
   l.yrecv = take(static_cast<size_t>(l.max_recv) * H * 2);
   l.bytes = align256(off);
   return l;
@@ -245,13 +311,14 @@ void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m,
 
 cudaError_t ep_route(const EpCall& c, cudaStream_t stream) { return launch_prefill_route(c.pc, stream); }
 
-cudaError_t ep_experts(const EpCall& c, cudaStream_t stream) {
+cudaError_t ep_experts(const EpCall& c, cudaStream_t stream, cudaEvent_t after_pull) {
   const PrefillDims& d = c.pc.dims;
   ep_prepare_kernel<<<1, 256, 0, stream>>>(c.map, c.peers, c.lay, c.es, c.pc.err);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return st;
   ep_pull_kernel<<<c.pc.sm_count * 4, 256, 0, stream>>>(c.map, c.peers, c.lay, c.es, d.hidden);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  if (after_pull != nullptr && (st = cudaEventRecord(after_pull, stream)) != cudaSuccess) return st;
   const int L = c.map.local;
   GroupedGemm g1 = prefill_gate_up_gemm(c.pc, true, false);
   g1.experts = L;
@@ -311,12 +378,13 @@ cudaError_t ep_forward(const EpCall& c, cudaStream_t stream, cudaEvent_t* ev) {
   if ((st = ep_arrive(c, stream)) != cudaSuccess || (st = ep_wait(c, 61, stream)) != cudaSuccess ||
       (st = mark(1)) != cudaSuccess)
     return st;
-  if ((st = ep_experts(c, stream)) != cudaSuccess || (st = mark(2)) != cudaSuccess) return st;
+  if ((st = ep_experts(c, stream, ev != nullptr ? ev[2] : nullptr)) != cudaSuccess || (st = mark(3)) != cudaSuccess)
+    return st;
   if ((st = ep_arrive(c, stream)) != cudaSuccess) return st;
-  if ((st = ep_shared(c, stream)) != cudaSuccess || (st = mark(3)) != cudaSuccess) return st;
-  if ((st = ep_wait(c, 62, stream)) != cudaSuccess) return st;
+  if ((st = ep_shared(c, stream)) != cudaSuccess) return st;
+  if ((st = ep_wait(c, 62, stream)) != cudaSuccess || (st = mark(4)) != cudaSuccess) return st;
   if ((st = ep_combine(c, stream)) != cudaSuccess) return st;
-  return mark(4);
+  return mark(5);
 }
 
 }  // namespace uocr_b200

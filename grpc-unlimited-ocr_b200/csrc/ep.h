@@ -29,6 +29,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
+#include <vector>
 
 #include "prefill.h"
 
@@ -36,13 +38,33 @@ namespace uocr_b200 {
 
 constexpr int kMaxEpRanks = 8;
 
-// Which rank owns expert e: contiguous ranges (e / local) or strided (e % world).
+// Which rank computes which rows. The rows of expert e that rank s routed go
+// to rank owner[e * world + s], into that rank's expert slot
+// slot[e * world + s]; rank d holds slot_count[d] experts, its slot i being
+// expert slot_expert[d * max_local + i] (slots in ascending expert id). An
+// expert may live on several ranks (a hot expert's rows split by source
+// rank), and ranks may hold different numbers of experts. The tables live in
+// device memory (the plan's arena); every rank builds the same ones.
 struct EpMap {
-  int world, rank, experts, local, strided;
-  __host__ __device__ int owner(int e) const { return strided ? e % world : e / local; }
-  __host__ __device__ int local_index(int e) const { return strided ? e / world : e % local; }
-  __host__ __device__ int global(int d, int i) const { return strided ? i * world + d : d * local + i; }
+  int world, rank, experts;
+  int local;      // this rank's slot count
+  int max_local;  // the largest slot count of any rank
+  const int* owner;        // [experts * world]
+  const int* slot;         // [experts * world]
+  const int* slot_expert;  // [world * max_local], -1 past a rank's slot count
 };
+
+// The host copy of the tables, from an owner table [experts * world] or, when
+// owner_in is null, from contiguous ranges (e / (experts / world)) or the
+// strided map (e % world), both with every source going to the one owner.
+struct EpTables {
+  int world = 0, experts = 0, max_local = 0;
+  std::vector<int> owner, slot, slot_expert, slot_count;
+  uint64_t hash = 0;  // of the owner table: ranks connect only with the same map
+};
+// False (with the reason) when an owner is outside [0, world), a rank holds
+// no expert, or the experts cannot be split by the rules above.
+bool build_ep_tables(int experts, int world, const int32_t* owner_in, bool strided, EpTables* t, std::string* why);
 
 // Exchange region base of every rank (this rank's own included).
 struct EpPeers {
@@ -85,7 +107,7 @@ struct EpCall {
 
 // The phases of one layer; ep_forward runs them with the barriers between.
 cudaError_t ep_route(const EpCall& c, cudaStream_t stream);
-cudaError_t ep_experts(const EpCall& c, cudaStream_t stream);
+cudaError_t ep_experts(const EpCall& c, cudaStream_t stream, cudaEvent_t after_pull = nullptr);
 cudaError_t ep_shared(const EpCall& c, cudaStream_t stream);
 cudaError_t ep_combine(const EpCall& c, cudaStream_t stream);
 // Barrier over the ranks' exchange regions: arrive publishes this rank's
@@ -94,7 +116,8 @@ cudaError_t ep_combine(const EpCall& c, cudaStream_t stream);
 // visible to every rank's kernels after its wait.
 cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream);
 cudaError_t ep_wait(const EpCall& c, int site, cudaStream_t stream);
-// Optional events (5): after route, wait 1, experts, shared, combine.
+// Optional events (6): after route, the first wait, the pull of the rows
+// over NVLink, the expert GEMMs, the shared expert and second wait, combine.
 cudaError_t ep_forward(const EpCall& c, cudaStream_t stream, cudaEvent_t* events = nullptr);
 
 }  // namespace uocr_b200

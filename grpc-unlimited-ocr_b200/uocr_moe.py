@@ -62,7 +62,7 @@ class MoeDesc(ctypes.Structure):
                 ("weight_format", ctypes.c_int32), ("renormalize", ctypes.c_int32),
                 ("router_bias", ctypes.c_int32), ("device", ctypes.c_int32), ("flags", ctypes.c_int32),
                 ("ep_world", ctypes.c_int32), ("ep_rank", ctypes.c_int32), ("rms_norm_eps", ctypes.c_float),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("ep_owner", ctypes.c_void_p)]
 
 
 class EpHandle(ctypes.Structure):
@@ -196,18 +196,22 @@ class Plan:
 
     def __init__(self, dims: Dims, max_rows: int, weight_format: int = WEIGHT_BF16, renormalize: bool = True,
                  router_bias: bool = False, device: int = 0, flags: int = 0, ep_world: int = 0, ep_rank: int = 0,
-                 rms_norm_eps: float = 1e-6):
+                 rms_norm_eps: float = 1e-6, ep_owner=None):
         """ep_world > 1 makes this plan rank ep_rank of an expert-parallel
         group (one process per GPU); connect it with ep_connect (see ep.py).
+        ep_owner (a sequence of experts * ep_world ints, see
+        ep.balanced_owner_table) places the experts; None = the built-in map.
         flags | PLAN_PRE_NORM puts the decoder's RMSNorm (epsilon
         rms_norm_eps) in front of every layer."""
         self.dims = dims
         self.max_rows = max_rows
         self.weight_format = weight_format
         self.ep_world, self.ep_rank = ep_world, ep_rank
+        self._owner = None if ep_owner is None else (ctypes.c_int32 * len(ep_owner))(*[int(v) for v in ep_owner])
         desc = MoeDesc(dims.hidden, dims.experts, dims.top_k, dims.ffn, dims.shared_ffn, dims.layers, max_rows,
                        weight_format, int(renormalize), int(router_bias), device, flags, ep_world, ep_rank,
-                       rms_norm_eps, 0)
+                       rms_norm_eps, 0,
+                       None if self._owner is None else ctypes.cast(self._owner, ctypes.c_void_p).value)
         self.desc = desc
         h = ctypes.c_void_p()
         _check(lib().uocr_moe_plan_create(ctypes.byref(desc), ctypes.byref(h)))
@@ -270,7 +274,8 @@ class Plan:
         rows = h.shape[0] if rows is None else rows
         out = (ctypes.c_float * 8)()
         _check(lib().uocr_moe_profile_stack(self.h, _ptr(h), rows, iters, out, _stream(stream)))
-        names = {3: self.DECODE_KERNELS, 5: self.EP_PHASES}.get(int(out[6]), self.PREFILL_KERNELS)
+        names = self.DECODE_KERNELS if int(out[6]) == 3 else (self.EP_PHASES if self.ep_world > 1
+                                                                   else self.PREFILL_KERNELS)
         res = {n: out[i] for i, n in enumerate(names)}
         res["stack"] = out[7]
         return res
@@ -279,7 +284,7 @@ class Plan:
         _check(lib().uocr_moe_check(self.h, _stream(stream)))
 
     # ---- expert parallelism
-    EP_PHASES = ("route", "exchange_wait", "experts", "shared", "combine")
+    EP_PHASES = ("route", "exchange_wait", "pull", "expert_gemms", "shared_and_wait", "combine")
 
     def ep_handle(self) -> bytes:
         h = EpHandle()

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define UOCR_MOE_ABI_VERSION 4
+#define UOCR_MOE_ABI_VERSION 5
 
 typedef enum uocr_status {
   UOCR_OK = 0,
@@ -79,6 +79,15 @@ typedef struct uocr_moe_desc {
   int32_t ep_rank;           /* this plan's rank in [0, ep_world) */
   float rms_norm_eps;        /* with UOCR_PLAN_PRE_NORM: the norm's epsilon (DecoderDims::rms_norm_eps) */
   int32_t reserved;          /* 0 */
+  /* Expert placement under expert parallelism, or NULL: [routed_experts *
+   * ep_world] int32, entry e * ep_world + s = the rank that computes the rows
+   * of expert e that rank s routed. An expert may appear for several ranks (a
+   * hot expert replicated, its rows split by source rank); a rank holds the
+   * weights of every expert it appears for, and each rank must hold at least
+   * one. Every rank passes the same table (connect checks it). NULL: the
+   * contiguous ranges, or UOCR_PLAN_EP_STRIDED's e % ep_world, with
+   * routed_experts a multiple of ep_world. Read at creation only. */
+  const int32_t* ep_owner;
 } uocr_moe_desc;
 
 /* forward_stack replays a CUDA graph it captured on the first call for the
@@ -228,9 +237,10 @@ int uocr_moe_profile_stack(uocr_moe_plan* plan, float* h, int64_t rows, int32_t 
 
 /* ---- Expert parallelism across the GPUs of one node ----------------------
  * No reference counterpart (the reference has no multi-GPU path). A plan with
- * ep_world = G > 1 is one rank of G processes, one per GPU: it holds
- * routed_experts / G of the experts (set_layer still takes the full stacks
- * and keeps its own experts) and forwards its own rows. Every forward call on
+ * ep_world = G > 1 is one rank of G processes, one per GPU: it holds its
+ * share of the experts (routed_experts / G of them, or the ones desc.ep_owner
+ * assigns it; set_layer still takes the full stacks and keeps its own) and
+ * forwards its own rows. Every forward call on
  * such a plan is collective: all G ranks make the same calls in the same
  * order, any row count including 0. Layers run the prefill path (bf16,
  * hidden % 256 == 0, expert_ffn and shared_ffn % 128 == 0) whatever the row

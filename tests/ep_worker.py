@@ -29,12 +29,28 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     strided = os.environ.get("EP_STRIDED", "0") == "1"
+    balanced = os.environ.get("EP_BALANCED", "0") == "1"
     total = int(os.environ.get("EP_ROWS", "4096"))
     cfg = C.CONFIGS[3]
     start, count = ep.rows_of(total, world, rank)
     t = C.device_layer(cfg, 0, device=dev)
+    owner = None
+    if balanced:
+        # Placement from a calibration pass: every rank's routing histogram.
+        cal = M.Plan(cfg.dims(), max_rows=max(count, 17), router_bias=True, device=local)
+        C.load_layer(cal, cfg, 0, t)
+        xc = C.device_input(cfg, total, device=dev)[start:start + count].contiguous()
+        ids = torch.empty(max(count, 1), cfg.top_k, dtype=torch.int32, device=dev)
+        if count > 0:
+            cal.forward(0, xc, torch.empty_like(xc), ids)
+        cal.check()
+        cal.close()
+        mine = torch.bincount(ids[:count].reshape(-1).long(), minlength=cfg.experts)
+        allc = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allc, mine)
+        owner = ep.balanced_owner_table([c.cpu().tolist() for c in allc], world)
     plan = M.Plan(cfg.dims(), max_rows=max(count, 1), router_bias=True, device=local,
-                  flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank)
+                  flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank, ep_owner=owner)
     C.load_layer(plan, cfg, 0, t)
     ep.connect(plan)
     x = C.device_input(cfg, total, device=dev)[start:start + count].contiguous()
@@ -72,7 +88,7 @@ def main():
     # graph) against the same stack on one GPU.
     dims2 = cfg.dims(layers=2)
     plan2 = M.Plan(dims2, max_rows=max(count, 1), router_bias=True, device=local,
-                   flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank)
+                   flags=M.PLAN_EP_STRIDED if strided else 0, ep_world=world, ep_rank=rank, ep_owner=owner)
     single2 = M.Plan(dims2, max_rows=max(count, 17), router_bias=True, device=local)
     t1 = C.device_layer(cfg, 1, device=dev)
     for pl in (plan2, single2):
@@ -102,7 +118,8 @@ def main():
     single2.close()
     dist.destroy_process_group()
     if rank == 0:
-        print(f"EP world {world} strided {strided} rows {total}: {'EP_OK' if flag.item() == 0 else 'EP_MISMATCH'}")
+        print(f"EP world {world} strided {strided} balanced {balanced} rows {total}: "
+              f"{'EP_OK' if flag.item() == 0 else 'EP_MISMATCH'}")
     sys.exit(0 if flag.item() == 0 else 1)
 
 

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
     lib = M.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.uocr_abi_version() == 4
+    assert lib.uocr_abi_version() == 5
 
 
 def test_struct_layouts_match_the_header(tmp_path):
@@ -88,13 +88,26 @@ def test_plan_create_rejects_bad_shapes(bad):
 
 @pytest.mark.parametrize("bad,code", [
     (dict(ep_world=9, ep_rank=0), 1), (dict(ep_world=-1), 1), (dict(ep_world=2, ep_rank=2), 1),
-    (dict(ep_world=3, ep_rank=0), 1),  # 8 experts do not split over 3 ranks
+    (dict(ep_world=3, ep_rank=0, hidden=256, expert_ffn=128, shared_ffn=128), 1),  # 8 experts over 3 ranks, no table
     (dict(ep_world=2, ep_rank=0), 2),  # hidden 64: not a prefill shape
     (dict(ep_world=2, ep_rank=1, hidden=256, expert_ffn=128, shared_ffn=128, weight_format=1), 2)])
 def test_plan_create_rejects_bad_expert_parallel_setups(bad, code):
     h = ctypes.c_void_p()
     rc = M.lib().uocr_moe_plan_create(ctypes.byref(_desc(**bad)), ctypes.byref(h))
     assert rc == code and not h.value
+
+
+@pytest.mark.parametrize("table,why", [
+    ([0, 1] * 7 + [0, 2], "is not a rank"),       # expert 7's rows from rank 1 to rank 2 of 2
+    ([0, 0] * 8, "holds no expert"),              # rank 1 would hold nothing
+])
+def test_plan_create_rejects_bad_owner_tables(table, why):
+    owner = (ctypes.c_int32 * len(table))(*table)
+    d = _desc(ep_world=2, ep_rank=0, hidden=256, expert_ffn=128, shared_ffn=128)
+    d.ep_owner = ctypes.cast(owner, ctypes.c_void_p).value
+    h = ctypes.c_void_p()
+    assert M.lib().uocr_moe_plan_create(ctypes.byref(d), ctypes.byref(h)) == 1 and not h.value
+    assert why in M.lib().uocr_last_error().decode()
 
 
 def test_ep_entry_points_reject_bad_arguments():

@@ -56,7 +56,7 @@ def test_c_program_reads_a_checkpoint(tmp_path):
     assert out[0] == f"tensors {len(arrays)}"
     assert out[1] == f"dtype {M.DTYPE_BF16} rank 2 shape {a.shape[0]} {a.shape[1]} bytes {a.nbytes} first {int(a.flat[0])}"
     assert out[2] == "absent rc 1: no tensor named model.layers.9.mlp.gate.weight"
-    assert out[3] == "abi 4"
+    assert out[3] == "abi 5"
     bad = tmp_path / "bad.json"
     bad.write_text("{}")
     r = subprocess.run([str(exe), str(bad), name], capture_output=True, text=True)

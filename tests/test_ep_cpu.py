@@ -173,3 +173,52 @@ def test_two_gloo_ranks_agree_with_one_process(strided):
         p.join(120)
     assert all(p.exitcode == 0 for p in procs)
     assert q.get(timeout=5) is True
+
+
+# ---- load-balanced placement ----------------------------------------------
+
+# Rows per expert of the config-3 prefill layer (32768 rows, top-6, the
+# Zipf(1.2)-biased router), as the bench measured them on B200.
+C3_HISTOGRAM = [26872, 21042, 16749, 13694, 11519, 10011, 8258, 7256, 6636, 5722, 4861, 4539, 4174, 3601, 3388, 3118,
+                2828, 2627, 2452, 2226, 2118, 1845, 1820, 1751, 1707, 1393, 1321, 1474, 1294, 1281, 1074, 1103, 808,
+                869, 959, 782, 836, 733, 641, 698, 717, 606, 643, 638, 557, 534, 507, 495, 557, 487, 422, 445, 408,
+                455, 348, 357, 378, 315, 310, 325, 270, 233, 270, 251]
+
+
+def _by_source(hist, W):
+    return [[h // W + (1 if s < h % W else 0) for h in hist] for s in range(W)]
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_balanced_owner_table_evens_out_the_received_rows(W):
+    E = len(C3_HISTOGRAM)
+    cbs = _by_source(C3_HISTOGRAM, W)
+    owner = ep.balanced_owner_table(cbs, W)
+    assert len(owner) == E * W and all(0 <= d < W for d in owner)
+    got = ep.rows_received(owner, cbs, E, W)
+    assert sum(got) == sum(C3_HISTOGRAM)
+    assert max(got) / (sum(got) / W) <= 1.05
+    # the built-in maps are far off on this histogram
+    assert max(ep.rows_received(ep.owner_table(E, W, True), cbs, E, W)) / (sum(got) / W) > 1.07
+    for d in range(W):
+        assert len(ep.slots_of(owner, E, W, d)) >= 1
+    for e in range(E):
+        reps = sorted({owner[e * W + s] for s in range(W)})
+        assert W % len(reps) == 0  # replicas split the sources evenly
+        for s in range(W):  # replica j takes the sources s % r == j
+            assert owner[e * W + s] == owner[e * W + s % len(reps)]
+    assert ep.balanced_owner_table(cbs, W) == owner  # deterministic: every rank computes the same table
+
+
+def test_owner_table_matches_the_built_in_maps():
+    for E, W in ((64, 8), (16, 4)):
+        for strided in (False, True):
+            owner = ep.owner_table(E, W, strided)
+            for d in range(W):
+                assert ep.slots_of(owner, E, W, d) == ep.local_experts(d, E, W, strided)
+
+
+def test_balanced_table_with_more_ranks_than_hot_experts():
+    cbs = _by_source([1000, 1, 1], 4)
+    owner = ep.balanced_owner_table(cbs, 4)
+    assert all(len(ep.slots_of(owner, 3, 4, d)) >= 1 for d in range(4))

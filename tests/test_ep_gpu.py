@@ -14,10 +14,10 @@ from test_decode_gpu import BF16_TOL, _tiny_layer, _upload, to_np
 pytestmark = pytest.mark.gpu
 
 
-def _group(n, dims, max_rows, w, torch, cuda, strided=False):
+def _group(n, dims, max_rows, w, torch, cuda, strided=False, owner=None):
     flags = M.PLAN_EP_STRIDED if strided else 0
     plans = [M.Plan(dims, max_rows=max_rows, router_bias=w.router_bias is not None, flags=flags, ep_world=n,
-                    ep_rank=r) for r in range(n)]
+                    ep_rank=r, ep_owner=owner) for r in range(n)]
     keep = [_upload(p, w, torch, cuda) for p in plans]
     M.ep_connect_local(plans)
     return plans, keep
@@ -149,4 +149,40 @@ def test_ep_plan_misuse_is_reported(cuda):
     with pytest.raises(M.UocrError) as e:
         a.ep_connect([a.ep_handle(), c.ep_handle()])
     assert e.value.code == 1
+    del keep
+
+
+@pytest.mark.parametrize("n,rows", [(2, [300, 257]), (4, [0, 129, 500, 64]), (8, [100] * 8)])
+def test_balanced_placement_equals_single_plan(cuda, n, rows):
+    """A load-balanced owner table (hot experts replicated, their rows split
+    by source rank; ranks holding different numbers of experts) moves rows
+    differently but must still give the single plan's output bit for bit."""
+    import torch
+
+    import ep
+    rng = np.random.default_rng(7 * n + sum(rows))
+    H, E, K, F, S = 256, 32, 4, 128, 128
+    w = _skewed(rng, H, E, F, S)
+    dims = M.Dims(H, E, K, F, S)
+    x = torch.from_numpy(rng.standard_normal((sum(rows), H)).astype(np.float32)).to(cuda)
+    single = M.Plan(dims, max_rows=sum(rows), router_bias=True)
+    _upload(single, w, torch, cuda)
+    y = torch.empty_like(x)
+    ids = torch.empty(sum(rows), K, dtype=torch.int32, device=cuda)
+    single.forward(0, x, y, ids)
+    single.check()
+    # the calibration histogram: rows each source rank routes to each expert
+    flat = ids.cpu().numpy()
+    starts = np.concatenate([[0], np.cumsum(rows)])
+    cbs = [np.bincount(flat[starts[r]:starts[r + 1]].ravel(), minlength=E) for r in range(n)]
+    owner = ep.balanced_owner_table(cbs, n, share=0.1)  # a small share: the hot experts are replicated
+    assert len({owner[e * n + s] for e in range(E) for s in range(n)}) == n
+    assert any(len({owner[e * n + s] for s in range(n)}) > 1 for e in range(E))  # some expert is replicated
+    plans, keep = _group(n, dims, max(max(rows), 1), w, torch, cuda, owner=owner)
+    xs = [t.contiguous() for t in torch.split(x, rows)]
+    ys = [torch.full_like(t, float("nan")) for t in xs]
+    M.ep_forward_local(plans, 0, xs, ys)
+    for p in plans:
+        p.check()
+    assert torch.equal(torch.cat(ys), y)
     del keep

@@ -20,13 +20,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world,strided,rows", [(2, False, 4096), (2, True, 1000), (4, False, 8192),
-                                                (8, False, 32768)])
-def test_ep_ranks_equal_single_gpu(world, strided, rows):
+@pytest.mark.parametrize("world,placement,rows", [(2, "contiguous", 4096), (2, "strided", 1000),
+                                                  (2, "balanced", 4096), (4, "contiguous", 8192),
+                                                  (4, "balanced", 8192), (8, "contiguous", 32768),
+                                                  (8, "balanced", 32768)])
+def test_ep_ranks_equal_single_gpu(world, placement, rows):
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    env = dict(os.environ, EP_STRIDED="1" if strided else "0", EP_ROWS=str(rows), NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, EP_STRIDED="1" if placement == "strided" else "0",
+               EP_BALANCED="1" if placement == "balanced" else "0", EP_ROWS=str(rows), NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "ep_worker.py")]
