@@ -227,12 +227,16 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     y = torch.empty_like(x)
     ids = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
     owner, cbs, y1 = None, None, None
+    # The inputs come from torch's default stream; the plans run on `stream`
+    # (a non-blocking stream), so wait for them explicitly.
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
         # Calibration and reference: this rank's rows through a one-GPU plan.
         single = M.Plan(cfg.dims(), max_rows=max(T, 1), router_bias=True, device=dev.index or 0)
         C.load_layer(single, cfg, 0, t)
         y1 = torch.empty_like(x)
+        torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             single.forward(0, x, y1, ids, stream=stream)
             single.check(stream=stream)
@@ -250,6 +254,7 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     C.load_layer(plan, cfg, 0, t)
     if world > 1:
         ep.connect(plan)
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             plan.forward(0, x, y, ids, stream=stream)
@@ -395,6 +400,7 @@ def run_page_decode(M, C, dev, stream, int8, steps=None, prefill_rows=None, laye
     wbytes, obytes = dec.bytes()
     x = C.decoder_prompt(cfg, n, device=dev)
     toks = torch.empty(steps, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()  # made on the default stream, used on `stream`
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     with torch.cuda.stream(stream):
         for _ in range(2):  # warm-up: captures the decode graph
@@ -588,12 +594,18 @@ def decode_ids_and_inputs(plan, cfg, x, stream):
     return inputs, got, active, bool(torch.isfinite(hh).all().item())
 
 
+def torch_sync():
+    import torch
+    torch.cuda.synchronize()
+
+
 def decode_section(plan, cfg, T, fmt_int8, steps, stream, dev, check_routes):
     """One named decode configuration: tokens/s, the step's algorithmic bytes
     (from the distinct experts the produced ids touched) against the measured
     HBM peak, the gate/up kernel's fraction, and the ids check."""
     import moe_configs as C
     x = C.device_input(cfg, T, device=dev)
+    torch_sync()
     ms, _ = time_decode(plan, x, steps, 3, stream)
     h = x.clone()
     prof = plan.profile_stack(h, iters=5, stream=stream)
@@ -702,6 +714,7 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     x = C.device_input(cfg, T, device=dev)
     h = torch.empty_like(x)
+    torch.cuda.synchronize()  # made on the default stream, used on `stream`
 
     clocks = ClockSampler(local)
     ms, clk = time_decode(plan, x, args.steps, args.warmup, stream, clocks=clocks, barrier=barrier)

@@ -55,6 +55,7 @@ def _run(torch, cuda, dec, prompt, vocab, steps, stream):
     toks = torch.empty(steps, dtype=torch.int32, device=cuda)
     lg = torch.empty(steps, vocab, device=cuda)
     x = torch.from_numpy(prompt).to(cuda)
+    torch.cuda.synchronize()  # x comes from the default stream; `stream` does not wait for it
     with torch.cuda.stream(stream):
         dec.prefill(x, logits0, tok0, stream=stream)
         dec.decode(steps, toks, lg, stream=stream)
