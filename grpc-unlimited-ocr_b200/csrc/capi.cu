@@ -838,6 +838,37 @@ int uocr_moe_forward(uocr_moe_plan* p, int64_t layer, const float* x, int64_t ro
   return UOCR_OK;
 }
 
+int uocr_moe_router_logits(uocr_moe_plan* p, int64_t layer, const float* x, int64_t rows, float* logits,
+                           void* stream_v) {
+  if (p == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: null plan");
+  if (layer < 0 || layer >= p->d.layers) return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: layer out of range");
+  if (rows < 0 || rows > p->d.max_rows)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: rows outside [0, max_rows]");
+  if (rows == 0) return UOCR_OK;
+  if (x == nullptr || logits == nullptr) return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: null x or logits");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: x must be 16-byte aligned");
+  const LayerDev& L = p->layers[static_cast<size_t>(layer)];
+  if (!L.loaded) return fail(UOCR_ERR_INVALID_ARGUMENT, "router_logits: layer weights not set");
+  DeviceGuard guard(p->d.device);
+  auto stream = static_cast<cudaStream_t>(stream_v);
+  const uocr_moe_desc& d = p->d;
+  const int T = static_cast<int>(rows), H = static_cast<int>(d.hidden), E = static_cast<int>(d.routed_experts);
+  const RowNorm norm{L.norm, d.rms_norm_eps, p->pre_norm ? 1 : 0};
+  if (rows > p->decode_rows || p->ep) {
+    if (p->pre_norm) {
+      UOCR_TRY(launch_rms_norm_rows(x, rows, H, norm, p->xnorm, stream), "router_logits: pre-norm");
+      x = p->xnorm;
+    }
+    UOCR_TRY(launch_router_logits_rows(x, T, H, L.router, L.bias, E, logits, stream), "router_logits");
+    return UOCR_OK;
+  }
+  const RouteOut ro{p->route, static_cast<int>(d.experts_per_token), d.renormalize, p->ids, p->weights, p->counter,
+                    p->err};
+  UOCR_TRY(launch_router_logits(x, T, H, L.router, L.bias, E, logits, stream, false, &ro, norm), "router_logits");
+  return UOCR_OK;
+}
+
 int uocr_moe_forward_stack(uocr_moe_plan* p, float* h, int64_t rows, void* stream_v) {
   if (p == nullptr || (h == nullptr && rows > 0))
     return fail(UOCR_ERR_INVALID_ARGUMENT, "forward_stack: null argument");

@@ -9,33 +9,50 @@
 
 namespace uocr_b200 {
 
-// A row's selections: expert id, weight and the expert output row (bf16).
+// A row's selections in combine order: weight and the expert output row (bf16).
 struct CombineRow {
   int n;
-  int eid[kMaxTopK];
   float w[kMaxTopK];
   const __nv_bfloat16* src[kMaxTopK];
 };
 
-// Ascending expert id; a fully unrolled exchange network, so the arrays stay
-// in registers.
-__device__ __forceinline__ void sort_selections(CombineRow& r) {
-#pragma unroll
-  for (int a = 0; a < kMaxTopK - 1; ++a) {
-#pragma unroll
-    for (int b = 0; b < kMaxTopK - 1 - a; ++b) {
-      if (b + 1 < r.n && r.eid[b + 1] < r.eid[b]) {
-        const int te = r.eid[b];
-        r.eid[b] = r.eid[b + 1];
-        r.eid[b + 1] = te;
-        const float tw = r.w[b];
-        r.w[b] = r.w[b + 1];
-        r.w[b + 1] = tw;
-        const __nv_bfloat16* ts = r.src[b];
-        r.src[b] = r.src[b + 1];
-        r.src[b + 1] = ts;
-      }
+// The selections of the block's row in ascending expert id (a stable
+// order: equal ids keep their slot order). Thread j < n fetches selection j
+// and counts the selections ahead of it; the ranked weight and row pointer go
+// to shared memory, and after the barrier every thread reads the ordered list.
+// One rank per selection instead of a sorting network in every thread.
+struct CombineList {
+  float w[kMaxTopK];
+  const __nv_bfloat16* src[kMaxTopK];
+};
+
+// id_of(i): selection i's expert id; fetch(j, id, &w, &src): its weight and
+// expert output row (null for a dropped selection). Every thread of the block
+// calls this (it holds a barrier).
+template <class IdOf, class Fetch>
+__device__ __forceinline__ void order_selections(int n, IdOf id_of, Fetch fetch, CombineList* list,
+                                                 CombineRow& r) {
+  const int j = threadIdx.x;
+  if (j < n) {
+    const int e = id_of(j);
+    int rank = 0;
+    for (int i = 0; i < n; ++i) {
+      const int ei = id_of(i);
+      rank += (ei < e || (ei == e && i < j)) ? 1 : 0;
     }
+    float w;
+    const __nv_bfloat16* src;
+    fetch(j, e, &w, &src);
+    list->w[rank] = w;
+    list->src[rank] = src;
+  }
+  __syncthreads();
+  r.n = n;
+#pragma unroll
+  for (int q = 0; q < kMaxTopK; ++q) {
+    if (q >= n) break;
+    r.w[q] = list->w[q];
+    r.src[q] = list->src[q];
   }
 }
 

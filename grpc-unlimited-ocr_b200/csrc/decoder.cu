@@ -205,6 +205,41 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The cluster's splits merged through distributed shared memory, after every
+// block of the cluster wrote its hmax[G], hsum[G] (max and exp sum per head)
+// and accs[G][128] (p . V with p = exp(s - hmax)): this block takes dims
+// [split * D, split * D + D) of every head (D = 128 / splits), tpi threads per
+// (head, dim) item sharing the splits; weights exp(m_s - m), then the
+// weighted sum over the weighted exp-sum total, rounded to bf16. Every thread
+// of the block calls it.
+template <int G>
+__device__ __forceinline__ void cluster_merge(const float* hmax, const float* hsum, const float* accs, int split,
+                                              int splits, int qh0, float* merged) {
+  cluster_sync_all();  // every split's hmax, hsum and accs are written
+  const int D = kDecHeadDim / splits;
+  const int items = G * D;
+  const int tpi = kAttnThreads / items;  // a power of two, 2..32
+  const int item = threadIdx.x / tpi, li = threadIdx.x % tpi;
+  const int a = item / D, d = split * D + item % D;
+  float m = -INFINITY;
+  for (int r = li; r < splits; r += tpi) m = fmaxf(m, ld_cluster(cluster_addr(&hmax[a], r)));
+  for (int off = tpi / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  float tot = 0.0f, o = 0.0f;
+  for (int r = li; r < splits; r += tpi) {
+    const float ms = ld_cluster(cluster_addr(&hmax[a], r));
+    if (ms == -INFINITY) continue;
+    const float w = expf(ms - m);
+    tot = fmaf(w, ld_cluster(cluster_addr(&hsum[a], r)), tot);
+    o = fmaf(w, ld_cluster(cluster_addr(accs + a * kDecHeadDim + d, r)), o);
+  }
+  for (int off = tpi / 2; off > 0; off >>= 1) {
+    tot += __shfl_xor_sync(0xffffffffu, tot, off);
+    o += __shfl_xor_sync(0xffffffffu, o, off);
+  }
+  if (li == 0) merged[(qh0 + a) * kDecHeadDim + d] = bf16_round(o / tot);
+  cluster_sync_all();  // no block leaves while others read its shared memory
+}
+
 // Split-key attention, one thread-block cluster per key/value head: block
 // (g, split) takes a contiguous share of keys 0..pos for the G query heads
 // that read head g (one cluster per query head, 4x the blocks, measured
@@ -362,33 +397,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attn_kernel(DecShape s, cons
     for (int w = 0; w < kAttnWarps; ++w) v += red[w * G * kDecHeadDim + it];
     accs[it] = v;
   }
-  cluster_sync_all();  // every split's hmax, hsum and accs are written
-  // Merge: this block takes dims [split * D, split * D + D) of every head
-  // (D = 128 / splits); tpi threads per (head, dim) item share the splits.
-  {
-    const int D = kDecHeadDim / splits;
-    const int items = G * D;
-    const int tpi = kAttnThreads / items;  // a power of two, 2..32
-    const int item = threadIdx.x / tpi, li = threadIdx.x % tpi;
-    const int a = item / D, d = split * D + item % D;
-    float m = -INFINITY;
-    for (int r = li; r < splits; r += tpi) m = fmaxf(m, ld_cluster(cluster_addr(&hmax[a], r)));
-    for (int off = tpi / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float tot = 0.0f, o = 0.0f;
-    for (int r = li; r < splits; r += tpi) {
-      const float ms = ld_cluster(cluster_addr(&hmax[a], r));
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - m);
-      tot = fmaf(w, ld_cluster(cluster_addr(&hsum[a], r)), tot);
-      o = fmaf(w, ld_cluster(cluster_addr(accs + a * kDecHeadDim + d, r)), o);
-    }
-    for (int off = tpi / 2; off > 0; off >>= 1) {
-      tot += __shfl_xor_sync(0xffffffffu, tot, off);
-      o += __shfl_xor_sync(0xffffffffu, o, off);
-    }
-    if (li == 0) merged[(qh0 + a) * kDecHeadDim + d] = bf16_round(o / tot);
-  }
-  cluster_sync_all();  // no block leaves while others read its shared memory
+  cluster_merge<G>(hmax, hsum, accs, split, splits, qh0, merged);
 }
 
 // x += wo . merged (the attention's merged rows, bf16 values), the weight
@@ -717,6 +726,179 @@ const void* attn_fn(int G) {
   }
 }
 
+// ---- decode attention on the tensor cores --------------------------------
+
+constexpr int kTcKeysPerWarp = 48;  // keys a warp scores per round (6 tiles of 8, 3 chunks of 16 for p . V)
+constexpr int kTcRound = kTcKeysPerWarp * kAttnWarps;
+constexpr int kKvStride = kDecHeadDim + 8;  // padded bf16 row of the staged K and V (conflict-free fragments)
+
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, const void* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_addr(row_addr)));
+}
+
+// The same split-key attention as dec_attn_kernel with the products on the
+// tensor cores: the G query heads are the rows of 16-row mma tiles (the other
+// rows zero), the split's K and V rows staged in shared memory by cp.async
+// (K and V rows padded to 136 bf16, so every fragment load is conflict-free;
+// V's fragments come transposed from ldmatrix). Warp w takes 48 keys a round
+// (s = q . k as 6 tiles of 8 keys x 8 chunks of 16 dims, then an online
+// softmax per head: running max, rescale, exp; p rounded to bf16 as the A
+// operand of p . V, 3 chunks of 16 keys x 16 tiles of 8 dims). The warps'
+// (max, sum, p . V) per head are merged in shared memory, then the cluster
+// merges its splits as dec_attn_kernel does.
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) dec_attn_tc_kernel(DecShape s, const float* __restrict__ q,
+                                                                   const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+                                                                   const DecState* st, float* merged, int cap,
+                                                                   float scale) {
+  extern __shared__ __align__(16) unsigned char sraw[];
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(sraw);            // [cap][136]
+  __nv_bfloat16* vs = ks + static_cast<size_t>(cap) * kKvStride;         // [cap][136]
+  float* wo = reinterpret_cast<float*>(vs + static_cast<size_t>(cap) * kKvStride);  // [warps][G][128]
+  float* accs = wo + kAttnWarps * G * kDecHeadDim;                        // [G][128]
+  __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
+  __shared__ float hmax[G], hsum[G];
+  pdl_wait();
+  const int qh0 = blockIdx.x * G, split = blockIdx.y, splits = gridDim.y;
+  const int g = qh0 / (s.heads / s.kv);
+  const int keys = st->pos + 1;
+  const int chunk = (keys + splits - 1) / splits;
+  const int first = split * chunk;
+  const int n = max(0, min(keys, first + chunk) - first);
+  const __nv_bfloat16* kh = kc + (static_cast<int64_t>(g) * s.max_pos + first) * kDecHeadDim;
+  const __nv_bfloat16* vh = vc + (static_cast<int64_t>(g) * s.max_pos + first) * kDecHeadDim;
+  for (int c = threadIdx.x; c < n * (kDecHeadDim / 8); c += kAttnThreads) {
+    const int key = c / (kDecHeadDim / 8), c8 = c % (kDecHeadDim / 8);
+    cp_async16(ks + key * kKvStride + c8 * 8, kh + c * 8);
+    cp_async16(vs + key * kKvStride + c8 * 8, vh + c * 8);
+  }
+  cp_async_commit();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gr = lane >> 2, tq = lane & 3;
+  // Q as the A operand: row gr < G is query head qh0 + gr, other rows zero.
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    if (gr < G) {
+      const float* qr = q + (qh0 + gr) * kDecHeadDim + kk * 16 + 2 * tq;
+      const float2 lo = __ldcg(reinterpret_cast<const float2*>(qr));
+      const float2 hi = __ldcg(reinterpret_cast<const float2*>(qr + 8));
+      qa[kk][0] = pack_bf16(lo.x, lo.y);
+      qa[kk][1] = pack_bf16(hi.x, hi.y);
+    } else {
+      qa[kk][0] = qa[kk][1] = 0u;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  float o[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;  // for row gr (valid when gr < G)
+  for (int base = warp * kTcKeysPerWarp; base < n; base += kTcRound) {
+    float sc[6][4];
+#pragma unroll
+    for (int nt = 0; nt < 6; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+      const int key = base + nt * 8 + gr;
+      const __nv_bfloat16* kr = ks + min(key, n - 1) * kKvStride;  // keys past n: a staged row, masked below
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 2 * tq);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 8 + 2 * tq);
+        const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+        mma_bf16_16816(sc[nt], a, b0, b1);
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 6; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = base + nt * 8 + 2 * tq + e;
+        const float v = key < n ? sc[nt][e] * scale : -INFINITY;
+        sc[nt][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
+    m_run = m_new;
+    l_run *= alpha;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      o[d][0] *= alpha;
+      o[d][1] *= alpha;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 6; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float p = sc[nt][e] == -INFINITY ? 0.0f : expf(sc[nt][e] - m_run);
+        sc[nt][e] = p;
+        l_run += p;
+      }
+#pragma unroll
+    for (int kc2 = 0; kc2 < 3; ++kc2) {
+      const uint32_t pa[4] = {pack_bf16(sc[2 * kc2][0], sc[2 * kc2][1]), 0u,
+                              pack_bf16(sc[2 * kc2 + 1][0], sc[2 * kc2 + 1][1]), 0u};
+      // rows of the 16-key chunk; keys past n read a staged (finite) row with p = 0
+      const int krow = min(base + kc2 * 16 + (lane & 15), n - 1);
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        uint32_t b0, b1;
+        ldmatrix_x2_trans(b0, b1, vs + krow * kKvStride + d * 8);
+        mma_bf16_16816(o[d], pa, b0, b1);
+      }
+    }
+  }
+  // this warp's row sum (the four lanes of a row hold parts of it)
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (gr < G) {
+    if (tq == 0) {
+      wm[warp][gr] = m_run;
+      wl[warp][gr] = l_run;
+    }
+#pragma unroll
+    for (int d = 0; d < 16; ++d)
+      *reinterpret_cast<float2*>(wo + (warp * G + gr) * kDecHeadDim + d * 8 + 2 * tq) = make_float2(o[d][0], o[d][1]);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int a = threadIdx.x;
+    float m = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, wm[w][a]);
+    float l = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w)
+      if (wm[w][a] != -INFINITY) l = fmaf(expf(wm[w][a] - m), wl[w][a], l);
+    hmax[a] = m;
+    hsum[a] = l;
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < G * kDecHeadDim; it += kAttnThreads) {
+    const int a = it / kDecHeadDim;
+    float v = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w)
+      if (wm[w][a] != -INFINITY) v = fmaf(expf(wm[w][a] - hmax[a]), wo[(w * G) * kDecHeadDim + it], v);
+    accs[it] = v;
+  }
+  cluster_merge<G>(hmax, hsum, accs, split, splits, qh0, merged);
+}
+
+const void* attn_tc_fn(int G) {
+  switch (G) {
+    case 1: return reinterpret_cast<const void*>(dec_attn_tc_kernel<1>);
+    case 2: return reinterpret_cast<const void*>(dec_attn_tc_kernel<2>);
+    case 4: return reinterpret_cast<const void*>(dec_attn_tc_kernel<4>);
+    case 8: return reinterpret_cast<const void*>(dec_attn_tc_kernel<8>);
+    default: return nullptr;
+  }
+}
+
 template <typename Rows>
 void* qkv_fn() {
   return reinterpret_cast<void*>(dec_qkv_kernel<Rows>);
@@ -745,8 +927,9 @@ cudaError_t prepare_decoder_kernels() {
   if ((st = allow_max_dynamic_smem(dec_oproj_kernel<Q8Rows>)) != cudaSuccess) return st;
   if ((st = allow_max_dynamic_smem(dec_lmhead_kernel<Bf16Rows>)) != cudaSuccess) return st;
   if ((st = allow_max_dynamic_smem(dec_lmhead_kernel<Q8Rows>)) != cudaSuccess) return st;
-  for (int G : {1, 2, 4, 8}) {
-    const void* fn = attn_fn(G);
+  for (int i = 0; i < 8; ++i) {
+    const int G = 1 << (i % 4);
+    const void* fn = i < 4 ? attn_fn(G) : attn_tc_fn(G);
     int optin = 0;
     cudaFuncAttributes a{};
     if ((st = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return st;
@@ -782,57 +965,80 @@ size_t dec_attn_smem(const DecShape& s, int splits, bool v_smem) {
   return (G * capr + kAttnWarps * G * kDecHeadDim + G * kDecHeadDim) * 4 + (v_smem ? cap * kDecHeadDim * 2 : 0);
 }
 
-cudaError_t plan_dec_attn(const DecShape& s, int* splits, bool* v_smem) {
-  const void* fn = attn_fn(s.heads / s.kv);
-  if (fn == nullptr) return cudaErrorInvalidValue;
+size_t dec_attn_tc_smem(const DecShape& s, int splits) {
+  const size_t G = static_cast<size_t>(s.heads / s.kv);
+  const size_t cap = static_cast<size_t>((s.max_pos + splits - 1) / splits);
+  return 2 * cap * kKvStride * 2 + (kAttnWarps * G * kDecHeadDim + G * kDecHeadDim) * 4;
+}
+
+namespace {
+// Whether a cluster of c blocks of fn with smem bytes can be placed.
+bool cluster_fits(const void* fn, const DecShape& s, int c, size_t smem) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(s.kv, c);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = c;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return clusters >= 1;
+}
+}  // namespace
+
+cudaError_t plan_dec_attn(const DecShape& s, bool cuda_cores, int* splits, int* mode) {
+  const int G = s.heads / s.kv;
+  const void* fn = attn_fn(G);
+  const void* tc = attn_tc_fn(G);
+  if (fn == nullptr || tc == nullptr) return cudaErrorInvalidValue;
   int dev = 0, optin = 0;
   cudaError_t st = cudaGetDevice(&dev);
   if (st == cudaSuccess) st = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (st != cudaSuccess) return st;
+  const size_t limit = static_cast<size_t>(optin) - 1024;
   for (int c : {16, 8}) {
-    bool vsm = dec_attn_smem(s, c, true) <= static_cast<size_t>(optin) - 256;
-    const size_t smem = dec_attn_smem(s, c, vsm);
-    if (smem > static_cast<size_t>(optin) - 256) continue;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(s.kv, c);
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = c;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    st = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg);
-    if (st != cudaSuccess) {
-      cudaGetLastError();
-      continue;
-    }
-    if (clusters >= 1) {
+    if (!cuda_cores && dec_attn_tc_smem(s, c) <= limit && cluster_fits(tc, s, c, dec_attn_tc_smem(s, c))) {
       *splits = c;
-      *v_smem = vsm;
+      *mode = kAttnTensorCores;
       return cudaSuccess;
+    }
+    for (int vsm : {1, 0}) {
+      const size_t smem = dec_attn_smem(s, c, vsm != 0);
+      if (smem <= limit && cluster_fits(fn, s, c, smem)) {
+        *splits = c;
+        *mode = vsm ? kAttnCudaCoresSmemV : kAttnCudaCores;
+        return cudaSuccess;
+      }
     }
   }
   return cudaErrorNotSupported;
 }
 
 cudaError_t launch_dec_attn(const DecShape& s, const float* q, const __nv_bfloat16* kcache,
-                            const __nv_bfloat16* vcache, const DecState* st, float* merged, int splits, bool v_smem,
+                            const __nv_bfloat16* vcache, const DecState* st, float* merged, int splits, int mode,
                             cudaStream_t stream, bool pdl) {
-  const void* fn = attn_fn(s.heads / s.kv);
+  const int G = s.heads / s.kv;
+  const bool tc = mode == kAttnTensorCores;
+  const void* fn = tc ? attn_tc_fn(G) : attn_fn(G);
   if (fn == nullptr) return cudaErrorInvalidValue;
   DecShape sh = s;
   int cap = (s.max_pos + splits - 1) / splits;
-  int vsm = v_smem ? 1 : 0;
+  int vsm = mode == kAttnCudaCoresSmemV ? 1 : 0;
   float scale = 1.0f / sqrtf(static_cast<float>(kDecHeadDim));
-  void* args[] = {&sh, &q, &kcache, &vcache, &st, &merged, &cap, &vsm, &scale};
+  void* args_cc[] = {&sh, &q, &kcache, &vcache, &st, &merged, &cap, &vsm, &scale};
+  void* args_tc[] = {&sh, &q, &kcache, &vcache, &st, &merged, &cap, &scale};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(s.kv, splits);
   cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = dec_attn_smem(s, splits, v_smem);
+  cfg.dynamicSmemBytes = tc ? dec_attn_tc_smem(s, splits) : dec_attn_smem(s, splits, vsm != 0);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -843,7 +1049,7 @@ cudaError_t launch_dec_attn(const DecShape& s, const float* q, const __nv_bfloat
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelExC(&cfg, fn, args);
+  return cudaLaunchKernelExC(&cfg, fn, tc ? args_tc : args_cc);
 }
 
 cudaError_t launch_dec_oproj(const DecShape& s, bool int8, const float* merged, DecMatrix wo, float* x, int sm_count,

@@ -55,12 +55,16 @@ cudaError_t launch_dec_qkv(const DecShape& s, bool int8, float* x, const __nv_bf
 // one thread-block cluster of `splits` blocks per key/value head; the blocks
 // merge their partials through distributed shared memory into merged
 // ([heads * 128], bf16 values). plan_dec_attn picks the split count (16, or
-// 8 where a 16-block cluster cannot be placed) and whether a split's V rows
-// fit in shared memory; dec_attn_smem is the launch's dynamic shared memory.
+// 8 where a 16-block cluster cannot be placed) and the mode.
+// Modes: the products on the tensor cores (a split's K and V rows staged in
+// shared memory; the default where they fit), or on the CUDA cores with the V
+// rows in shared memory or read from global memory.
+enum DecAttnMode : int { kAttnCudaCores = 0, kAttnCudaCoresSmemV = 1, kAttnTensorCores = 2 };
 size_t dec_attn_smem(const DecShape& s, int splits, bool v_smem);
-cudaError_t plan_dec_attn(const DecShape& s, int* splits, bool* v_smem);
+size_t dec_attn_tc_smem(const DecShape& s, int splits);
+cudaError_t plan_dec_attn(const DecShape& s, bool cuda_cores, int* splits, int* mode);
 cudaError_t launch_dec_attn(const DecShape& s, const float* q, const __nv_bfloat16* kcache,
-                            const __nv_bfloat16* vcache, const DecState* st, float* merged, int splits, bool v_smem,
+                            const __nv_bfloat16* vcache, const DecState* st, float* merged, int splits, int mode,
                             cudaStream_t stream, bool pdl);
 
 // Decode step, layer part 3: x += wo . merged.

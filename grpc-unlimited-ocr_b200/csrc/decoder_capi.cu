@@ -69,7 +69,7 @@ struct uocr_decoder {
   bool int8 = false;
   int sm_count = 1;
   int splits = 1;        // attention blocks (one cluster) per key/value head
-  bool v_smem = true;    // the attention keeps a split's V rows in shared memory
+  int attn_mode = 0;     // DecAttnMode of the decode attention
   int64_t qkv_rows = 0;  // (heads + 2 kv) * 128
   uocr_moe_plan* moe = nullptr;
   std::vector<DecLayer> layers;
@@ -218,7 +218,7 @@ int decode_step(uocr_decoder* p, cudaStream_t stream, cudaEvent_t* ev = nullptr)
                            p->inv_freq, p->state, p->q, kc_of(p, l), vc_of(p, l), p->sm_count, stream, pdl),
             "decode: q/k/v");
     DEC_TRY(mark(l, 1), "decode: event");
-    DEC_TRY(launch_dec_attn(s, p->q, kc_of(p, l), vc_of(p, l), p->state, p->merged, p->splits, p->v_smem, stream,
+    DEC_TRY(launch_dec_attn(s, p->q, kc_of(p, l), vc_of(p, l), p->state, p->merged, p->splits, p->attn_mode, stream,
                             pdl),
             "decode: attention");
     DEC_TRY(mark(l, 2), "decode: event");
@@ -270,7 +270,8 @@ int uocr_decoder_create(const uocr_decoder_desc* desc, uocr_decoder** out) {
   int sms = 0;
   cudaError_t st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.device);
   if (st == cudaSuccess) st = prepare_decoder_kernels();
-  if (st == cudaSuccess) st = plan_dec_attn(p->shape, &p->splits, &p->v_smem);
+  if (st == cudaSuccess)
+    st = plan_dec_attn(p->shape, (d.flags & UOCR_DECODER_CUDA_CORE_ATTENTION) != 0, &p->splits, &p->attn_mode);
   if (st != cudaSuccess) {
     delete p;
     return dcuda(st, "decoder_create: device set-up");

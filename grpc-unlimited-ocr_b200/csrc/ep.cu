@@ -143,23 +143,22 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, Ep
                                                          const int* __restrict__ pos_of,
                                                          const int* __restrict__ remote_base,
                                                          const float* shared_out, const float* resid, float* y) {
+  __shared__ CombineList list;
   const int t = blockIdx.x;
   if (t >= T) return;
+  const int64_t b = static_cast<int64_t>(t) * K;
   CombineRow r;
-  r.n = K;
-#pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j) {
-    if (j >= K) break;
-    const int e = ids[static_cast<int64_t>(t) * K + j];
-    const int p = pos_of[static_cast<int64_t>(t) * K + j];
-    r.eid[j] = e;
-    r.w[j] = weights[static_cast<int64_t>(t) * K + j];
-    r.src[j] = (p < 0 || e < 0 || e >= m.experts)
+  order_selections(
+      K, [&](int i) { return ids[b + i]; },
+      [&](int j, int e, float* w, const __nv_bfloat16** src) {
+        const int p = pos_of[b + j];
+        *w = weights[b + j];
+        *src = (p < 0 || e < 0 || e >= m.experts)
                    ? nullptr
                    : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner[e * m.world + m.rank]] + lay.yrecv) +
                          (static_cast<int64_t>(remote_base[e]) + p) * H;
-  }
-  sort_selections(r);
+      },
+      &list, r);
   const int64_t o = static_cast<int64_t>(t) * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     combine_cols8(r, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,

@@ -1,6 +1,6 @@
-// Prefill path (rows > 16): router logits for many rows, top-k, the
-// token -> expert permutation, and the weighted combine. The expert GEMMs are
-// the tcgen05 grouped GEMM (tc_gemm.cu).
+// Prefill path (rows > 16): top-k, the token -> expert permutation, and the
+// weighted combine. The router logits for many rows are router_rows.cu's; the
+// expert GEMMs are the tcgen05 grouped GEMM (tc_gemm.cu).
 //
 // The permutation is a histogram / exclusive scan / scatter that keeps every
 // expert's rows in token order, so the permuted layout — and everything
@@ -17,126 +17,7 @@
 namespace uocr_b200 {
 namespace {
 
-constexpr int kRouterTokens = 32;   // rows per router block
-constexpr int kRouterExperts = 32;  // experts per router block
-constexpr int kRouterChunk = 64;    // K elements staged per step
 constexpr int kPermBlock = 256;     // rows per permutation block (8 warps x 32)
-
-__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// logits[t, e] in the reference's dot order (eight lane partial sums over
-// i = 8j + lane, fixed tree, tail, bias: src/backend/reference/ops.cpp:25-38,
-// :91-109), every product and sum separately rounded. Block = 32 rows x 8
-// lanes; blockIdx.y selects 32 experts. K is staged in chunks of 64 by
-// asynchronous 4-byte copies straight into a lane-major layout
-// ([row][lane][j], rows padded to 12 floats: conflict-free 16-byte reads), two
-// buffers deep, so the next chunk streams in while this one is multiplied.
-constexpr int kRouterPer = kRouterChunk / 8;  // chain elements per lane per chunk
-constexpr int kRouterPad = kRouterPer + 4;
-constexpr int kRouterTile = kRouterTokens * 8 * kRouterPad;  // floats per operand tile
-size_t router_rows_smem_bytes() { return static_cast<size_t>(4) * kRouterTile * sizeof(float); }
-
-__global__ void __launch_bounds__(256) router_logits_rows_kernel(const float* __restrict__ x, int T, int H,
-                                                                 const float* __restrict__ router,
-                                                                 const float* __restrict__ bias, int E,
-                                                                 float* __restrict__ logits) {
-  extern __shared__ __align__(16) float rsm[];  // [2 buffers][x tile, w tile]
-  const int tid = threadIdx.x;
-  const int lane8 = tid & 7, tl = tid >> 3;
-  const int t = blockIdx.x * kRouterTokens + tl;
-  const int e0 = blockIdx.y * kRouterExperts;
-  const int ne = min(kRouterExperts, E - e0);
-  const int full = H & ~7;
-  const int nchunks = (full + kRouterChunk - 1) / kRouterChunk;
-  auto stage = [&](int chunk) {
-    float* xs = rsm + (chunk & 1) * 2 * kRouterTile;
-    float* ws = xs + kRouterTile;
-    const int k0 = chunk * kRouterChunk;
-    const int kc = min(kRouterChunk, full - k0);
-#pragma unroll
-    for (int u = 0; u < kRouterTokens * kRouterChunk / 256; ++u) {
-      const int i = tid + u * 256;
-      const int r = i / kRouterChunk, c = i % kRouterChunk;
-      const int tr = blockIdx.x * kRouterTokens + r;
-      const bool ok = c < kc && tr < T;
-      cp_async4(xs + (r * 8 + (c & 7)) * kRouterPad + (c >> 3), ok ? x + static_cast<int64_t>(tr) * H + k0 + c : x,
-                ok);
-      const bool okw = c < kc && r < ne;
-      cp_async4(ws + (r * 8 + (c & 7)) * kRouterPad + (c >> 3),
-                okw ? router + static_cast<int64_t>(e0 + r) * H + k0 + c : router, okw);
-    }
-    cp_async_commit();
-  };
-  float acc[kRouterExperts];
-#pragma unroll
-  for (int i = 0; i < kRouterExperts; ++i) acc[i] = 0.0f;
-  if (nchunks > 0) stage(0);
-  for (int ch = 0; ch < nchunks; ++ch) {
-    if (ch + 1 < nchunks) {
-      stage(ch + 1);
-      cp_async_wait_one();
-    } else {
-      cp_async_wait_all();
-    }
-    __syncthreads();
-    const float* xs = rsm + (ch & 1) * 2 * kRouterTile;
-    const float* ws = xs + kRouterTile;
-    const int per = min(kRouterChunk, full - ch * kRouterChunk) >> 3;
-    const float* xr = xs + (tl * 8 + lane8) * kRouterPad;
-    if (per == kRouterPer) {
-#pragma unroll
-      for (int m = 0; m < kRouterPer; m += 4) {
-        const float4 xv = *reinterpret_cast<const float4*>(xr + m);
-#pragma unroll
-        for (int i = 0; i < kRouterExperts; ++i) {
-          const float4 wv = *reinterpret_cast<const float4*>(ws + (i * 8 + lane8) * kRouterPad + m);
-          float a = acc[i];
-          a = __fadd_rn(a, __fmul_rn(xv.x, wv.x));
-          a = __fadd_rn(a, __fmul_rn(xv.y, wv.y));
-          a = __fadd_rn(a, __fmul_rn(xv.z, wv.z));
-          a = __fadd_rn(a, __fmul_rn(xv.w, wv.w));
-          acc[i] = a;
-        }
-      }
-    } else {
-      for (int m = 0; m < per; ++m) {
-        const float xv = xr[m];
-#pragma unroll
-        for (int i = 0; i < kRouterExperts; ++i)
-          acc[i] = __fadd_rn(acc[i], __fmul_rn(xv, ws[(i * 8 + lane8) * kRouterPad + m]));
-      }
-    }
-    __syncthreads();  // this buffer is refilled two chunks on
-  }
-  // Combine the eight lanes of each (row, expert): lanes of a row are eight
-  // consecutive threads of one warp.
-  const int base = (tid & 31) & ~7;
-#pragma unroll
-  for (int i = 0; i < kRouterExperts; ++i) {  // unrolled: acc stays in registers
-    if (i >= ne) break;
-    float a[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) a[q] = __shfl_sync(0xffffffffu, acc[i], base + q);
-    if (lane8 == 0 && t < T) {
-      const int e = e0 + i;
-      const float* xrow = x + static_cast<int64_t>(t) * H;
-      const float* wr = router + static_cast<int64_t>(e) * H;
-      float tail = 0.0f;
-      for (int c = full; c < H; ++c) tail = __fadd_rn(tail, __fmul_rn(__ldg(xrow + c), __ldg(wr + c)));
-      const float lo = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
-      const float hi = __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7]));
-      float sum = __fadd_rn(__fadd_rn(lo, hi), tail);
-      if (bias != nullptr) sum = __fadd_rn(sum, bias[e]);
-      logits[static_cast<int64_t>(t) * E + e] = sum;
-    }
-  }
-}
 
 __global__ void __launch_bounds__(256) topk_rows_i32_kernel(const float* __restrict__ logits, int T, int E, int K,
                                                             int renorm, int* ids, float* weights) {
@@ -299,19 +180,19 @@ __global__ void __launch_bounds__(256) combine_kernel(int T, int H, int K, const
                                                       const int* __restrict__ pos_of,
                                                       const __nv_bfloat16* __restrict__ yperm,
                                                       const float* shared_out, const float* resid, float* y) {
+  __shared__ CombineList list;
   const int t = blockIdx.x;
   if (t >= T) return;
+  const int64_t b = static_cast<int64_t>(t) * K;
   CombineRow r;
-  r.n = K;
-#pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j) {
-    if (j >= K) break;
-    r.eid[j] = ids[static_cast<int64_t>(t) * K + j];
-    r.w[j] = weights[static_cast<int64_t>(t) * K + j];
-    const int p = pos_of[static_cast<int64_t>(t) * K + j];
-    r.src[j] = p < 0 ? nullptr : yperm + static_cast<int64_t>(p) * H;
-  }
-  sort_selections(r);
+  order_selections(
+      K, [&](int i) { return ids[b + i]; },
+      [&](int j, int, float* w, const __nv_bfloat16** src) {
+        *w = weights[b + j];
+        const int p = pos_of[b + j];
+        *src = p < 0 ? nullptr : yperm + static_cast<int64_t>(p) * H;
+      },
+      &list, r);
   const int64_t o = static_cast<int64_t>(t) * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     combine_cols8(r, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
@@ -352,24 +233,6 @@ void carve_prefill_scratch(const PrefillDims& d, void* base, PrefillScratch* s, 
     s->yperm = reinterpret_cast<__nv_bfloat16*>(take(T * K * H * 2));
   }
   s->bytes = off;
-}
-
-cudaError_t launch_router_logits_rows(const float* x, int T, int H, const float* router, const float* bias, int E,
-                                      float* logits, cudaStream_t stream) {
-  if (T == 0) return cudaSuccess;
-  static bool attr_done[kMaxDevices] = {};
-  int dev = 0;
-  cudaError_t st = cudaGetDevice(&dev);
-  if (st != cudaSuccess) return st;
-  if (dev < kMaxDevices && !attr_done[dev]) {
-    st = cudaFuncSetAttribute(router_logits_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(router_rows_smem_bytes()));
-    if (st != cudaSuccess) return st;
-    attr_done[dev] = true;
-  }
-  const dim3 grid((T + kRouterTokens - 1) / kRouterTokens, (E + kRouterExperts - 1) / kRouterExperts);
-  router_logits_rows_kernel<<<grid, 256, router_rows_smem_bytes(), stream>>>(x, T, H, router, bias, E, logits);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_route(const PrefillCall& c, cudaStream_t stream) {

@@ -24,6 +24,7 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 PLAN_NO_GRAPHS = 1
 PLAN_EP_STRIDED = 4
 PLAN_PRE_NORM = 8
+DECODER_CUDA_CORE_ATTENTION = 1
 EP_HANDLE_BYTES = 256
 
 # Synthetic tensor kinds (one generator stream per tensor per layer).
@@ -42,7 +43,7 @@ DECODER_EXPORTS = [
 EXPORTS = [
     "uocr_last_error", "uocr_abi_version", "uocr_moe_plan_create", "uocr_moe_plan_destroy", "uocr_moe_plan_bytes",
     "uocr_moe_set_layer", "uocr_moe_set_layer_parts", "uocr_checkpoint_open", "uocr_checkpoint_close",
-    "uocr_checkpoint_count", "uocr_checkpoint_tensor", "uocr_moe_load_layer", "uocr_moe_forward", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
+    "uocr_checkpoint_count", "uocr_checkpoint_tensor", "uocr_moe_load_layer", "uocr_moe_forward", "uocr_moe_router_logits", "uocr_moe_forward_stack", "uocr_moe_check", "uocr_moe_profile_stack",
     "uocr_moe_ep_handle", "uocr_moe_ep_connect", "uocr_moe_ep_connect_local", "uocr_moe_ep_forward_local",
     "uocr_ops_check", "uocr_expert_topk",
     "uocr_expert_ffn_one", "uocr_expert_ffn_one_noalloc", "uocr_expert_ffn_one_q8", "uocr_linear", "uocr_quantize_q8", "uocr_synth_fill", "uocr_synth_stream",
@@ -130,6 +131,7 @@ def lib() -> ctypes.CDLL:
         L.uocr_checkpoint_tensor.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(TensorView)]
         L.uocr_moe_load_layer.argtypes = [vp, vp, i64, i64, vp]
         L.uocr_moe_forward.argtypes = [vp, i64, vp, i64, vp, vp, vp, vp]
+        L.uocr_moe_router_logits.argtypes = [vp, i64, vp, i64, vp, vp]
         L.uocr_moe_forward_stack.argtypes = [vp, vp, i64, vp]
         L.uocr_moe_check.argtypes = [vp, vp]
         L.uocr_moe_profile_stack.argtypes = [vp, vp, i64, i32, ctypes.POINTER(f32), vp]
@@ -261,6 +263,11 @@ class Plan:
         rows = x.shape[0] if rows is None else rows
         _check(lib().uocr_moe_forward(self.h, layer, _ptr(x), rows, _ptr(y), _ptr(ids), _ptr(weights),
                                       _stream(stream)))
+
+    def router_logits(self, layer: int, x, logits, stream=None, rows: int | None = None):
+        """logits [rows, E] = the layer's router gate on x (+ bias, after the plan's pre-norm)."""
+        rows = x.shape[0] if rows is None else rows
+        _check(lib().uocr_moe_router_logits(self.h, layer, _ptr(x), rows, _ptr(logits), _stream(stream)))
 
     def forward_stack(self, h, stream=None, rows: int | None = None):
         rows = h.shape[0] if rows is None else rows
@@ -420,10 +427,10 @@ class Decoder:
 
     def __init__(self, hidden, layers, heads, kv_heads, vocab, max_positions, max_prefill, experts, top_k, ffn,
                  shared_ffn, weight_format: int = WEIGHT_BF16, renormalize: bool = True, rope_theta: float = 1e4,
-                 rms_norm_eps: float = 1e-6, device: int = 0):
+                 rms_norm_eps: float = 1e-6, device: int = 0, flags: int = 0):
         self.desc = DecoderDesc(hidden, layers, heads, kv_heads, 128, vocab, max_positions, max_prefill, experts,
                                 top_k, ffn, shared_ffn, rope_theta, rms_norm_eps, weight_format, int(renormalize),
-                                device, 0)
+                                device, flags)
         h = ctypes.c_void_p()
         _check(lib().uocr_decoder_create(ctypes.byref(self.desc), ctypes.byref(h)))
         self.h = h

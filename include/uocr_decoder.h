@@ -50,8 +50,12 @@ typedef struct uocr_decoder_desc {
   int32_t weight_format;     /* uocr_weight_format: bf16, or per-output-channel int8 for every projection */
   int32_t renormalize;       /* MoE top-k weights divided by their sum */
   int32_t device;
-  int32_t flags;             /* 0 */
+  int32_t flags;             /* UOCR_DECODER_* bits */
 } uocr_decoder_desc;
+
+/* The decode attention's products on the CUDA cores instead of the tensor
+ * cores (the default wherever a split's K and V rows fit in shared memory). */
+#define UOCR_DECODER_CUDA_CORE_ATTENTION 1
 
 /* One layer's weights, fp32 or bf16 (dtype), host or device (memory); the
  * norm gains and the router are fp32. They are converted on the device to

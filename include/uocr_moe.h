@@ -215,6 +215,16 @@ int uocr_moe_load_layer(uocr_moe_plan* plan, const uocr_checkpoint* ckpt, int64_
 int uocr_moe_forward(uocr_moe_plan* plan, int64_t layer, const float* x, int64_t rows, float* y, int32_t* ids,
                      float* weights, void* stream);
 
+/* logits [rows, E] = the layer's router gate on x [rows, H] (+ its bias; the
+ * plan's pre-norm first when it has one): the gemm_nt of CudaDecoder::moe
+ * (src/model/cuda/cuda_decoder.cpp:139-140) and ref::linear of
+ * MixtureOfExperts::forward (src/model/feed_forward.cpp:38), in the CPU
+ * reference's dot order (src/backend/reference/ops.cpp:25-38, :91-109), with
+ * the kernel forward uses at that row count. Device pointers; x is 16-byte
+ * aligned. */
+int uocr_moe_router_logits(uocr_moe_plan* plan, int64_t layer, const float* x, int64_t rows, float* logits,
+                           void* stream);
+
 /* h <- h + MoE_l(h) for l = 0 .. layers-1, in place on device memory h
  * [rows, H]: the decoder's residual around its feed-forward block
  * (src/model/decoder.cpp:181,201) with nothing between the layers. h is

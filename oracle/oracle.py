@@ -197,6 +197,18 @@ def moe_forward(w: MoeWeights, x: np.ndarray, top_k: int, renormalize: bool, thr
     return MoeResult(y, ids, wts, logits, margin, om)
 
 
+def linear(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None, threads: int = 0) -> np.ndarray:
+    """y [m, n] = x [m, k] . w [n, k]^T (+ bias) in the reference's dot order
+    (src/backend/reference/ops.cpp:25-38, :91-109): oracle_linear."""
+    x, w = _c(x), _c(w)
+    m, k = x.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float32)
+    b = None if bias is None else _c(bias)
+    lib().oracle_linear(_p(x), m, k, _p(w), n, None if b is None else _p(b), _p(y), threads)
+    return y
+
+
 def rms_norm(x: np.ndarray, weight: np.ndarray | None, eps: float) -> np.ndarray:
     """The decoder's pre-feed-forward RMSNorm, restated from
     src/backend/reference/ops.cpp:129-141: per row, ss = the sum in index order

@@ -30,13 +30,13 @@ def _device_layer(torch, cuda, L: D.DecoderLayer):
             "shared_down": f(L.moe.shared_down)}
 
 
-def _build(torch, cuda, shape, fmt, seed=5):
+def _build(torch, cuda, shape, fmt, seed=5, flags=0):
     H, layers, heads, kv, vocab, E, K, F, S, n, steps = shape
     dims = D.DecoderDims(H, layers, heads, kv, 128, vocab, E, K, F, S)
     w_dev = D.synth_weights(dims, seed, int8=False, norm_sigma=0.1)  # the device quantises these itself
     w_ora = D.synth_weights(dims, seed, int8=fmt == M.WEIGHT_INT8, norm_sigma=0.1)
     dec = M.Decoder(H, layers, heads, kv, vocab, max_positions=n + steps + 3, max_prefill=n, experts=E, top_k=K,
-                    ffn=F, shared_ffn=S, weight_format=fmt)
+                    ffn=F, shared_ffn=S, weight_format=fmt, flags=flags)
     keep = []
     for li, L in enumerate(w_dev.layers):
         t = _device_layer(torch, cuda, L)
@@ -64,11 +64,16 @@ def _run(torch, cuda, dec, prompt, vocab, steps, stream):
     return logits0.cpu().numpy(), int(tok0.item()), toks.cpu().numpy(), lg.cpu().numpy()
 
 
+# The decode attention on the tensor cores (the default) and on the CUDA cores.
+ATTENTION = {"tensor_cores": 0, "cuda_cores": M.DECODER_CUDA_CORE_ATTENTION}
+
+
+@pytest.mark.parametrize("attention", list(ATTENTION))
 @pytest.mark.parametrize("fmt", [M.WEIGHT_BF16, M.WEIGHT_INT8])
 @pytest.mark.parametrize("shape", SHAPES)
-def test_decoder_against_oracle(cuda, shape, fmt):
+def test_decoder_against_oracle(cuda, shape, fmt, attention):
     import torch
-    dims, dec, w_ora = _build(torch, cuda, shape, fmt)
+    dims, dec, w_ora = _build(torch, cuda, shape, fmt, flags=ATTENTION[attention])
     n, steps = shape[-2], shape[-1]
     prompt = D.synth_prompt(dims, 5, n)
     side = torch.cuda.Stream()

@@ -60,6 +60,39 @@ def test_prefill_small_shapes(cuda, T, H, E, K, F, S, renorm):
     np.testing.assert_allclose(wts, want.weights, rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("T,H,E,bias,pre_norm", [
+    (1, 256, 8, False, False), (7, 512, 64, True, False), (16, 2048, 64, False, True),  # the decode routers
+    (17, 256, 8, False, False), (100, 512, 40, True, False), (333, 1024, 128, False, False),
+    (4100, 2048, 64, True, False), (300, 768, 64, False, True)])
+def test_router_logits_bitwise(cuda, T, H, E, bias, pre_norm):
+    """The router gate in the reference's fp32 dot order: bitwise equal to the
+    oracle's restatement of ref::linear (and of its RMSNorm first) on every row
+    count, both router kernels, partial expert tiles (E = 40) and a bias."""
+    import torch
+    rng = np.random.default_rng(T + E)
+    w = _tiny_layer(rng, H, E, 128, 128)
+    if bias:
+        w.router_bias = (rng.standard_normal(E) * 0.5).astype(np.float32)
+    gain = (1.0 + 0.2 * rng.standard_normal(H)).astype(np.float32)
+    plan = M.Plan(M.Dims(H, E, min(4, E), 128, 128), max_rows=T, router_bias=bias,
+                  flags=M.PLAN_PRE_NORM if pre_norm else 0, rms_norm_eps=1e-5)
+    keep = _upload(plan, w, torch, cuda)
+    if pre_norm:
+        keep["norm"] = torch.from_numpy(gain).to(cuda)
+        plan.set_layer(0, keep["router"], keep["gate"], keep["up"], keep["down"], keep["shared_gate"],
+                       keep["shared_up"], keep["shared_down"], router_bias=keep.get("router_bias"), norm=keep["norm"])
+    x = (rng.standard_normal((T, H)) * 2.0).astype(np.float32)
+    logits = torch.full((T, E), float("nan"), device=cuda)
+    plan.router_logits(0, torch.from_numpy(x).to(cuda), logits)
+    plan.check()
+    xin = O.rms_norm(x, gain, 1e-5) if pre_norm else x
+    want = O.linear(xin, w.router, w.router_bias)
+    got = to_np(logits)
+    bad = np.argwhere(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{len(bad)} logits differ, first {bad[:3].tolist()}"
+    del keep
+
+
 def test_prefill_skewed_expert_load(cuda):
     """Most rows routed to a handful of experts (a large router bias), some experts empty."""
     import torch
