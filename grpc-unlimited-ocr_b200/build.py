@@ -23,10 +23,6 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", 
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
 
 
-# Per-source flags (none at present).
-FILE_FLAGS: dict[str, list[str]] = {}
-
-
 def _headers():
     return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
         glob.glob(os.path.join(ROOT, "include", "*.h"))
@@ -37,7 +33,7 @@ def _compile(src: str, verbose_ptxas: bool) -> str:
     newest_dep = max([os.path.getmtime(src)] + [os.path.getmtime(h) for h in _headers()])
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest_dep and not verbose_ptxas:
         return obj
-    cmd = [NVCC, *ARCH, *FLAGS, *FILE_FLAGS.get(os.path.basename(src), []), "-c", src, "-o", obj]
+    cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)
