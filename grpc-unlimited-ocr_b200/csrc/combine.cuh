@@ -9,18 +9,13 @@
 
 namespace uocr_b200 {
 
-// A row's selections in combine order: weight and the expert output row (bf16).
-struct CombineRow {
-  int n;
-  float w[kMaxTopK];
-  const __nv_bfloat16* src[kMaxTopK];
-};
-
 // The selections of the block's row in ascending expert id (a stable
-// order: equal ids keep their slot order). Thread j < n fetches selection j
-// and counts the selections ahead of it; the ranked weight and row pointer go
-// to shared memory, and after the barrier every thread reads the ordered list.
-// One rank per selection instead of a sorting network in every thread.
+// order: equal ids keep their slot order): weight and expert output row
+// (bf16; null for a dropped selection). Thread j < n fetches selection j and
+// counts the selections ahead of it; the ranked weight and row pointer go to
+// shared memory, which every thread then reads — one rank per selection
+// instead of a sorting network in every thread, and no per-thread copy of the
+// list in registers.
 struct CombineList {
   float w[kMaxTopK];
   const __nv_bfloat16* src[kMaxTopK];
@@ -30,8 +25,7 @@ struct CombineList {
 // expert output row (null for a dropped selection). Every thread of the block
 // calls this (it holds a barrier).
 template <class IdOf, class Fetch>
-__device__ __forceinline__ void order_selections(int n, IdOf id_of, Fetch fetch, CombineList* list,
-                                                 CombineRow& r) {
+__device__ __forceinline__ void order_selections(int n, IdOf id_of, Fetch fetch, CombineList* list) {
   const int j = threadIdx.x;
   if (j < n) {
     const int e = id_of(j);
@@ -47,25 +41,18 @@ __device__ __forceinline__ void order_selections(int n, IdOf id_of, Fetch fetch,
     list->src[rank] = src;
   }
   __syncthreads();
-  r.n = n;
-#pragma unroll
-  for (int q = 0; q < kMaxTopK; ++q) {
-    if (q >= n) break;
-    r.w[q] = list->w[q];
-    r.src[q] = list->src[q];
-  }
 }
 
-// Columns c .. c+7 of the row: every selection's 16 bytes are loaded before
-// any is added (src[j] null: a dropped selection).
-__device__ __forceinline__ void combine_cols8(const CombineRow& r, int64_t c, const float* shared_row,
+// Columns c .. c+7 of the row (its n ordered selections in r): every
+// selection's 16 bytes are loaded before any is added.
+__device__ __forceinline__ void combine_cols8(const CombineList& r, int n, int64_t c, const float* shared_row,
                                               const float* resid_row, float* y_row) {
   // Every load of the 8 columns first (expert rows, shared output, residual),
   // then the arithmetic.
   uint4 pk[kMaxTopK];
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j)
-    if (j < r.n && r.src[j] != nullptr) pk[j] = __ldcg(reinterpret_cast<const uint4*>(r.src[j] + c));
+    if (j < n && r.src[j] != nullptr) pk[j] = __ldcg(reinterpret_cast<const uint4*>(r.src[j] + c));
   float4 sa = make_float4(0, 0, 0, 0), sb = sa, ra = sa, rb = sa;
   if (shared_row != nullptr) {
     sa = __ldcg(reinterpret_cast<const float4*>(shared_row + c));
@@ -78,7 +65,7 @@ __device__ __forceinline__ void combine_cols8(const CombineRow& r, int64_t c, co
   float routed[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) {
-    if (j >= r.n || r.src[j] == nullptr) continue;
+    if (j >= n || r.src[j] == nullptr) continue;
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {

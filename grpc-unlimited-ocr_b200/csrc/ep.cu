@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
 // y[t, c] = shared[t, c] + sum over t's experts in ascending id of w * (the
 // owner's yrecv row), + resid: the single-GPU combine (combine.cuh) with the
 // rows read from the owners. One block per row.
-__global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, EpMap m, EpPeers peers, EpLayout lay,
+__global__ void __launch_bounds__(256, 3) ep_combine_kernel(int T, int H, int K, EpMap m, EpPeers peers, EpLayout lay,
                                                          const int* __restrict__ ids,
                                                          const float* __restrict__ weights,
                                                          const int* __restrict__ pos_of,
@@ -147,7 +147,6 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, Ep
   const int t = blockIdx.x;
   if (t >= T) return;
   const int64_t b = static_cast<int64_t>(t) * K;
-  CombineRow r;
   order_selections(
       K, [&](int i) { return ids[b + i]; },
       [&](int j, int e, float* w, const __nv_bfloat16** src) {
@@ -158,10 +157,10 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(int T, int H, int K, Ep
                    : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner[e * m.world + m.rank]] + lay.yrecv) +
                          (static_cast<int64_t>(remote_base[e]) + p) * H;
       },
-      &list, r);
+      &list);
   const int64_t o = static_cast<int64_t>(t) * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
-    combine_cols8(r, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
+    combine_cols8(list, K, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
                   y + o);
 }
 

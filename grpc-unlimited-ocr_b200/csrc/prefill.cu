@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restri
 // y[t, c] = shared[t, c] + sum over t's experts in ascending id of w * yperm[pos, c]
 // (+ resid[t, c] in the stack), the reference's addition order
 // (src/model/feed_forward.cpp:65-76). One block per row, 8 columns per thread.
-__global__ void __launch_bounds__(256) combine_kernel(int T, int H, int K, const int* __restrict__ ids,
+__global__ void __launch_bounds__(256, 3) combine_kernel(int T, int H, int K, const int* __restrict__ ids,
                                                       const float* __restrict__ weights,
                                                       const int* __restrict__ pos_of,
                                                       const __nv_bfloat16* __restrict__ yperm,
@@ -184,7 +184,6 @@ __global__ void __launch_bounds__(256) combine_kernel(int T, int H, int K, const
   const int t = blockIdx.x;
   if (t >= T) return;
   const int64_t b = static_cast<int64_t>(t) * K;
-  CombineRow r;
   order_selections(
       K, [&](int i) { return ids[b + i]; },
       [&](int j, int, float* w, const __nv_bfloat16** src) {
@@ -192,10 +191,10 @@ __global__ void __launch_bounds__(256) combine_kernel(int T, int H, int K, const
         const int p = pos_of[b + j];
         *src = p < 0 ? nullptr : yperm + static_cast<int64_t>(p) * H;
       },
-      &list, r);
+      &list);
   const int64_t o = static_cast<int64_t>(t) * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
-    combine_cols8(r, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
+    combine_cols8(list, K, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
                   y + o);
 }
 
