@@ -137,6 +137,9 @@ struct uocr_moe_plan {
   bool ep_connected = false;
   bool ep_local_group = false;
   uint64_t ep_wait_ns = 20ull * 1000 * 1000 * 1000;  // UOCR_EP_WAIT_MS at creation, default 20 s
+  // The shared expert's stream under expert parallelism (overlaps the pull).
+  cudaStream_t ep_side = nullptr;
+  cudaEvent_t ep_fork = nullptr, ep_join = nullptr;
 
   // Captured forward_stack graphs, keyed by (h, rows, stream); least recently used evicted.
   struct GraphEntry {
@@ -386,6 +389,9 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     // A block of its own: CUDA IPC exports whole cudaMalloc allocations.
     st = cudaMalloc(&p->exchange, p->elay.bytes);
     if (st == cudaSuccess) st = cudaMemset(p->exchange, 0, p->elay.bytes);
+    if (st == cudaSuccess) st = cudaStreamCreateWithFlags(&p->ep_side, cudaStreamNonBlocking);
+    if (st == cudaSuccess) st = cudaEventCreateWithFlags(&p->ep_fork, cudaEventDisableTiming);
+    if (st == cudaSuccess) st = cudaEventCreateWithFlags(&p->ep_join, cudaEventDisableTiming);
     if (st != cudaSuccess) {
       uocr_moe_plan_destroy(p);
       return cuda_fail(st, "plan_create: exchange region");
@@ -409,6 +415,9 @@ int uocr_moe_plan_destroy(uocr_moe_plan* p) {
   if (p->arena != nullptr) cudaFree(p->arena);
   for (char* q : p->opened) cudaIpcCloseMemHandle(q);
   if (p->exchange != nullptr) cudaFree(p->exchange);
+  if (p->ep_fork != nullptr) cudaEventDestroy(p->ep_fork);
+  if (p->ep_join != nullptr) cudaEventDestroy(p->ep_join);
+  if (p->ep_side != nullptr) cudaStreamDestroy(p->ep_side);
   delete p;
   return UOCR_OK;
 }
@@ -707,6 +716,9 @@ EpCall ep_call(const uocr_moe_plan* p, const LayerDev& L, const float* x, int64_
   c.up_local = as_bf16(L.up);
   c.down_local = as_bf16(L.down);
   c.wait_ns = p->ep_wait_ns;
+  c.side = p->ep_side;
+  c.fork = p->ep_fork;
+  c.join = p->ep_join;
   return c;
 }
 

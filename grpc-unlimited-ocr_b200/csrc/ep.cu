@@ -376,10 +376,25 @@ cudaError_t ep_forward(const EpCall& c, cudaStream_t stream, cudaEvent_t* ev) {
   if ((st = ep_arrive(c, stream)) != cudaSuccess || (st = ep_wait(c, 61, stream)) != cudaSuccess ||
       (st = mark(1)) != cudaSuccess)
     return st;
+  // The shared expert needs only this rank's own rows (x^): on the side
+  // stream it runs while the pull, which NVLink bounds, crosses to this rank
+  // and the routed GEMMs follow. The measurement path keeps one stream so
+  // that its phases stay separable.
+  const bool overlap = ev == nullptr && c.side != nullptr && c.pc.rows > 0 && c.pc.dims.shared_ffn > 0;
+  if (overlap) {
+    if ((st = cudaEventRecord(c.fork, stream)) != cudaSuccess ||
+        (st = cudaStreamWaitEvent(c.side, c.fork, 0)) != cudaSuccess || (st = ep_shared(c, c.side)) != cudaSuccess ||
+        (st = cudaEventRecord(c.join, c.side)) != cudaSuccess)
+      return st;
+  }
   if ((st = ep_experts(c, stream, ev != nullptr ? ev[2] : nullptr)) != cudaSuccess || (st = mark(3)) != cudaSuccess)
     return st;
   if ((st = ep_arrive(c, stream)) != cudaSuccess) return st;
-  if ((st = ep_shared(c, stream)) != cudaSuccess) return st;
+  if (overlap) {
+    if ((st = cudaStreamWaitEvent(stream, c.join, 0)) != cudaSuccess) return st;
+  } else if ((st = ep_shared(c, stream)) != cudaSuccess) {
+    return st;
+  }
   if ((st = ep_wait(c, 62, stream)) != cudaSuccess || (st = mark(4)) != cudaSuccess) return st;
   if ((st = ep_combine(c, stream)) != cudaSuccess) return st;
   return mark(5);

@@ -103,6 +103,11 @@ struct EpCall {
   const __nv_bfloat16* up_local;
   const __nv_bfloat16* down_local;
   uint64_t wait_ns;  // how long a barrier waits for the other ranks
+  // A stream of the plan's own and two events: ep_forward runs the shared
+  // expert there while the pull and the routed GEMMs run on the caller's
+  // stream (null: everything on the caller's stream).
+  cudaStream_t side;
+  cudaEvent_t fork, join;
 };
 
 // The phases of one layer; ep_forward runs them with the barriers between.

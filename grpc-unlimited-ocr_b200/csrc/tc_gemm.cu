@@ -7,7 +7,8 @@
 //           (M=128, N=256, K=16, fp32 accumulate) into one of two 256-column
 //           accumulators, and commits stage releases and "tile done";
 //   warps 2-5 epilogue: tcgen05.ld the accumulator (thread = tile row), fuse
-//           SwiGLU (gate columns 0-127, up columns 128-255) or convert, store.
+//           SwiGLU (gate columns 0-127, up columns 128-255) or convert, and
+//           store through a per-warp staging area as whole row segments.
 // Groups are the routed experts (rows = the expert's segment of the permuted
 // activations) plus, optionally, the shared expert over all rows. Tiles are
 // (group, 128-row block, 256-column block), dealt to blocks round-robin.
@@ -32,6 +33,7 @@ constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kStageTileBytes = 32 * 128;  // an epilogue warp's staging area: 32 rows x 128 bytes
 constexpr int kTmemCols = 512;          // two 256-column fp32 accumulators
 constexpr int kThreads = 192;
 constexpr int kMaxGroups = kMaxExperts + 1;
@@ -78,38 +80,6 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* start, int groups,
   const int nt = lo < a.experts ? a.n_tiles_routed : a.n_tiles_shared;
   const int local = t - start[lo];
   return Tile{lo, local / nt, local % nt};
-}
-
-__device__ __forceinline__ void store_bf16x32(void* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 pk;
-    uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
-      w[i] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    d[q] = pk;
-  }
-}
-
-__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
-  float4* d = reinterpret_cast<float4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-}
-
-// dst += v (each output element belongs to one thread of one tile).
-__device__ __forceinline__ void add_f32x32(float* dst, const float (&v)[32]) {
-  float4* d = reinterpret_cast<float4*>(dst);
-  float4 o[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) o[q] = d[q];
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    d[q] = make_float4(o[q].x + v[4 * q], o[q].y + v[4 * q + 1], o[q].z + v[4 * q + 2], o[q].w + v[4 * q + 3]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __grid_constant__ KernelArgs args) {
@@ -250,8 +220,58 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
     }
   } else {
     // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+    // A thread holds one row's 32 columns after each tcgen05.ld; they pass
+    // through a 4 KB swizzled staging area of the warp so that the stores
+    // leave as whole 64-byte (bf16) or 128-byte (fp32) row segments, several
+    // rows per instruction, instead of 32 rows x 16 bytes.
     const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
+    unsigned char* stg = smem + kStages * kStageBytes + (warp - 2) * kStageTileBytes;
+    // This lane's 32 values as bf16 into its row of the staging area, then
+    // out: lane j of pass i takes 16 bytes of row (32 i + j) / 4.
+    auto put_bf16 = [&](const float (&v)[32], __nv_bfloat16* out, int64_t ld, int64_t row0, int nvalid) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 pk;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v[k * 8 + 2 * i], v[k * 8 + 2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(stg + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) = pk;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int idx = it * 32 + lane, rr = idx >> 2, k = idx & 3;
+        const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
+        if (rr < nvalid) *reinterpret_cast<uint4*>(out + (row0 + rr) * ld + k * 8) = val;
+      }
+      __syncwarp();
+    };
+    // The same for fp32 (128 bytes a row); acc: out += v.
+    auto put_f32 = [&](const float (&v)[32], float* out, int64_t ld, int64_t row0, int nvalid, bool acc) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<float4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int idx = it * 32 + lane, rr = idx >> 3, k = idx & 7;
+        const float4 val = *reinterpret_cast<const float4*>(stg + rr * 128 + ((k ^ (rr & 7)) << 4));
+        if (rr < nvalid) {
+          float4* d = reinterpret_cast<float4*>(out + (row0 + rr) * ld + k * 4);
+          if (acc) {
+            const float4 o = *d;
+            *d = make_float4(o.x + val.x, o.y + val.y, o.z + val.z, o.w + val.w);
+          } else {
+            *d = val;
+          }
+        }
+      }
+      __syncwarp();
+    };
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       const Tile tl = decode_tile(t, tile_start, groups, args);
@@ -264,9 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
       }
       tc_fence_after();
       const int rows = routed ? __ldcg(args.seg_count + tl.g) : args.shared_rows;
-      const int r = tl.m * kBM + row_in_tile;
-      const bool valid = r < rows;
-      const int64_t out_row = (routed ? __ldcg(args.seg_start + tl.g) : 0) + static_cast<int64_t>(r);
+      // This warp's 32 rows: the first is row0 of the output, nvalid of them exist.
+      const int r0 = tl.m * kBM + quarter * 32;
+      const int nvalid = rows - r0 < 0 ? 0 : (rows - r0 > 32 ? 32 : rows - r0);
+      const int64_t row0 = (routed ? __ldcg(args.seg_start + tl.g) : 0) + static_cast<int64_t>(r0);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       if (args.mode == 0) {
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared);
@@ -278,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
           tmem_ld32(taddr + kBN / 2 + c, u);
 #pragma unroll
           for (int i = 0; i < 32; ++i) g[i] = swiglu(g[i], u[i]);
-          if (valid) store_bf16x32(out + out_row * ld + tl.n * (kBN / 2) + c, g);
+          put_bf16(g, out + tl.n * (kBN / 2) + c, ld, row0, nvalid);
         }
       } else {
         const bool f32 = !routed && args.shared_out_f32;
@@ -287,16 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
         for (int c = 0; c < kBN; c += 32) {
           float v[32];
           tmem_ld32(taddr + c, v);
-          if (valid) {
-            if (f32 && args.shared_accumulate)
-              add_f32x32(static_cast<float*>(args.out_shared) + out_row * ld + tl.n * kBN + c, v);
-            else if (f32)
-              store_f32x32(static_cast<float*>(args.out_shared) + out_row * ld + tl.n * kBN + c, v);
-            else
-              store_bf16x32(static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared) + out_row * ld +
-                                tl.n * kBN + c,
-                            v);
-          }
+          if (f32)
+            put_f32(v, static_cast<float*>(args.out_shared) + tl.n * kBN + c, ld, row0, nvalid,
+                    args.shared_accumulate != 0);
+          else
+            put_bf16(v, static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared) + tl.n * kBN + c, ld,
+                     row0, nvalid);
         }
       }
       tc_fence_before();
@@ -343,7 +360,9 @@ bool make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, i
 
 }  // namespace
 
-size_t grouped_gemm_smem_bytes() { return static_cast<size_t>(kStages) * kStageBytes + 1024; }
+size_t grouped_gemm_smem_bytes() {
+  return static_cast<size_t>(kStages) * kStageBytes + 4 * kStageTileBytes + 1024;
+}
 
 cudaError_t launch_grouped_gemm(const GroupedGemm& g, cudaStream_t stream) {
   static bool attr_done[kMaxDevices] = {};
