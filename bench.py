@@ -283,12 +283,11 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         ep_equal = bool(eq.item())
         del y1
         # Bytes this rank moves over NVLink: the rows it pulls from other
-        # ranks for its experts, and the expert outputs its combine pulls
-        # from other owners (bf16 rows of H).
+        # ranks for its experts, and the same rows' expert outputs, which its
+        # down GEMM's epilogue stores back into their ranks (bf16 rows of H).
         pulled = sum(cbs[s][e] for e in range(E) for s in range(world)
                      if owner[e * world + s] == rank and s != rank) * H * 2
-        combined = sum(cbs[rank][e] for e in range(E) if owner[e * world + rank] != rank) * H * 2
-        link = torch.tensor([pulled, prof["pull"], combined, prof["combine"]], dtype=torch.float64, device=dev)
+        link = torch.tensor([pulled, prof["pull"], pulled, prof["expert_gemms"]], dtype=torch.float64, device=dev)
         links = [torch.empty_like(link) for _ in range(world)]
         dist.all_gather(links, link)
         links = [v.cpu().tolist() for v in links]
@@ -329,7 +328,8 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         desc = {"balanced": "load-balanced owner table (hot experts replicated)",
                 "strided": "e % G", "contiguous": "contiguous ranges e // (E / G)"}[placement]
         out["parallelism"] = f"expert-parallel x{world}: {desc}, {min(slots)}-{max(slots)} experts and " \
-                             f"{total // world} rows per GPU; rows and outputs pulled over NVLink by peer loads"
+                             f"{total // world} rows per GPU; rows pulled over NVLink by peer loads, outputs stored back by the " \
+                             f"down GEMM's epilogue (peer stores)"
         out["roofline"] = {"bound": "tensor", "kernel": "whole layer per GPU", "achieved": per_gpu, "peak": peak,
                            "peak_source": peak_src, "unit": "TFLOP/s", "frac": per_gpu / peak,
                            "algorithmic_flops_per_layer": total_flops}
@@ -340,11 +340,14 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         # NVLink: bytes each rank pulls / its pull (or combine) kernel time.
         out["nvlink"] = {
             "pull_gbs_per_rank": [round(v[0] / (v[1] * 1e-3) / 1e9, 1) if v[1] > 0 else None for v in links],
-            "combine_gbs_per_rank": [round(v[2] / (v[3] * 1e-3) / 1e9, 1) if v[3] > 0 else None for v in links],
-            "pull_bytes_per_rank": [int(v[0]) for v in links], "combine_bytes_per_rank": [int(v[2]) for v in links],
-            "note": "bytes crossing NVLink (rows from or to other ranks only) / the kernel's device time "
-                    "(the combine's time includes its HBM traffic); peer copy measured on this pool: 770 GB/s per "
-                    "direction"}
+            "pull_bytes_per_rank": [int(v[0]) for v in links],
+            "push_bytes_per_rank": [int(v[2]) for v in links],
+            "push_gbs_over_expert_gemms_per_rank": [round(v[2] / (v[3] * 1e-3) / 1e9, 1) if v[3] > 0 else None
+                                                    for v in links],
+            "note": "bytes crossing NVLink (rows from or to other ranks only). pull: the pull kernel's peer loads / "
+                    "its device time. push: expert outputs the down GEMM's epilogue stores into the ranks the rows "
+                    "came from, tile by tile while the tensor cores work; their rate is given over the whole "
+                    "expert-GEMM phase. Peer copy measured on this pool: 770 GB/s per direction"}
     if world == 1 and rank == 0:
         out["ids_check"] = route_check(cfg, [x.cpu().numpy()], [ids.cpu().numpy()], norm=False,
                                        bias=t["router_bias"].cpu().numpy())

@@ -400,6 +400,7 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     p->pscratch.seg_count = reinterpret_cast<int*>(p->exchange + p->elay.seg_count);
     p->pscratch.seg_start = reinterpret_cast<int*>(p->exchange + p->elay.seg_start);
     p->pscratch.xperm = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.xperm);
+    p->pscratch.yperm = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.yback);
     p->epeers.base[p->emap.rank] = p->exchange;
   }
   *out = p;

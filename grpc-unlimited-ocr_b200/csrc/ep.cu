@@ -1,8 +1,8 @@
-// Expert-parallel prefill: the exchange between the route and expert phases,
-// the combine over the owners' outputs, and the barrier between the ranks'
-// exchange regions. Everything crosses NVLink as plain peer loads (and the
-// barrier's peer stores); no TMA reads peer memory — the grouped GEMMs read
-// only this GPU's xrecv / act.
+// Expert-parallel prefill: the exchange between the route and expert phases
+// and the barrier between the ranks' exchange regions. Rows cross NVLink as
+// plain peer loads (the pull) and as plain peer stores (the down GEMM's
+// epilogue sending each output row home, and the barrier's flags); no TMA
+// touches peer memory — the grouped GEMMs read only this GPU's xrecv / act.
 #include "ep.h"
 
 #include "combine.cuh"
@@ -31,14 +31,13 @@ __device__ __forceinline__ uint4 ld_cg16(const void* p) { return __ldcg(reinterp
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-// Every rank's per-expert counts and starts (peer loads), the receive layout
-// of every rank's expert slots, and where this rank's selections land in the
-// owners' yrecv. One block.
+// Every rank's per-expert counts and starts (peer loads) and the receive
+// layout of this rank's expert slots. One block.
 __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es,
                                                          ErrorWord* err) {
   __shared__ int cnt[kMaxEpRanks][kMaxExperts];
   __shared__ int tot[kMaxEpRanks * kMaxExperts];     // [d * max_local + i] rows slot i of rank d receives
-  __shared__ int rstart[kMaxEpRanks * kMaxExperts];  // its first row in rank d's yrecv
+  __shared__ int rstart[kMaxEpRanks * kMaxExperts];  // its first row in rank d's xrecv
   __shared__ int overflow;
   const int W = m.world, E = m.experts, ML = m.max_local;
   if (threadIdx.x == 0) overflow = 0;
@@ -77,11 +76,16 @@ __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers,
     es.recv_count[i] = overflow ? 0 : tot[m.rank * ML + i];
     es.recv_start[i] = overflow ? 0 : rstart[m.rank * ML + i];
   }
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int d = m.owner[e * W + m.rank], i = m.slot[e * W + m.rank];
-    int b = rstart[d * ML + i];
-    for (int s = 0; s < m.rank; ++s) b += m.owner[e * W + s] == d ? cnt[s][e] : 0;
-    es.remote_base[e] = b - es.seg_start_all[m.rank * E + e];
+  __syncthreads();
+  // (slot i, source s) segments of this rank's receive layout: slot-major,
+  // then source rank (the sources the owner table sends to this rank; the
+  // others' segments are empty).
+  for (int q = threadIdx.x; q < m.local * W; q += blockDim.x) {
+    const int i = q / W, s = q % W, e = m.slot_expert[m.rank * ML + i];
+    int d = overflow ? 0 : rstart[m.rank * ML + i];
+    for (int s2 = 0; s2 < s; ++s2) d += m.owner[e * W + s2] == m.rank ? cnt[s2][e] : 0;
+    es.seg_dst[q] = d;
+    es.seg_src[q] = es.seg_start_all[s * E + e];
   }
 }
 
@@ -94,14 +98,11 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
   __shared__ int seg_src[kMaxEpRanks * kMaxExperts];
   __shared__ int seg_rank[kMaxEpRanks * kMaxExperts];
   __shared__ int total;
-  const int W = m.world, L = m.local, E = m.experts, n = W * L;
+  const int W = m.world, L = m.local, n = W * L;
   for (int q = threadIdx.x; q < n; q += blockDim.x) {
-    const int i = q / W, s = q % W, e = m.slot_expert[m.rank * m.max_local + i];
-    int d = es.recv_start[i];
-    for (int s2 = 0; s2 < s; ++s2) d += m.owner[e * W + s2] == m.rank ? es.cnt_all[s2 * E + e] : 0;
-    seg_dst[q] = d;
-    seg_src[q] = es.seg_start_all[s * E + e];
-    seg_rank[q] = s;
+    seg_dst[q] = es.seg_dst[q];
+    seg_src[q] = es.seg_src[q];
+    seg_rank[q] = q % W;
   }
   if (threadIdx.x == 0) total = es.recv_start[L - 1] + es.recv_count[L - 1];
   __syncthreads();
@@ -132,36 +133,6 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
       }
     }
   }
-}
-
-// y[t, c] = shared[t, c] + sum over t's experts in ascending id of w * (the
-// owner's yrecv row), + resid: the single-GPU combine (combine.cuh) with the
-// rows read from the owners. One block per row.
-__global__ void __launch_bounds__(256, 3) ep_combine_kernel(int T, int H, int K, EpMap m, EpPeers peers, EpLayout lay,
-                                                         const int* __restrict__ ids,
-                                                         const float* __restrict__ weights,
-                                                         const int* __restrict__ pos_of,
-                                                         const int* __restrict__ remote_base,
-                                                         const float* shared_out, const float* resid, float* y) {
-  __shared__ CombineList list;
-  const int t = blockIdx.x;
-  if (t >= T) return;
-  const int64_t b = static_cast<int64_t>(t) * K;
-  order_selections(
-      K, [&](int i) { return ids[b + i]; },
-      [&](int j, int e, float* w, const __nv_bfloat16** src) {
-        const int p = pos_of[b + j];
-        *w = weights[b + j];
-        *src = (p < 0 || e < 0 || e >= m.experts)
-                   ? nullptr
-                   : reinterpret_cast<const __nv_bfloat16*>(peers.base[m.owner[e * m.world + m.rank]] + lay.yrecv) +
-                         (static_cast<int64_t>(remote_base[e]) + p) * H;
-      },
-      &list);
-  const int64_t o = static_cast<int64_t>(t) * H;
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
-    combine_cols8(list, K, c, shared_out != nullptr ? shared_out + o : nullptr, resid != nullptr ? resid + o : nullptr,
-                  y + o);
 }
 
 __global__ void ep_arrive_kernel(EpPeers peers, EpLayout lay, int rank, int world, unsigned* epoch) {
@@ -276,7 +247,7 @@ EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
   l.xperm = take(T * K * H * 2);
   l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) *
                (K < static_cast<size_t>(m.max_local) ? static_cast<int64_t>(K) : static_cast<int64_t>(m.max_local));
-  l.yrecv = take(static_cast<size_t>(l.max_recv) * H * 2);
+  l.yback = take(T * K * H * 2);
   l.bytes = align256(off);
   return l;
 }
@@ -300,7 +271,8 @@ void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m,
   s->seg_start_all = reinterpret_cast<int*>(take(W * E * 4));
   s->recv_count = reinterpret_cast<int*>(take(L * 4));
   s->recv_start = reinterpret_cast<int*>(take(L * 4));
-  s->remote_base = reinterpret_cast<int*>(take(E * 4));
+  s->seg_dst = reinterpret_cast<int*>(take(L * W * 4));
+  s->seg_src = reinterpret_cast<int*>(take(L * W * 4));
   s->epoch = reinterpret_cast<unsigned*>(take(sizeof(unsigned)));
   s->xrecv = reinterpret_cast<__nv_bfloat16*>(take(R * H * 2));
   s->act = reinterpret_cast<__nv_bfloat16*>(take(R * F * 2));
@@ -338,7 +310,11 @@ cudaError_t ep_experts(const EpCall& c, cudaStream_t stream, cudaEvent_t after_p
   g2.b0_routed = c.down_local;
   g2.b1_routed = c.down_local;
   g2.b_routed_rows = static_cast<int64_t>(L) * d.hidden;
-  g2.out_routed = c.peers.base[c.map.rank] + c.lay.yrecv;
+  g2.out_routed = nullptr;  // every row goes home through the scatter
+  g2.scatter.world = c.map.world;
+  g2.scatter.seg_dst = c.es.seg_dst;
+  g2.scatter.seg_src = c.es.seg_src;
+  for (int s = 0; s < c.map.world; ++s) g2.scatter.base[s] = c.peers.base[s] + c.lay.yback;
   return launch_grouped_gemm(g2, stream);
 }
 
@@ -349,14 +325,7 @@ cudaError_t ep_shared(const EpCall& c, cudaStream_t stream) {
   return launch_grouped_gemm(prefill_down_gemm(c.pc, false, true), stream);
 }
 
-cudaError_t ep_combine(const EpCall& c, cudaStream_t stream) {
-  const PrefillCall& p = c.pc;
-  if (p.rows <= 0) return cudaSuccess;
-  ep_combine_kernel<<<p.rows, 256, 0, stream>>>(p.rows, p.dims.hidden, p.dims.top_k, c.map, c.peers, c.lay, p.ids,
-                                                p.weights, p.scratch.pos_of, c.es.remote_base,
-                                                p.dims.shared_ffn > 0 ? p.scratch.shared_out : nullptr, p.resid, p.y);
-  return cudaGetLastError();
-}
+cudaError_t ep_combine(const EpCall& c, cudaStream_t stream) { return launch_prefill_combine(c.pc, stream); }
 
 cudaError_t ep_arrive(const EpCall& c, cudaStream_t stream) {
   ep_arrive_kernel<<<1, 32, 0, stream>>>(c.peers, c.lay, c.map.rank, c.map.world, c.es.epoch);

@@ -8,7 +8,7 @@
 //   flags     [kMaxEpRanks] u32   barrier epochs, flags[s] written by rank s
 //   seg_count [E] i32, seg_start [E] i32   this rank's rows per global expert
 //   xperm     [max_rows*k, H] bf16        this rank's rows grouped by expert
-//   yrecv     [max_recv, H] bf16          outputs of this rank's experts
+//   yback     [max_rows*k, H] bf16        their expert outputs, same positions
 // Per layer, on rank r:
 //   route    router + top-k + permutation of its own rows into xperm (the
 //            single-GPU prefill stages)
@@ -16,10 +16,13 @@
 //   experts  for each of its experts, the segments of every rank's xperm are
 //            pulled over NVLink (peer loads) into xrecv, source rank order, so
 //            an expert's rows are in global row order as on one GPU; the
-//            grouped GEMMs write yrecv
-//   arrive   then the shared expert on its own rows while the others finish
-//   wait     then the combine pulls each selection's output row from the
-//            expert owner's yrecv and adds them in ascending expert id.
+//            down GEMM's epilogue stores each output row into the yback of
+//            the rank it came from (peer stores, tile by tile), at the
+//            position the row has in that rank's xperm
+//   (the shared expert on its own rows runs alongside, on a second stream)
+//   arrive, wait
+//   combine  the single-GPU combine over its own yback: every selection's
+//            output row is local by then.
 // Each output row of the grouped GEMM depends on its own input row only, so
 // the result is bitwise the single-GPU result for the same rows.
 #pragma once
@@ -72,7 +75,7 @@ struct EpPeers {
 };
 
 struct EpLayout {
-  size_t flags, seg_count, seg_start, xperm, yrecv, bytes;
+  size_t flags, seg_count, seg_start, xperm, yback, bytes;
   int64_t max_recv;  // rows one rank's experts can receive: world * max_rows * min(k, local)
 };
 EpLayout ep_layout(const PrefillDims& d, const EpMap& m);
@@ -82,8 +85,9 @@ struct EpScratch {
   int* cnt_all;      // [world, E] every rank's rows per global expert, read after the first barrier
   int* seg_start_all;  // [world, E] and where they start in that rank's xperm
   int* recv_count;   // [local] rows each local expert receives
-  int* recv_start;   // [local] its first row in xrecv / yrecv
-  int* remote_base;  // [E] row of this rank's first selection of e in the owner's yrecv, minus seg_start[e]
+  int* recv_start;   // [local] its first row in xrecv
+  int* seg_dst;      // [local * world] first xrecv row of (slot i, source s)
+  int* seg_src;      // [local * world] that segment's first row in source s's xperm (and yback)
   unsigned* epoch;   // barrier epoch counter
   __nv_bfloat16* xrecv;  // [max_recv, H]
   __nv_bfloat16* act;    // [max_recv, F]

@@ -322,9 +322,7 @@ GroupedGemm prefill_down_gemm(const PrefillCall& c, bool routed, bool shared) {
 }
 
 cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
-  const PrefillDims& d = c.dims;
-  const PrefillScratch& s = c.scratch;
-  const int T = c.rows, H = d.hidden, K = d.top_k, S = d.shared_ffn;
+  const int T = c.rows;
   if (T <= 0) return cudaSuccess;
   // Optional per-kernel timing: an event after each stage of the path.
   auto mark = [&](int i) { return c.events != nullptr ? cudaEventRecord(c.events[i], stream) : cudaSuccess; };
@@ -336,10 +334,18 @@ cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream) {
   if ((st = launch_grouped_gemm(prefill_down_gemm(c, true, true), stream)) != cudaSuccess ||
       (st = mark(4)) != cudaSuccess)
     return st;
-  combine_kernel<<<T, 256, 0, stream>>>(T, H, K, c.ids, c.weights, s.pos_of, s.yperm, S > 0 ? s.shared_out : nullptr,
-                                        c.resid, c.y);
-  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  if ((st = launch_prefill_combine(c, stream)) != cudaSuccess) return st;
   return mark(5);
+}
+
+cudaError_t launch_prefill_combine(const PrefillCall& c, cudaStream_t stream) {
+  const PrefillDims& d = c.dims;
+  const PrefillScratch& s = c.scratch;
+  const int T = c.rows;
+  if (T <= 0) return cudaSuccess;
+  combine_kernel<<<T, 256, 0, stream>>>(T, d.hidden, d.top_k, c.ids, c.weights, s.pos_of, s.yperm,
+                                        d.shared_ffn > 0 ? s.shared_out : nullptr, c.resid, c.y);
+  return cudaGetLastError();
 }
 
 }  // namespace uocr_b200

@@ -67,6 +67,9 @@ struct PrefillCall {
   cudaEvent_t* events;
 };
 
+// The weighted combine alone (c.scratch.yperm holds the routed outputs at the
+// positions pos_of gives).
+cudaError_t launch_prefill_combine(const PrefillCall& c, cudaStream_t stream);
 cudaError_t launch_router_logits_rows(const float* x, int T, int H, const float* router, const float* bias, int E,
                                       float* logits, cudaStream_t stream);
 cudaError_t launch_prefill(const PrefillCall& c, cudaStream_t stream);

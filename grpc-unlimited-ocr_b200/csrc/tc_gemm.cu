@@ -54,6 +54,7 @@ struct KernelArgs {
   int shared_out_f32;
   int shared_accumulate;  // with shared_out_f32: out += A.B^T
   ErrorWord* err;
+  RowScatter scatter;
 };
 
 struct __align__(8) Barriers {
@@ -220,34 +221,47 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
     }
   } else {
     // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
-    // A thread holds one row's 32 columns after each tcgen05.ld; they pass
-    // through a 4 KB swizzled staging area of the warp so that the stores
-    // leave as whole 64-byte (bf16) or 128-byte (fp32) row segments, several
-    // rows per instruction, instead of 32 rows x 16 bytes.
+    // A thread holds one row's 32 columns after each tcgen05.ld; 64 bf16 or
+    // 32 fp32 columns pass through a 4 KB swizzled staging area of the warp so
+    // that the stores leave as whole 128-byte row lines, four rows per
+    // instruction, instead of 32 rows x 16 bytes.
     const int quarter = warp & 3;
     unsigned char* stg = smem + kStages * kStageBytes + (warp - 2) * kStageTileBytes;
-    // This lane's 32 values as bf16 into its row of the staging area, then
-    // out: lane j of pass i takes 16 bytes of row (32 i + j) / 4.
-    auto put_bf16 = [&](const float (&v)[32], __nv_bfloat16* out, int64_t ld, int64_t row0, int nvalid) {
+    // 64 columns of this lane's row as bf16 (two tcgen05.ld chunks, v0 then
+    // v1) into its 128-byte row of the staging area, then out as whole
+    // 128-byte lines: lane j of pass i takes 16 bytes of row (32 i + j) / 8,
+    // stored at rowp[i] (that row's first column; null: the row does not
+    // exist) + col.
+    auto put_bf16x64 = [&](const float (&v0)[32], const float (&v1)[32], __nv_bfloat16* const (&rowp)[8], int col) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 8; ++k) {
         uint4 pk;
         uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(v[k * 8 + 2 * i], v[k * 8 + 2 * i + 1]);
+          const float a = k < 4 ? v0[(k & 3) * 8 + 2 * i] : v1[(k & 3) * 8 + 2 * i];
+          const float b = k < 4 ? v0[(k & 3) * 8 + 2 * i + 1] : v1[(k & 3) * 8 + 2 * i + 1];
+          const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
           w[i] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        *reinterpret_cast<uint4*>(stg + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) = pk;
+        *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) = pk;
       }
       __syncwarp();
 #pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int idx = it * 32 + lane, rr = idx >> 2, k = idx & 3;
-        const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
-        if (rr < nvalid) *reinterpret_cast<uint4*>(out + (row0 + rr) * ld + k * 8) = val;
+      for (int it = 0; it < 8; ++it) {
+        const int idx = it * 32 + lane, rr = idx >> 3, k = idx & 7;
+        const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((k ^ (rr & 7)) << 4));
+        if (rowp[it] != nullptr) *reinterpret_cast<uint4*>(rowp[it] + col + k * 8) = val;
       }
       __syncwarp();
+    };
+    // The rows of the passes for a plain output: row0 + (32 i + lane) / 8.
+    auto plain_rows = [&](__nv_bfloat16* out, int64_t ld, int64_t row0, int nvalid, __nv_bfloat16* (&rowp)[8]) {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = (it * 32 + lane) >> 3;
+        rowp[it] = rr < nvalid ? out + (row0 + rr) * ld : nullptr;
+      }
     };
     // The same for fp32 (128 bytes a row); acc: out += v.
     auto put_f32 = [&](const float (&v)[32], float* out, int64_t ld, int64_t row0, int nvalid, bool acc) {
@@ -292,28 +306,75 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_gemm_kernel(const __gr
       if (args.mode == 0) {
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared);
         const int64_t ld = routed ? args.ld_out_routed : args.ld_out_shared;
+        __nv_bfloat16* rowp[8];
+        plain_rows(out + tl.n * (kBN / 2), ld, row0, nvalid, rowp);
 #pragma unroll 1
-        for (int c = 0; c < kBN / 2; c += 32) {
-          float g[32], u[32];
-          tmem_ld32(taddr + c, g);
+        for (int c = 0; c < kBN / 2; c += 64) {
+          float g0[32], g1[32], u[32];
+          tmem_ld32(taddr + c, g0);
           tmem_ld32(taddr + kBN / 2 + c, u);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) g[i] = swiglu(g[i], u[i]);
-          put_bf16(g, out + tl.n * (kBN / 2) + c, ld, row0, nvalid);
+          for (int i = 0; i < 32; ++i) g0[i] = swiglu(g0[i], u[i]);
+          tmem_ld32(taddr + c + 32, g1);
+          tmem_ld32(taddr + kBN / 2 + c + 32, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g1[i] = swiglu(g1[i], u[i]);
+          put_bf16x64(g0, g1, rowp, c);
+        }
+      } else if (routed && args.scatter.world > 0) {
+        // This lane's four rows of the passes: their segment and destination.
+        const int W = args.scatter.world;
+        const int my_dst = lane < W ? __ldcg(args.scatter.seg_dst + tl.g * W + lane) : 0;
+        const int my_src = lane < W ? __ldcg(args.scatter.seg_src + tl.g * W + lane) : 0;
+        __nv_bfloat16* rowp[8];
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int rr = (it * 32 + lane) >> 3;
+          const int64_t R = row0 + rr;
+          int s_sel = 0, d_sel = 0, src_sel = 0;
+          for (int s2 = 0; s2 < W; ++s2) {
+            const int d = __shfl_sync(0xffffffffu, my_dst, s2);
+            const int sr = __shfl_sync(0xffffffffu, my_src, s2);
+            if (d <= R) {
+              s_sel = s2;
+              d_sel = d;
+              src_sel = sr;
+            }
+          }
+          rowp[it] = rr < nvalid ? static_cast<__nv_bfloat16*>(args.scatter.base[s_sel]) +
+                                       (static_cast<int64_t>(src_sel) + (R - d_sel)) * args.ld_out_routed +
+                                       tl.n * kBN
+                                 : nullptr;
+        }
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 64) {
+          float v0[32], v1[32];
+          tmem_ld32(taddr + c, v0);
+          tmem_ld32(taddr + c + 32, v1);
+          put_bf16x64(v0, v1, rowp, c);
         }
       } else {
         const bool f32 = !routed && args.shared_out_f32;
         const int64_t ld = routed ? args.ld_out_routed : args.ld_out_shared;
+        if (f32) {
 #pragma unroll 1
-        for (int c = 0; c < kBN; c += 32) {
-          float v[32];
-          tmem_ld32(taddr + c, v);
-          if (f32)
+          for (int c = 0; c < kBN; c += 32) {
+            float v[32];
+            tmem_ld32(taddr + c, v);
             put_f32(v, static_cast<float*>(args.out_shared) + tl.n * kBN + c, ld, row0, nvalid,
                     args.shared_accumulate != 0);
-          else
-            put_bf16(v, static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared) + tl.n * kBN + c, ld,
-                     row0, nvalid);
+          }
+        } else {
+          __nv_bfloat16* rowp[8];
+          plain_rows(static_cast<__nv_bfloat16*>(routed ? args.out_routed : args.out_shared) + tl.n * kBN, ld, row0,
+                     nvalid, rowp);
+#pragma unroll 1
+          for (int c = 0; c < kBN; c += 64) {
+            float v0[32], v1[32];
+            tmem_ld32(taddr + c, v0);
+            tmem_ld32(taddr + c + 32, v1);
+            put_bf16x64(v0, v1, rowp, c);
+          }
         }
       }
       tc_fence_before();
@@ -412,6 +473,9 @@ cudaError_t launch_grouped_gemm(const GroupedGemm& g, cudaStream_t stream) {
   a.shared_out_f32 = g.shared_out_f32 ? 1 : 0;
   a.shared_accumulate = g.shared_accumulate ? 1 : 0;
   a.err = g.err;
+  if (g.scatter.world < 0 || g.scatter.world > kMaxScatterRanks || (g.scatter.world > 0 && g.mode != 1))
+    return cudaErrorInvalidValue;
+  a.scatter = g.scatter;
   tc_grouped_gemm_kernel<<<g.blocks, kThreads, grouped_gemm_smem_bytes(), stream>>>(a);
   return cudaGetLastError();
 }

@@ -23,6 +23,22 @@ namespace uocr_b200 {
 // mode 1 (down): b0 = b1 = the down stack; output columns A.B[j], n_cols a
 //   multiple of 256.
 // k_* are multiples of 64; every matrix is row-major with 16-byte aligned rows.
+//
+// Routed output rows sent to other GPUs' memory (expert parallelism, mode 1):
+// with world > 0, routed output row R (a group's rows arrive source after
+// source) belongs to segment (group g, source s), the last s with
+// seg_dst[g * world + s] <= R (an empty segment starts where the next one
+// does), and is stored as row seg_src[g * world + s] + R - seg_dst[g * world + s]
+// of base[s] (ld_out_routed elements per row) instead of out_routed: each
+// tile's rows go straight from the epilogue to the GPU they came from.
+constexpr int kMaxScatterRanks = 8;
+struct RowScatter {
+  int world;
+  const int* seg_dst;
+  const int* seg_src;
+  void* base[kMaxScatterRanks];
+};
+
 struct GroupedGemm {
   int mode;
   int experts;
@@ -51,6 +67,7 @@ struct GroupedGemm {
   bool shared_accumulate;  // with shared_out_f32: out_shared += A.B^T (a residual add)
   ErrorWord* err;
   int blocks;  // persistent grid size (the SM count)
+  RowScatter scatter;  // world 0: routed rows to out_routed
 };
 
 size_t grouped_gemm_smem_bytes();

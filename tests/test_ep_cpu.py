@@ -1,8 +1,9 @@
 """Expert-parallel host logic on the CPU: row and expert ownership, the
 exchange arithmetic (restated here in numpy: each rank's per-expert segments,
-the receive layout of every rank's experts, and where each selection's output
-lands) checked against the single-GPU permutation, and the same arithmetic
-run by two gloo ranks that exchange their counts as the GPUs do."""
+the receive layout of every rank's experts, and where the down GEMM stores
+each received row's output — home, at the row's position in its source's
+permuted layout) checked against the single-GPU permutation, and the same
+arithmetic run by two gloo ranks that exchange their counts as the GPUs do."""
 import os
 import socket
 
@@ -59,23 +60,33 @@ def receive_layout(cnt_all, W, E, strided):
     return tot, rstart
 
 
-def remote_base(rank, cnt_all, seg_start_own, rstart, W, E, strided):
-    out = np.zeros(E, np.int64)
-    for e in range(E):
-        d = ep.expert_owner(e, E, W, strided)
-        i = ep.local_experts(d, E, W, strided).index(e)
-        out[e] = rstart[d, i] + cnt_all[:rank, e].sum() - seg_start_own[e]
-    return out
+def segments(d, cnt_all, seg_start_all, rstart, W, E, strided):
+    """Rank d's (slot, source) segments as the prepare kernel lays them out:
+    (first receive row, first row in the source's xperm, source), slot-major."""
+    segs = []
+    for i, e in enumerate(ep.local_experts(d, E, W, strided)):
+        for s in range(W):
+            segs.append((int(rstart[d, i] + cnt_all[:s, e].sum()), int(seg_start_all[s, e]), s))
+    return segs
+
+
+def home_of(segs, r):
+    """The scatter of the down GEMM's epilogue: receive row r goes to row
+    seg_src + r - seg_dst of the last segment starting at or before r."""
+    dst, src, s = [g for g in segs if g[0] <= r][-1]
+    return s, src + r - dst
 
 
 def simulate(ids_per_rank, W, E, strided):
     """Per-rank permutations, the pulls into every owner's receive rows, and
-    each selection's remote row. Returns, per owner, the (source rank, row)
-    of each received row, and per source the remote row of each selection."""
+    where each received row's output goes home. Returns, per owner, the
+    (source rank, row) of each received row and the (source rank, position)
+    its output is stored at."""
     perms = [permute(ids, E) for ids in ids_per_rank]
     cnt_all = np.stack([p[0] for p in perms])
+    seg_start_all = np.stack([p[1] for p in perms])
     tot, rstart = receive_layout(cnt_all, W, E, strided)
-    recv = []
+    recv, home = [], []
     for d in range(W):
         rows = []
         for i, e in enumerate(ep.local_experts(d, E, W, strided)):
@@ -86,11 +97,28 @@ def simulate(ids_per_rank, W, E, strided):
                 rows += [(s, int(t) // ids_per_rank[s].shape[1]) for t in toks]
         assert len(rows) == tot[d].sum()
         recv.append(rows)
-    remote = []
+        segs = segments(d, cnt_all, seg_start_all, rstart, W, E, strided)
+        home.append([home_of(segs, r) for r in range(len(rows))])
+    return recv, home, perms
+
+
+def check_homes(ids_per_rank, recv, home, perms, W, E, strided):
+    """Every selection's output lands exactly once, at its own position of its
+    source's permuted layout (where the single-GPU combine reads it), and the
+    row stored there is the one that was pulled."""
+    landed = [dict() for _ in range(W)]
+    for d in range(W):
+        for r, ((s, t), (hs, p)) in enumerate(zip(recv[d], home[d])):
+            assert hs == s
+            assert p not in landed[s]
+            landed[s][p] = t
     for s in range(W):
-        rb = remote_base(s, cnt_all, perms[s][1], rstart, W, E, strided)
-        remote.append(rb[ids_per_rank[s]] + perms[s][2])
-    return recv, remote
+        n = len(ids_per_rank[s])
+        assert len(landed[s]) == n * ids_per_rank[s].shape[1]
+        pos = perms[s][2]
+        for t in range(n):
+            for j in range(ids_per_rank[s].shape[1]):
+                assert landed[s][int(pos[t, j])] == t
 
 
 @pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False), (8, True)])
@@ -102,7 +130,7 @@ def test_exchange_arithmetic_reproduces_single_gpu_order(W, strided):
     p = 1.0 / np.arange(1, E + 1) ** 1.2
     ids_per_rank = [np.stack([rng.choice(E, K, replace=False, p=p / p.sum()) for _ in range(n)]).astype(np.int64)
                     if n else np.zeros((0, K), np.int64) for n in rows]
-    recv, remote = simulate(ids_per_rank, W, E, strided)
+    recv, home, perms = simulate(ids_per_rank, W, E, strided)
     offsets = np.concatenate([[0], np.cumsum(rows)])
     glob_ids = np.concatenate(ids_per_rank)
     for d in range(W):
@@ -113,12 +141,7 @@ def test_exchange_arithmetic_reproduces_single_gpu_order(W, strided):
         for e in ep.local_experts(d, E, W, strided):
             want += [t for t in range(len(glob_ids)) if e in glob_ids[t]]
         assert got == want
-    for s in range(W):
-        for t in range(rows[s]):
-            for j in range(K):
-                e = ids_per_rank[s][t, j]
-                d = ep.expert_owner(e, E, W, strided)
-                assert recv[d][remote[s][t, j]] == (s, t)
+    check_homes(ids_per_rank, recv, home, perms, W, E, strided)
 
 
 # ---- two gloo ranks ----------------------------------------------------------
@@ -143,19 +166,27 @@ def _gloo_rank(rank, world, port, E, K, strided, result_q):
         # the counts exchange the prepare kernel does with peer loads
         allc = [torch.zeros(E, dtype=torch.int64) for _ in range(world)]
         dist.all_gather(allc, torch.from_numpy(seg_count))
+        alls = [torch.zeros(E, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(alls, torch.from_numpy(seg_start))
         cnt_all = torch.stack(allc).numpy()
+        seg_start_all = torch.stack(alls).numpy()
         _, rstart = receive_layout(cnt_all, world, E, strided)
-        rb = remote_base(rank, cnt_all, seg_start, rstart, world, E, strided)
+        # this rank's own (slot, source) segments, from the exchanged counts only
+        mine = segments(rank, cnt_all, seg_start_all, rstart, world, E, strided)
         # handles travel as opaque bytes, in rank order
         handles = ep.exchange_handles(bytes([rank]) * 256)
         assert [h[0] for h in handles] == list(range(world))
         obj = [None] * world
-        dist.all_gather_object(obj, (ids, rb[ids] + pos if n else np.zeros((0, K), np.int64)))
+        dist.all_gather_object(obj, (ids, mine))
         if rank == 0:
             ids_all = [o[0] for o in obj]
-            _, remote = simulate(ids_all, world, E, strided)
-            ok = all(np.array_equal(remote[s], obj[s][1]) for s in range(world))
-            result_q.put(ok)
+            recv, home, perms = simulate(ids_all, world, E, strided)
+            ok = True
+            for d in range(world):
+                segs_d = obj[d][1]
+                ok &= [home_of(segs_d, r) for r in range(len(recv[d]))] == home[d]
+            check_homes(ids_all, recv, home, perms, world, E, strided)
+            result_q.put(bool(ok))
     finally:
         dist.destroy_process_group()
 
