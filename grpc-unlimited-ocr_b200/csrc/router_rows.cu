@@ -65,7 +65,7 @@ constexpr int kRouterTile = kRouterTokens * 4 * kRouterPad;  // floats per opera
 static_assert(kRouterTokens == 32 && kRouterExperts == 32, "8 row groups x 8 expert groups x 4 lane pairs");
 size_t router_rows_smem_bytes() { return static_cast<size_t>(4) * kRouterTile * sizeof(float); }
 
-__global__ void __launch_bounds__(256, 2) router_logits_rows_kernel(const float* __restrict__ x, int T, int H,
+__global__ void __launch_bounds__(256, 3) router_logits_rows_kernel(const float* __restrict__ x, int T, int H,
                                                                     const float* __restrict__ router,
                                                                     const float* __restrict__ bias, int E,
                                                                     float* __restrict__ logits, float neg_zero) {
