@@ -216,6 +216,7 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     GPU) quantises the layer per output channel; the prefill path then expands
     it to bf16 per layer before the GEMMs (the expansion is timed inside the
     router's interval of kernel_ms)."""
+    import numpy as np
     import torch
     cfg = C.CONFIGS[3]
     total = rows or cfg.rows[0]
@@ -283,11 +284,18 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         ep_equal = bool(eq.item())
         del y1
         # Bytes this rank moves over NVLink: the rows it pulls from other
-        # ranks for its experts, and the same rows' expert outputs, which its
-        # down GEMM's epilogue stores back into their ranks (bf16 rows of H).
-        pulled = sum(cbs[s][e] for e in range(E) for s in range(world)
+        # ranks — each source row once however many of this rank's experts
+        # take it — and the expert outputs of every selection it received,
+        # which its down GEMM's epilogue stores back (bf16 rows of H).
+        own = np.asarray(owner, np.int64)[ids.cpu().numpy().astype(np.int64) * world + rank]  # [rows, k]
+        sent = torch.tensor([int((own == d).any(axis=1).sum()) if d != rank else 0 for d in range(world)],
+                            dtype=torch.int64, device=dev)
+        sent_all = [torch.empty_like(sent) for _ in range(world)]
+        dist.all_gather(sent_all, sent)
+        pulled = sum(int(v[rank]) for v in sent_all) * H * 2
+        pushed = sum(cbs[s][e] for e in range(E) for s in range(world)
                      if owner[e * world + s] == rank and s != rank) * H * 2
-        link = torch.tensor([pulled, prof["pull"], pulled, prof["expert_gemms"]], dtype=torch.float64, device=dev)
+        link = torch.tensor([pulled, prof["pull"], pushed, prof["expert_gemms"]], dtype=torch.float64, device=dev)
         links = [torch.empty_like(link) for _ in range(world)]
         dist.all_gather(links, link)
         links = [v.cpu().tolist() for v in links]
@@ -344,8 +352,8 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
             "push_bytes_per_rank": [int(v[2]) for v in links],
             "push_gbs_over_expert_gemms_per_rank": [round(v[2] / (v[3] * 1e-3) / 1e9, 1) if v[3] > 0 else None
                                                     for v in links],
-            "note": "bytes crossing NVLink (rows from or to other ranks only). pull: the pull kernel's peer loads / "
-                    "its device time. push: expert outputs the down GEMM's epilogue stores into the ranks the rows "
+            "note": "bytes crossing NVLink (rows from or to other ranks only). pull: the pull kernel's peer loads "
+                    "(a source row once per owning rank) / its device time. push: expert outputs the down GEMM's epilogue stores into the ranks the rows "
                     "came from, tile by tile while the tensor cores work; their rate is given over the whole "
                     "expert-GEMM phase. Peer copy measured on this pool: 770 GB/s per direction"}
     if world == 1 and rank == 0:

@@ -89,6 +89,36 @@ __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers,
   }
 }
 
+// first_p of this rank's xperm positions: for each row, the selections that
+// one owner takes reach that owner's receive rows in ascending expert order
+// (its slots are in ascending id), so the lowest expert id's position is the
+// one the owner pulls over NVLink; the others point at it. Thread per row.
+__global__ void ep_first_kernel(EpMap m, int T, int K, const int* __restrict__ ids, const int* __restrict__ pos_of,
+                                int* __restrict__ first_p) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  int e[kMaxTopK], d[kMaxTopK], p[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j >= K) break;
+    e[j] = ids[static_cast<int64_t>(t) * K + j];
+    p[j] = pos_of[static_cast<int64_t>(t) * K + j];
+    d[j] = (e[j] >= 0 && e[j] < m.experts) ? m.owner[e[j] * m.world + m.rank] : -1;
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j >= K) break;
+    if (p[j] < 0 || d[j] < 0) continue;
+    int best = j;
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i) {
+      if (i >= K) break;
+      if (d[i] == d[j] && p[i] >= 0 && e[i] < e[best]) best = i;
+    }
+    first_p[p[j]] = p[best];
+  }
+}
+
 // xrecv rows of this rank's expert slots: slot-major, then source rank (the
 // sources this slot takes; the others' segments are empty), each (slot,
 // source) segment a contiguous run of the source's xperm. One warp per row,
@@ -98,7 +128,7 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
   __shared__ int seg_src[kMaxEpRanks * kMaxExperts];
   __shared__ int seg_rank[kMaxEpRanks * kMaxExperts];
   __shared__ int total;
-  const int W = m.world, L = m.local, n = W * L;
+  const int W = m.world, L = m.local, n = W * L, E = m.experts;
   for (int q = threadIdx.x; q < n; q += blockDim.x) {
     seg_dst[q] = es.seg_dst[q];
     seg_src[q] = es.seg_src[q];
@@ -116,8 +146,65 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
       if (seg_dst[mid] <= r) lo = mid;
       else hi = mid - 1;
     }
-    const int64_t src_row = seg_src[lo] + (r - seg_dst[lo]);
-    const uint4* src = reinterpret_cast<const uint4*>(peers.base[seg_rank[lo]] + lay.xperm) + src_row * nch;
+    const int s = seg_rank[lo];
+    const int src_row = seg_src[lo] + (r - seg_dst[lo]);
+    // A row this rank takes for several experts crosses once: the position
+    // of its lowest-id selection owned here is pulled, the others copied
+    // from xrecv afterwards (ep_dup_kernel).
+    // The copy source is a receive row before r (its expert id is lower); a
+    // position that does not resolve to one is pulled like any other.
+    int from = -1;
+    if (lane == 0) {
+      const int fp = ld_relaxed_sys(reinterpret_cast<const int*>(peers.base[s] + lay.first_p) + src_row);
+      if (fp >= 0 && fp < src_row) {
+        // fp's expert: the last expert of source s whose segment starts at
+        // or before it (empty segments start where the next one does).
+        const int* st = es.seg_start_all + s * E;
+        int a = 0, b = E - 1;
+        while (a < b) {
+          const int mid = (a + b + 1) >> 1;
+          if (st[mid] <= fp) a = mid;
+          else b = mid - 1;
+        }
+        if (m.owner[a * W + s] == m.rank) {
+          const int q = m.slot[a * W + s] * W + s;
+          const int r0 = es.seg_dst[q] + (fp - es.seg_src[q]);
+          if (r0 >= 0 && r0 < r) from = r0;
+        }
+      }
+      es.dup[r] = from;
+    }
+    from = __shfl_sync(0xffffffffu, from, 0);
+    if (from >= 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(peers.base[s] + lay.xperm) + static_cast<int64_t>(src_row) * nch;
+    uint4* dst = reinterpret_cast<uint4*>(es.xrecv) + static_cast<int64_t>(r) * nch;
+    for (int c0 = 0; c0 < nch; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = c0 + lane + 32 * u;
+        if (idx < nch) v[u] = ld_cg16(src + idx);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = c0 + lane + 32 * u;
+        if (idx < nch) dst[idx] = v[u];
+      }
+    }
+  }
+}
+
+// The rows ep_pull_kernel left to copy locally: each from the receive row
+// that pulled it. One warp per row, grid-stride.
+__global__ void __launch_bounds__(256) ep_dup_kernel(EpMap m, EpScratch es, int H) {
+  const int total = es.recv_start[m.local - 1] + es.recv_count[m.local - 1];
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int nch = H / 8;
+  for (int r = warp; r < total; r += nwarps) {
+    const int from = es.dup[r];
+    if (from < 0 || from >= r) continue;  // pulled (a copy always comes from an earlier row)
+    const uint4* src = reinterpret_cast<const uint4*>(es.xrecv) + static_cast<int64_t>(from) * nch;
     uint4* dst = reinterpret_cast<uint4*>(es.xrecv) + static_cast<int64_t>(r) * nch;
     for (int c0 = 0; c0 < nch; c0 += 32 * 8) {
       uint4 v[8];
@@ -245,6 +332,7 @@ EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
   l.seg_count = take(E * 4);
   l.seg_start = take(E * 4);
   l.xperm = take(T * K * H * 2);
+  l.first_p = take(T * K * 4);
   l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) *
                (K < static_cast<size_t>(m.max_local) ? static_cast<int64_t>(K) : static_cast<int64_t>(m.max_local));
   l.yback = take(T * K * H * 2);
@@ -273,13 +361,21 @@ void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m,
   s->recv_start = reinterpret_cast<int*>(take(L * 4));
   s->seg_dst = reinterpret_cast<int*>(take(L * W * 4));
   s->seg_src = reinterpret_cast<int*>(take(L * W * 4));
+  s->dup = reinterpret_cast<int*>(take(static_cast<size_t>(R) * 4));
   s->epoch = reinterpret_cast<unsigned*>(take(sizeof(unsigned)));
   s->xrecv = reinterpret_cast<__nv_bfloat16*>(take(R * H * 2));
   s->act = reinterpret_cast<__nv_bfloat16*>(take(R * F * 2));
   s->bytes = align256(off);
 }
 
-cudaError_t ep_route(const EpCall& c, cudaStream_t stream) { return launch_prefill_route(c.pc, stream); }
+cudaError_t ep_route(const EpCall& c, cudaStream_t stream) {
+  cudaError_t st = launch_prefill_route(c.pc, stream);
+  if (st != cudaSuccess || c.pc.rows <= 0) return st;
+  const int T = c.pc.rows;
+  ep_first_kernel<<<(T + 255) / 256, 256, 0, stream>>>(c.map, T, c.pc.dims.top_k, c.pc.ids, c.pc.scratch.pos_of,
+                                                     reinterpret_cast<int*>(c.peers.base[c.map.rank] + c.lay.first_p));
+  return cudaGetLastError();
+}
 
 cudaError_t ep_experts(const EpCall& c, cudaStream_t stream, cudaEvent_t after_pull) {
   const PrefillDims& d = c.pc.dims;
@@ -287,6 +383,8 @@ cudaError_t ep_experts(const EpCall& c, cudaStream_t stream, cudaEvent_t after_p
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return st;
   ep_pull_kernel<<<c.pc.sm_count * 4, 256, 0, stream>>>(c.map, c.peers, c.lay, c.es, d.hidden);
+  if ((st = cudaGetLastError()) != cudaSuccess) return st;
+  ep_dup_kernel<<<c.pc.sm_count * 4, 256, 0, stream>>>(c.map, c.es, d.hidden);
   if ((st = cudaGetLastError()) != cudaSuccess) return st;
   if (after_pull != nullptr && (st = cudaEventRecord(after_pull, stream)) != cudaSuccess) return st;
   const int L = c.map.local;

@@ -8,6 +8,9 @@
 //   flags     [kMaxEpRanks] u32   barrier epochs, flags[s] written by rank s
 //   seg_count [E] i32, seg_start [E] i32   this rank's rows per global expert
 //   xperm     [max_rows*k, H] bf16        this rank's rows grouped by expert
+//   first_p   [max_rows*k] i32            per xperm position: the position of the
+//                                          same row's selection with the lowest
+//                                          expert id among those the same rank owns
 //   yback     [max_rows*k, H] bf16        their expert outputs, same positions
 // Per layer, on rank r:
 //   route    router + top-k + permutation of its own rows into xperm (the
@@ -15,7 +18,9 @@
 //   barrier  (arrive, wait)
 //   experts  for each of its experts, the segments of every rank's xperm are
 //            pulled over NVLink (peer loads) into xrecv, source rank order, so
-//            an expert's rows are in global row order as on one GPU; the
+//            an expert's rows are in global row order as on one GPU — a row
+//            that several of its experts take crosses once (first_p), the
+//            other copies are made from xrecv itself; the
 //            down GEMM's epilogue stores each output row into the yback of
 //            the rank it came from (peer stores, tile by tile), at the
 //            position the row has in that rank's xperm
@@ -75,7 +80,7 @@ struct EpPeers {
 };
 
 struct EpLayout {
-  size_t flags, seg_count, seg_start, xperm, yback, bytes;
+  size_t flags, seg_count, seg_start, xperm, first_p, yback, bytes;
   int64_t max_recv;  // rows one rank's experts can receive: world * max_rows * min(k, local)
 };
 EpLayout ep_layout(const PrefillDims& d, const EpMap& m);
@@ -88,6 +93,7 @@ struct EpScratch {
   int* recv_start;   // [local] its first row in xrecv
   int* seg_dst;      // [local * world] first xrecv row of (slot i, source s)
   int* seg_src;      // [local * world] that segment's first row in source s's xperm (and yback)
+  int* dup;          // [max_recv] receive row to copy this one from (a row pulled once), -1: pulled
   unsigned* epoch;   // barrier epoch counter
   __nv_bfloat16* xrecv;  // [max_recv, H]
   __nv_bfloat16* act;    // [max_recv, F]

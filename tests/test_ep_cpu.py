@@ -121,6 +121,68 @@ def check_homes(ids_per_rank, recv, home, perms, W, E, strided):
                 assert landed[s][int(pos[t, j])] == t
 
 
+def first_positions(ids, pos, rank, W, E, strided):
+    """ep_first_kernel: per xperm position of `rank`, the position of the same
+    row's selection with the lowest expert id among those one owner takes."""
+    first = np.full(ids.size, -1, np.int64)
+    for t in range(ids.shape[0]):
+        owners = [ep.expert_owner(int(e), E, W, strided) for e in ids[t]]
+        for j, e in enumerate(ids[t]):
+            same = [i for i in range(ids.shape[1]) if owners[i] == owners[j]]
+            best = min(same, key=lambda i: ids[t, i])
+            first[pos[t, j]] = pos[t, best]
+    return first
+
+
+def pull_plan(d, recv_rows, segs, seg_start_all, firsts, W, E, strided):
+    """ep_pull_kernel's choice per receive row of rank d: -1 = pulled over
+    NVLink, else the earlier receive row it is copied from (ep_dup_kernel)."""
+    plan = []
+    for r in range(len(recv_rows)):
+        dst, src, s = [g for g in segs if g[0] <= r][-1]
+        p = src + r - dst
+        fp = int(firsts[s][p])
+        frm = -1
+        if 0 <= fp < p:
+            a = max(e for e in range(E) if seg_start_all[s, e] <= fp)
+            if ep.expert_owner(a, E, W, strided) == d:
+                i = ep.local_experts(d, E, W, strided).index(a)
+                q = i * W + s
+                r0 = segs[q][0] + fp - segs[q][1]
+                if 0 <= r0 < r:
+                    frm = r0
+        plan.append(frm)
+    return plan
+
+
+@pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False)])
+def test_each_row_crosses_once_per_owner(W, strided):
+    """The deduplicated pull: every (source row, owner) pair is pulled exactly
+    once, and every other receive row of the same source row copies a pulled
+    row holding the same source row — xrecv ends up as the full pull."""
+    rng = np.random.default_rng(7 + W)
+    E, K = 32, 6
+    rows = rng.integers(20, 60, size=W)
+    ids_per_rank = [np.stack([rng.choice(E, K, replace=False) for _ in range(n)]).astype(np.int64) for n in rows]
+    recv, _, perms = simulate(ids_per_rank, W, E, strided)
+    cnt_all = np.stack([p[0] for p in perms])
+    seg_start_all = np.stack([p[1] for p in perms])
+    _, rstart = receive_layout(cnt_all, W, E, strided)
+    firsts = [first_positions(ids_per_rank[s], perms[s][2], s, W, E, strided) for s in range(W)]
+    pulled_total = sel_total = 0
+    for d in range(W):
+        segs = segments(d, cnt_all, seg_start_all, rstart, W, E, strided)
+        plan = pull_plan(d, recv[d], segs, seg_start_all, firsts, W, E, strided)
+        pulled = [recv[d][r] for r in range(len(plan)) if plan[r] < 0]
+        assert len(pulled) == len(set(pulled)) == len(set(recv[d]))
+        for r, frm in enumerate(plan):
+            if frm >= 0:
+                assert plan[frm] < 0 and recv[d][frm] == recv[d][r]
+        pulled_total += sum(1 for (s, _), f in zip(recv[d], plan) if f < 0 and s != d)
+        sel_total += sum(1 for s, _ in recv[d] if s != d)
+    assert pulled_total < sel_total  # rows with several experts on one owner cross once
+
+
 @pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False), (8, True)])
 def test_exchange_arithmetic_reproduces_single_gpu_order(W, strided):
     rng = np.random.default_rng(W)
