@@ -399,7 +399,8 @@ int uocr_moe_plan_create(const uocr_moe_desc* desc, uocr_moe_plan** out) {
     p->arena_bytes += p->elay.bytes;
     p->pscratch.seg_count = reinterpret_cast<int*>(p->exchange + p->elay.seg_count);
     p->pscratch.seg_start = reinterpret_cast<int*>(p->exchange + p->elay.seg_start);
-    p->pscratch.xperm = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.xperm);
+    p->pscratch.xperm = nullptr;  // the owners pull rows straight from x^
+    p->pscratch.xhat = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.xhat);
     p->pscratch.yperm = reinterpret_cast<__nv_bfloat16*>(p->exchange + p->elay.yback);
     p->epeers.base[p->emap.rank] = p->exchange;
   }

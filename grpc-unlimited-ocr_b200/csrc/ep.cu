@@ -19,6 +19,11 @@ __device__ __forceinline__ int ld_relaxed_sys(const int* p) {
   asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int2 ld_relaxed_sys2(const int2* p) {
+  int2 v;
+  asm volatile("ld.relaxed.sys.global.v2.s32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -89,12 +94,13 @@ __global__ void __launch_bounds__(256) ep_prepare_kernel(EpMap m, EpPeers peers,
   }
 }
 
-// first_p of this rank's xperm positions: for each row, the selections that
-// one owner takes reach that owner's receive rows in ascending expert order
-// (its slots are in ascending id), so the lowest expert id's position is the
-// one the owner pulls over NVLink; the others point at it. Thread per row.
+// src_of of this rank's permuted positions: the row's index, and the position
+// of its first selection on the same owner — the selections one owner takes
+// reach its receive rows in ascending expert order (its slots are in
+// ascending id), so the lowest expert id's position is the one the owner
+// pulls over NVLink; the others point at it. Thread per row.
 __global__ void ep_first_kernel(EpMap m, int T, int K, const int* __restrict__ ids, const int* __restrict__ pos_of,
-                                int* __restrict__ first_p) {
+                                int2* __restrict__ src_of) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   int e[kMaxTopK], d[kMaxTopK], p[kMaxTopK];
@@ -115,14 +121,16 @@ __global__ void ep_first_kernel(EpMap m, int T, int K, const int* __restrict__ i
       if (i >= K) break;
       if (d[i] == d[j] && p[i] >= 0 && e[i] < e[best]) best = i;
     }
-    first_p[p[j]] = p[best];
+    src_of[p[j]] = make_int2(p[best], t);
   }
 }
 
 // xrecv rows of this rank's expert slots: slot-major, then source rank (the
 // sources this slot takes; the others' segments are empty), each (slot,
-// source) segment a contiguous run of the source's xperm. One warp per row,
-// grid-stride; 16-byte peer loads, all of a row in flight at once.
+// source) segment the source's selections of that expert in permuted order
+// (= row order), each row fetched from the source's x^ by the index src_of
+// gives. One warp per row, grid-stride; 16-byte peer loads, all of a row in
+// flight at once.
 __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, EpLayout lay, EpScratch es, int H) {
   __shared__ int seg_dst[kMaxEpRanks * kMaxExperts];
   __shared__ int seg_src[kMaxEpRanks * kMaxExperts];
@@ -153,9 +161,11 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
     // from xrecv afterwards (ep_dup_kernel).
     // The copy source is a receive row before r (its expert id is lower); a
     // position that does not resolve to one is pulled like any other.
-    int from = -1;
+    int from = -1, tok = 0;
     if (lane == 0) {
-      const int fp = ld_relaxed_sys(reinterpret_cast<const int*>(peers.base[s] + lay.first_p) + src_row);
+      const int2 so = ld_relaxed_sys2(reinterpret_cast<const int2*>(peers.base[s] + lay.src_of) + src_row);
+      const int fp = so.x;
+      tok = so.y;
       if (fp >= 0 && fp < src_row) {
         // fp's expert: the last expert of source s whose segment starts at
         // or before it (empty segments start where the next one does).
@@ -176,7 +186,9 @@ __global__ void __launch_bounds__(256) ep_pull_kernel(EpMap m, EpPeers peers, Ep
     }
     from = __shfl_sync(0xffffffffu, from, 0);
     if (from >= 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(peers.base[s] + lay.xperm) + static_cast<int64_t>(src_row) * nch;
+    tok = __shfl_sync(0xffffffffu, tok, 0);
+    if (tok < 0 || tok >= lay.max_rows) continue;  // never for a consistent table
+    const uint4* src = reinterpret_cast<const uint4*>(peers.base[s] + lay.xhat) + static_cast<int64_t>(tok) * nch;
     uint4* dst = reinterpret_cast<uint4*>(es.xrecv) + static_cast<int64_t>(r) * nch;
     for (int c0 = 0; c0 < nch; c0 += 32 * 8) {
       uint4 v[8];
@@ -331,8 +343,9 @@ EpLayout ep_layout(const PrefillDims& d, const EpMap& m) {
   l.flags = take(kMaxEpRanks * sizeof(unsigned));
   l.seg_count = take(E * 4);
   l.seg_start = take(E * 4);
-  l.xperm = take(T * K * H * 2);
-  l.first_p = take(T * K * 4);
+  l.max_rows = static_cast<int64_t>(T);
+  l.xhat = take(T * H * 2);
+  l.src_of = take(T * K * 8);
   l.max_recv = static_cast<int64_t>(m.world) * static_cast<int64_t>(T) *
                (K < static_cast<size_t>(m.max_local) ? static_cast<int64_t>(K) : static_cast<int64_t>(m.max_local));
   l.yback = take(T * K * H * 2);
@@ -373,7 +386,7 @@ cudaError_t ep_route(const EpCall& c, cudaStream_t stream) {
   if (st != cudaSuccess || c.pc.rows <= 0) return st;
   const int T = c.pc.rows;
   ep_first_kernel<<<(T + 255) / 256, 256, 0, stream>>>(c.map, T, c.pc.dims.top_k, c.pc.ids, c.pc.scratch.pos_of,
-                                                     reinterpret_cast<int*>(c.peers.base[c.map.rank] + c.lay.first_p));
+                                                     reinterpret_cast<int2*>(c.peers.base[c.map.rank] + c.lay.src_of));
   return cudaGetLastError();
 }
 

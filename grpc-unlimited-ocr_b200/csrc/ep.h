@@ -7,23 +7,28 @@
 // CUDA IPC) with the same layout on every rank:
 //   flags     [kMaxEpRanks] u32   barrier epochs, flags[s] written by rank s
 //   seg_count [E] i32, seg_start [E] i32   this rank's rows per global expert
-//   xperm     [max_rows*k, H] bf16        this rank's rows grouped by expert
-//   first_p   [max_rows*k] i32            per xperm position: the position of the
-//                                          same row's selection with the lowest
-//                                          expert id among those the same rank owns
-//   yback     [max_rows*k, H] bf16        their expert outputs, same positions
+//   xhat      [max_rows, H] bf16          this rank's rows, bf16-rounded
+//   src_of    [max_rows*k] {i32, i32}     per permuted position (the expert-
+//                                          grouped order of the selections):
+//                                          the position of the same row's
+//                                          selection with the lowest expert id
+//                                          among those the same rank owns, and
+//                                          the row's index in xhat
+//   yback     [max_rows*k, H] bf16        the selections' expert outputs, by
+//                                          permuted position
 // Per layer, on rank r:
-//   route    router + top-k + permutation of its own rows into xperm (the
+//   route    router + top-k + the permutation of its own rows, x^ (the
 //            single-GPU prefill stages)
 //   barrier  (arrive, wait)
-//   experts  for each of its experts, the segments of every rank's xperm are
-//            pulled over NVLink (peer loads) into xrecv, source rank order, so
-//            an expert's rows are in global row order as on one GPU — a row
-//            that several of its experts take crosses once (first_p), the
-//            other copies are made from xrecv itself; the
+//   experts  for each of its experts, the rows of every rank's segment of
+//            that expert are pulled over NVLink (peer loads of x^ rows) into
+//            xrecv, source rank order, so an expert's rows are in global row
+//            order as on one GPU — a row that several of its experts take
+//            crosses once (src_of), the other copies are made from xrecv
+//            itself; the
 //            down GEMM's epilogue stores each output row into the yback of
 //            the rank it came from (peer stores, tile by tile), at the
-//            position the row has in that rank's xperm
+//            permuted position of the selection on that rank
 //   (the shared expert on its own rows runs alongside, on a second stream)
 //   arrive, wait
 //   combine  the single-GPU combine over its own yback: every selection's
@@ -80,19 +85,20 @@ struct EpPeers {
 };
 
 struct EpLayout {
-  size_t flags, seg_count, seg_start, xperm, first_p, yback, bytes;
+  size_t flags, seg_count, seg_start, xhat, src_of, yback, bytes;
   int64_t max_recv;  // rows one rank's experts can receive: world * max_rows * min(k, local)
+  int64_t max_rows;  // rows of xhat
 };
 EpLayout ep_layout(const PrefillDims& d, const EpMap& m);
 
 // Per-rank scratch outside the exchange region.
 struct EpScratch {
   int* cnt_all;      // [world, E] every rank's rows per global expert, read after the first barrier
-  int* seg_start_all;  // [world, E] and where they start in that rank's xperm
+  int* seg_start_all;  // [world, E] and where they start in that rank's permuted order
   int* recv_count;   // [local] rows each local expert receives
   int* recv_start;   // [local] its first row in xrecv
   int* seg_dst;      // [local * world] first xrecv row of (slot i, source s)
-  int* seg_src;      // [local * world] that segment's first row in source s's xperm (and yback)
+  int* seg_src;      // [local * world] that segment's first permuted position in source s
   int* dup;          // [max_recv] receive row to copy this one from (a row pulled once), -1: pulled
   unsigned* epoch;   // barrier epoch counter
   __nv_bfloat16* xrecv;  // [max_recv, H]
@@ -103,7 +109,8 @@ size_t ep_scratch_bytes(const PrefillDims& d, const EpLayout& lay, const EpMap& 
 void carve_ep_scratch(const PrefillDims& d, const EpLayout& lay, const EpMap& m, void* base, EpScratch* s);
 
 struct EpCall {
-  PrefillCall pc;  // this rank's rows; pc.scratch's seg_count/seg_start/xperm point into its exchange region
+  PrefillCall pc;  // this rank's rows; pc.scratch's seg_count/seg_start/xhat/yperm point into its exchange
+                   // region, xperm is null (owners pull rows from x^)
   EpMap map;
   EpPeers peers;
   EpLayout lay;

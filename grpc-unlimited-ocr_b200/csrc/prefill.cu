@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(kPermBlock) positions_kernel(int T, int K, int
 }
 
 // The bf16 rows: x^ [T, H] for the shared expert and the permuted copies
-// xperm [T*K, H] for the routed experts. Grid-stride over (row, 8-column)
+// xperm [T*K, H] for the routed experts (xperm null: x^ alone — the
+// expert-parallel owners pull rows from x^). Grid-stride over (row, 8-column)
 // items, two per thread per step with both loads issued first.
 __global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restrict__ x, int T, int H, int K,
                                                            const int* __restrict__ pos_of,
@@ -164,10 +165,11 @@ __global__ void __launch_bounds__(256) permute_copy_kernel(const float* __restri
       pk.z = *reinterpret_cast<uint32_t*>(&h2);
       pk.w = *reinterpret_cast<uint32_t*>(&h3);
       *reinterpret_cast<uint4*>(xhat + t * H + c) = pk;
-      for (int j = 0; j < K; ++j) {
-        const int p = __ldg(pos_of + t * K + j);
-        if (p >= 0) *reinterpret_cast<uint4*>(xperm + static_cast<int64_t>(p) * H + c) = pk;
-      }
+      if (xperm != nullptr)
+        for (int j = 0; j < K; ++j) {
+          const int p = __ldg(pos_of + t * K + j);
+          if (p >= 0) *reinterpret_cast<uint4*>(xperm + static_cast<int64_t>(p) * H + c) = pk;
+        }
     }
   }
 }
