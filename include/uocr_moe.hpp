@@ -120,6 +120,10 @@ class MoePlan {
                std::int32_t* ids = nullptr, float* weights = nullptr) {
     check(uocr_moe_forward(plan_, layer, x, rows, y, ids, weights, stream));
   }
+  // The layer's router gate: logits [rows, E] in the CPU reference's dot order.
+  void router_logits(std::int64_t layer, const float* x, std::int64_t rows, float* logits, void* stream) {
+    check(uocr_moe_router_logits(plan_, layer, x, rows, logits, stream));
+  }
   void forward_stack(float* h, std::int64_t rows, void* stream) {
     check(uocr_moe_forward_stack(plan_, h, rows, stream));
   }
