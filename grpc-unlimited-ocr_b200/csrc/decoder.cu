@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     load_rows2(w, r0, r0 + kHalf, 0, qs, lane, u0, u1);
   }
   pdl_wait();
+  pdl_launch_dependents();  // the attention may start staging the cache's earlier rows
   const int pos = st->pos;
   if (embed != nullptr) {
     const uint2* row = reinterpret_cast<const uint2*>(embed + static_cast<int64_t>(st->token) * H);
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attn_kernel(DecShape s, cons
   __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(accs + G * kDecHeadDim);  // [cap][128] when v_smem
   __shared__ float hmax[G], hsum[G];
   pdl_wait();
+  pdl_launch_dependents();
   const int qh0 = blockIdx.x * G, split = blockIdx.y, splits = gridDim.y;
   const int g = qh0 / (s.heads / s.kv);  // the key/value head these query heads read
   const int keys = st->pos + 1;
@@ -409,6 +411,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   uint4 u0[kCpl], u1[kCpl];
   if (j < half) load_rows2(w, j, j + half, 0, qs, lane, u0, u1);
   pdl_wait();
+  pdl_launch_dependents();
   for (int e4 = threadIdx.x; e4 < K / 4; e4 += blockDim.x) {
     const float4 v = __ldcg(reinterpret_cast<const float4*>(merged) + e4);
     xs[quad_slot<Rows>(4 * e4, qs)] = v.x;
@@ -450,6 +453,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   uint4 u0[kCpl], u1[kCpl];
   if (j < half) load_rows2(w, j, j + half < s.vocab ? j + half : j, 0, qs, lane, u0, u1);
   pdl_wait();
+  pdl_launch_dependents();
   for (int e4 = threadIdx.x; e4 < H / 4; e4 += blockDim.x)
     reinterpret_cast<float4*>(xr)[e4] = __ldcg(reinterpret_cast<const float4*>(x) + e4);
   __syncthreads();
@@ -755,20 +759,32 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attn_tc_kernel(DecShape s, c
   float* accs = wo + kAttnWarps * G * kDecHeadDim;                        // [G][128]
   __shared__ float wm[kAttnWarps][G], wl[kAttnWarps][G];
   __shared__ float hmax[G], hsum[G];
-  pdl_wait();
+  // The position comes from the state the previous step's lm_head advanced
+  // (complete before this step's first kernel); the cache rows before it
+  // were written by earlier steps, so they are staged before the wait for
+  // the q/k/v grid, which writes only row pos.
   const int qh0 = blockIdx.x * G, split = blockIdx.y, splits = gridDim.y;
   const int g = qh0 / (s.heads / s.kv);
-  const int keys = st->pos + 1;
+  const int pos = st->pos;
+  const int keys = pos + 1;
   const int chunk = (keys + splits - 1) / splits;
   const int first = split * chunk;
   const int n = max(0, min(keys, first + chunk) - first);
+  const int n_old = max(0, min(n, pos - first));  // this split's rows before pos
   const __nv_bfloat16* kh = kc + (static_cast<int64_t>(g) * s.max_pos + first) * kDecHeadDim;
   const __nv_bfloat16* vh = vc + (static_cast<int64_t>(g) * s.max_pos + first) * kDecHeadDim;
-  for (int c = threadIdx.x; c < n * (kDecHeadDim / 8); c += kAttnThreads) {
-    const int key = c / (kDecHeadDim / 8), c8 = c % (kDecHeadDim / 8);
-    cp_async16(ks + key * kKvStride + c8 * 8, kh + c * 8);
-    cp_async16(vs + key * kKvStride + c8 * 8, vh + c * 8);
-  }
+  auto stage_rows = [&](int k0, int k1) {
+    for (int c = k0 * (kDecHeadDim / 8) + static_cast<int>(threadIdx.x); c < k1 * (kDecHeadDim / 8);
+         c += kAttnThreads) {
+      const int key = c / (kDecHeadDim / 8), c8 = c % (kDecHeadDim / 8);
+      cp_async16(ks + key * kKvStride + c8 * 8, kh + c * 8);
+      cp_async16(vs + key * kKvStride + c8 * 8, vh + c * 8);
+    }
+  };
+  stage_rows(0, n_old);
+  pdl_wait();
+  pdl_launch_dependents();
+  stage_rows(n_old, n);  // row pos, written by the q/k/v grid
   cp_async_commit();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gr = lane >> 2, tq = lane & 3;
