@@ -280,6 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch_s = S * Fm::kElemBytes / 16, nch_f = F * Fm::kElemBytes / 16;
   const int spr_s = S > 0 ? (nch_s + 32 * kStep - 1) / (32 * kStep) : 0;
   const int spr_f = (nch_f + 32 * kStep - 1) / (32 * kStep);
+  // int8 at one row with F = 1024: an expert's down row fills half a step,
+  // so a step carries two experts' rows (the first's chunks in w[0 .. qpr),
+  // the second's in w[qpr .. 2 qpr)): half the dependent steps, the same sums.
+  constexpr int qpr = kStep / 2;  // 16-byte chunks of one row per lane in a paired step
+  const bool pair = Fm::kElemBytes == 1 && MaxT == 1 && nch_f == 32 * qpr;
   float* sum = row_sum[warp];
   bool waited = false, have_route = false, staged = !stage_act;
   const __nv_bfloat16* acts = stage_act == 1 ? act_sm : act_s;  // [T, S]
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_ready(&route_ready, err, 24)) return false;
         have_route = true;
       }
-      nsteps = spr_s + sroute.count * spr_f;
+      nsteps = spr_s + (pair ? (sroute.count + 1) / 2 : sroute.count * spr_f);
       known = true;
       return true;
     };
@@ -336,6 +341,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         p = Fm::row(sdown, c);
         n = nch_s;
         base = st * 32 * kStep + lane;
+      } else if (pair) {
+        const int r0 = 2 * (st - spr_s);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (r0 + h >= sroute.count) break;
+          const uint4* pr = Fm::row(down, static_cast<int64_t>(sroute.expert[r0 + h]) * H + c);
+#pragma unroll
+          for (int q = 0; q < qpr; ++q) w[h * qpr + q] = ld_stream(pr + lane + 32 * q);
+        }
+        return;
       } else {
         const int r = (st - spr_s) / spr_f;
         p = Fm::row(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
@@ -372,6 +387,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) sum[t] = v;
             }
             acc[t] = 0.0f;
+          }
+        }
+        return;
+      }
+      if (pair) {
+        // (int8, one row) two experts' rows, each finished as below.
+        const int r0 = 2 * (st - spr_s);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = r0 + h;
+          if (r >= sroute.count) break;
+          const int b0 = sroute.base[r], n0 = sroute.ntok[r];
+          const float sc = Fm::scale(down, static_cast<int64_t>(sroute.expert[r]) * H + c);
+          for (int j = 0; j < n0; ++j) {
+            const __nv_bfloat16* ar = actr + static_cast<int64_t>(b0 + j) * F;
+            float a = 0.0f;
+#pragma unroll
+            for (int q = 0; q < qpr; ++q)
+              a += Fm::template dot_act<2>(w[h * qpr + q], ar + (lane + 32 * q) * Fm::kPerChunk);
+            const float v = warp_sum(a) * sc;
+            if (lane == 0) {
+              const int t = sroute.slot_tok[b0 + j];
+              sum[t] = __fadd_rn(sum[t], __fmul_rn(sroute.slot_w[b0 + j], v));
+            }
           }
         }
         return;
