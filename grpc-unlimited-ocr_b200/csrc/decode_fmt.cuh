@@ -65,6 +65,35 @@ struct Fmt<Bf16Rows> {
   }
 };
 
+// Packed fp32 pairs for the int8 gate/up dots (sm_100 f32x2): two weights
+// per instruction; each element rounds as the scalar fmaf / fsub would.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2_sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// Bytes 2p and 2p+1 of the sign-flipped word u as an fp32 pair of their int8
+// values: each byte under the bits of 2^23 + 128, minus that bias (exact).
+__device__ __forceinline__ uint64_t i8_pair(uint32_t u, int p) {
+  constexpr uint64_t kBias2 = 0x4B0000804B000080ull;  // (2^23 + 128, 2^23 + 128)
+  const uint32_t lo = __byte_perm(u, 0x4b000000u, p == 0 ? 0x7540u : 0x7542u);
+  const uint32_t hi = __byte_perm(u, 0x4b000000u, p == 0 ? 0x7541u : 0x7543u);
+  uint64_t v, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(v), "l"(kBias2));
+  return d;
+}
+
 template <>
 struct Fmt<Q8Rows> {
   static constexpr int kElemBytes = 1;
@@ -77,20 +106,18 @@ struct Fmt<Q8Rows> {
     return dot_xq(w, reinterpret_cast<const float4*>(x), 1);
   }
   static constexpr int kQuads = 4;
+  // Even and odd weights accumulate in the two halves of a packed pair.
   __device__ static float dot_xq(const uint4& w, const float4* x, int qs) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    float s = 0.0f;
+    uint64_t s = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float a, b, c, d;
-      i8x4_to_f32(words[q], a, b, c, d);
+      const uint32_t u = words[q] ^ 0x80808080u;
       const float4 xv = x[q * qs];
-      s = fmaf(a, xv.x, s);
-      s = fmaf(b, xv.y, s);
-      s = fmaf(c, xv.z, s);
-      s = fmaf(d, xv.w, s);
+      s = f2_fma(i8_pair(u, 0), f2_pack(xv.x, xv.y), s);
+      s = f2_fma(i8_pair(u, 1), f2_pack(xv.z, xv.w), s);
     }
-    return s;
+    return f2_sum(s);
   }
   template <int Cg = 0>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
