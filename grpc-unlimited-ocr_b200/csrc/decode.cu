@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const __nv_bfloat16* ar = acts + static_cast<int64_t>(t) * S;
 #pragma unroll
           for (int q = 0; q < kStep; ++q)
-            if (base + 32 * q < nch_s) acc[t] += Fm::template dot_act<2>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+            if (base + 32 * q < nch_s) acc[t] += Fm::template dot_act<2, (MaxT > 1)>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
         }
         if (st == spr_s - 1) {
           const float sc = Fm::scale(sdown, c);
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float a = 0.0f;
 #pragma unroll
             for (int q = 0; q < qpr; ++q)
-              a += Fm::template dot_act<2>(w[h * qpr + q], ar + (lane + 32 * q) * Fm::kPerChunk);
+              a += Fm::template dot_act<2, (MaxT > 1)>(w[h * qpr + q], ar + (lane + 32 * q) * Fm::kPerChunk);
             const float v = warp_sum(a) * sc;
             if (lane == 0) {
               const int t = sroute.slot_tok[b0 + j];
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float a = 0.0f;
 #pragma unroll
           for (int q = 0; q < kStep; ++q)
-            if (lane + 32 * q < nch_f) a += Fm::template dot_act<2>(w[q], ar + (lane + 32 * q) * Fm::kPerChunk);
+            if (lane + 32 * q < nch_f) a += Fm::template dot_act<2, (MaxT > 1)>(w[q], ar + (lane + 32 * q) * Fm::kPerChunk);
           const float v = warp_sum(a) * sc;
           if (lane == 0) {
             const int t = sroute.slot_tok[b0 + j];
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const __nv_bfloat16* ar = actr + static_cast<int64_t>(b0 + j) * F;
 #pragma unroll
         for (int q = 0; q < kStep; ++q)
-          if (base + 32 * q < nch_f) acc[j] += Fm::template dot_act<2>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
+          if (base + 32 * q < nch_f) acc[j] += Fm::template dot_act<2, (MaxT > 1)>(w[q], ar + (base + 32 * q) * Fm::kPerChunk);
       }
       if (sr == spr_f - 1) {
         const float sc = Fm::scale(down, static_cast<int64_t>(sroute.expert[r]) * H + c);

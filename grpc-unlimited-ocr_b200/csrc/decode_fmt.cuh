@@ -59,7 +59,7 @@ struct Fmt<Bf16Rows> {
   static constexpr int kQuads = 2;
   __device__ static float dot_xq(const uint4& w, const float4* x, int qs) { return dot8_bf16(w, x[0], x[qs]); }
   // 16 bytes of weights against bf16 activations (load mode as ld_act).
-  template <int Cg = 0>
+  template <int Cg = 0, bool Packed = false>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
     return dot8_bf16_bf16(w, ld_act<Cg>(reinterpret_cast<const uint4*>(act)));
   }
@@ -119,13 +119,29 @@ struct Fmt<Q8Rows> {
     }
     return f2_sum(s);
   }
-  template <int Cg = 0>
+  // Packed: even and odd weights in the two halves of an f32x2 accumulator
+  // (fewer instructions; the batch-1 down kernel keeps the scalar form, which
+  // needs fewer registers there).
+  template <int Cg = 0, bool Packed = false>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
     const uint4 a0 = ld_act<Cg>(reinterpret_cast<const uint4*>(act));
     const uint4 a1 = ld_act<Cg>(reinterpret_cast<const uint4*>(act) + 1);
     const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&a0);
     const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&a1);
+    if constexpr (Packed) {
+      uint64_t s2 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t u = words[q] ^ 0x80808080u;
+        const __nv_bfloat162* p = q < 2 ? p0 : p1;
+        const float2 f0 = __bfloat1622float2(p[(q & 1) * 2]);
+        const float2 f1 = __bfloat1622float2(p[(q & 1) * 2 + 1]);
+        s2 = f2_fma(i8_pair(u, 0), f2_pack(f0.x, f0.y), s2);
+        s2 = f2_fma(i8_pair(u, 1), f2_pack(f1.x, f1.y), s2);
+      }
+      return f2_sum(s2);
+    }
     float s = 0.0f;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
