@@ -40,33 +40,8 @@ __device__ __forceinline__ uint4 ld_act(const uint4* p) {
 template <typename Rows>
 struct Fmt;
 
-template <>
-struct Fmt<Bf16Rows> {
-  static constexpr int kElemBytes = 2;
-  static constexpr int kPerChunk = 8;  // weights per 16 bytes
-  __device__ static const uint4* row(const Bf16Rows& r, int64_t i) {
-    return reinterpret_cast<const uint4*>(r.w + i * r.cols);
-  }
-  __device__ static float scale(const Bf16Rows&, int64_t) { return 1.0f; }
-  // 16 bytes of weights against fp32 inputs in shared memory
-  __device__ static float dot_x(const uint4& w, const float* x) {
-    const float4 x0 = reinterpret_cast<const float4*>(x)[0];
-    const float4 x1 = reinterpret_cast<const float4*>(x)[1];
-    return dot8_bf16(w, x0, x1);
-  }
-  // The same product with the chunk's inputs stored as kQuads float4s
-  // `qs` float4s apart (the conflict-free shared layout of the gate/up kernel).
-  static constexpr int kQuads = 2;
-  __device__ static float dot_xq(const uint4& w, const float4* x, int qs) { return dot8_bf16(w, x[0], x[qs]); }
-  // 16 bytes of weights against bf16 activations (load mode as ld_act).
-  template <int Cg = 0, bool Packed = false>
-  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
-    return dot8_bf16_bf16(w, ld_act<Cg>(reinterpret_cast<const uint4*>(act)));
-  }
-};
-
-// Packed fp32 pairs for the int8 gate/up dots (sm_100 f32x2): two weights
-// per instruction; each element rounds as the scalar fmaf / fsub would.
+// Packed fp32 pairs for the decode dots (sm_100 f32x2): two weights per
+// instruction; each element rounds as the scalar fmaf / fsub would.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -93,6 +68,48 @@ __device__ __forceinline__ uint64_t i8_pair(uint32_t u, int p) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(v), "l"(kBias2));
   return d;
 }
+
+// The two bf16 weights of word v as an fp32 pair (exact: a bf16 is the top
+// half of an fp32).
+__device__ __forceinline__ uint64_t bf16_pair(uint32_t v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(v << 16), "r"(v & 0xffff0000u));
+  return r;
+}
+
+template <>
+struct Fmt<Bf16Rows> {
+  static constexpr int kElemBytes = 2;
+  static constexpr int kPerChunk = 8;  // weights per 16 bytes
+  __device__ static const uint4* row(const Bf16Rows& r, int64_t i) {
+    return reinterpret_cast<const uint4*>(r.w + i * r.cols);
+  }
+  __device__ static float scale(const Bf16Rows&, int64_t) { return 1.0f; }
+  // 16 bytes of weights against fp32 inputs in shared memory
+  __device__ static float dot_x(const uint4& w, const float* x) {
+    const float4 x0 = reinterpret_cast<const float4*>(x)[0];
+    const float4 x1 = reinterpret_cast<const float4*>(x)[1];
+    return dot8_bf16(w, x0, x1);
+  }
+  // The same product with the chunk's inputs stored as kQuads float4s
+  // `qs` float4s apart (the conflict-free shared layout of the gate/up kernel).
+  static constexpr int kQuads = 2;
+  // Even and odd weights accumulate in the two halves of a packed pair.
+  __device__ static float dot_xq(const uint4& w, const float4* x, int qs) {
+    const float4 x0 = x[0], x1 = x[qs];
+    uint64_t s = 0;
+    s = f2_fma(bf16_pair(w.x), f2_pack(x0.x, x0.y), s);
+    s = f2_fma(bf16_pair(w.y), f2_pack(x0.z, x0.w), s);
+    s = f2_fma(bf16_pair(w.z), f2_pack(x1.x, x1.y), s);
+    s = f2_fma(bf16_pair(w.w), f2_pack(x1.z, x1.w), s);
+    return f2_sum(s);
+  }
+  // 16 bytes of weights against bf16 activations (load mode as ld_act).
+  template <int Cg = 0, bool Packed = false>
+  __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
+    return dot8_bf16_bf16(w, ld_act<Cg>(reinterpret_cast<const uint4*>(act)));
+  }
+};
 
 template <>
 struct Fmt<Q8Rows> {
