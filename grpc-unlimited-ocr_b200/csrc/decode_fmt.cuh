@@ -105,19 +105,17 @@ struct Fmt<Bf16Rows> {
     return f2_sum(s);
   }
   // 16 bytes of weights against bf16 activations (load mode as ld_act).
-  // Packed: even and odd weights in the two halves of an f32x2 accumulator.
+  // Even and odd weights in the two halves of an f32x2 accumulator (Packed
+  // selects the packed form for int8 rows; bf16 rows always use it).
   template <int Cg = 0, bool Packed = false>
   __device__ static float dot_act(const uint4& w, const __nv_bfloat16* act) {
     const uint4 a = ld_act<Cg>(reinterpret_cast<const uint4*>(act));
-    if constexpr (Packed) {
-      uint64_t s = 0;
-      s = f2_fma(bf16_pair(w.x), bf16_pair(a.x), s);
-      s = f2_fma(bf16_pair(w.y), bf16_pair(a.y), s);
-      s = f2_fma(bf16_pair(w.z), bf16_pair(a.z), s);
-      s = f2_fma(bf16_pair(w.w), bf16_pair(a.w), s);
-      return f2_sum(s);
-    }
-    return dot8_bf16_bf16(w, a);
+    uint64_t s = 0;
+    s = f2_fma(bf16_pair(w.x), bf16_pair(a.x), s);
+    s = f2_fma(bf16_pair(w.y), bf16_pair(a.y), s);
+    s = f2_fma(bf16_pair(w.z), bf16_pair(a.z), s);
+    s = f2_fma(bf16_pair(w.w), bf16_pair(a.w), s);
+    return f2_sum(s);
   }
 };
 

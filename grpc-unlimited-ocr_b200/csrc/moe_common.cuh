@@ -125,20 +125,6 @@ __device__ __forceinline__ float dot8_bf16(const uint4& w, const float4& x0, con
   return s;
 }
 
-// Eight bf16 weights dotted with eight bf16 activations (one 128-bit load each).
-__device__ __forceinline__ float dot8_bf16_bf16(const uint4& w, const uint4& a) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&w);
-  const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&a);
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 wf = __bfloat1622float2(p[i]), af = __bfloat1622float2(q[i]);
-    s = fmaf(wf.x, af.x, s);
-    s = fmaf(wf.y, af.y, s);
-  }
-  return s;
-}
-
 // Four int8 weights packed in a word, as fp32, exactly. Integer-to-float
 // conversions issue at a fraction of the fp32 rate, which an int8 weight
 // stream at HBM speed would exceed; instead each byte, offset to b + 128 by
