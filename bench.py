@@ -216,7 +216,6 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
     GPU) quantises the layer per output channel; the prefill path then expands
     it to bf16 per layer before the GEMMs (the expansion is timed inside the
     router's interval of kernel_ms)."""
-    import numpy as np
     import torch
     cfg = C.CONFIGS[3]
     total = rows or cfg.rows[0]
@@ -287,9 +286,8 @@ def run_prefill(M, C, dev, stream, steps, warmup, cpu_budget, want_cpu, rows=Non
         # ranks — each source row once however many of this rank's experts
         # take it — and the expert outputs of every selection it received,
         # which its down GEMM's epilogue stores back (bf16 rows of H).
-        own = np.asarray(owner, np.int64)[ids.cpu().numpy().astype(np.int64) * world + rank]  # [rows, k]
-        sent = torch.tensor([int((own == d).any(axis=1).sum()) if d != rank else 0 for d in range(world)],
-                            dtype=torch.int64, device=dev)
+        sent = torch.tensor(ep.rows_pulled_from(ids.cpu().numpy(), owner, world, rank), dtype=torch.int64,
+                            device=dev)
         sent_all = [torch.empty_like(sent) for _ in range(world)]
         dist.all_gather(sent_all, sent)
         pulled = sum(int(v[rank]) for v in sent_all) * H * 2

@@ -56,6 +56,16 @@ def rows_received(owner: list[int], counts_by_source, experts: int, world: int) 
     return got
 
 
+def rows_pulled_from(ids, owner: list[int], world: int, rank: int) -> list[int]:
+    """How many of source `rank`'s rows each rank pulls over NVLink: a row
+    crosses once to every other rank that owns at least one of its selected
+    experts (for this source), however many of them it owns. ids [rows, k]."""
+    import numpy as np
+    ids = np.asarray(ids, np.int64).reshape(len(ids), -1) if len(ids) else np.zeros((0, 1), np.int64)
+    own = np.asarray(owner, np.int64)[ids * world + rank]
+    return [int((own == d).any(axis=1).sum()) if d != rank else 0 for d in range(world)]
+
+
 def balanced_owner_table(counts_by_source, world: int, share: float = 0.5) -> list[int]:
     """An owner table that evens out the rows the ranks' experts receive,
     from a calibration histogram counts_by_source[s][e] (rows source rank s

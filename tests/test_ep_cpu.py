@@ -183,6 +183,28 @@ def test_each_row_crosses_once_per_owner(W, strided):
     assert pulled_total < sel_total  # rows with several experts on one owner cross once
 
 
+@pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False)])
+def test_pull_byte_count_matches_the_pull_plan(W, strided):
+    """ep.rows_pulled_from (the bench's NVLink byte count) equals the rows the
+    deduplicated pull plan moves from each source to each owner."""
+    rng = np.random.default_rng(11 + W)
+    E, K = 32, 6
+    rows = rng.integers(10, 40, size=W)
+    ids_per_rank = [np.stack([rng.choice(E, K, replace=False) for _ in range(n)]).astype(np.int64) for n in rows]
+    recv, _, perms = simulate(ids_per_rank, W, E, strided)
+    cnt_all = np.stack([p[0] for p in perms])
+    seg_start_all = np.stack([p[1] for p in perms])
+    _, rstart = receive_layout(cnt_all, W, E, strided)
+    firsts = [first_positions(ids_per_rank[s], perms[s][2], s, W, E, strided) for s in range(W)]
+    owner = ep.owner_table(E, W, strided)
+    for d in range(W):
+        segs = segments(d, cnt_all, seg_start_all, rstart, W, E, strided)
+        plan = pull_plan(d, recv[d], segs, seg_start_all, firsts, W, E, strided)
+        for s in range(W):
+            moved = sum(1 for (src, _), f in zip(recv[d], plan) if src == s and f < 0) if s != d else 0
+            assert moved == ep.rows_pulled_from(ids_per_rank[s], owner, W, s)[d]
+
+
 @pytest.mark.parametrize("W,strided", [(2, False), (4, True), (8, False), (8, True)])
 def test_exchange_arithmetic_reproduces_single_gpu_order(W, strided):
     rng = np.random.default_rng(W)
